@@ -1,0 +1,435 @@
+#!/usr/bin/env python3
+"""RocketKV on B200: sparse-decode steps/s (28 layers, 8k context, budget 1024)
+plus stage-1 eviction ms/layer, each with its roofline fraction.
+
+Workload (one rank): 64 sequences x 28 layers.  Every (sequence, layer) item
+holds the cache left by stage-1 eviction of an 8192-token prompt at token
+budget 1024 -- compute_rocket_params(1024, 8192, 32, 128) gives 3685 kept
+tokens, top-k 512, page 2, r 71 -- plus a 32-token recent window, so
+len_k = 3717 bf16 rows per KV head (24 query / 8 KV heads, dim 128).  A step
+decodes one token for all 64 sequences through the 28 layers: one launch of
+the stage-2 kernel over 64 * 28 * 8 = 14336 (item, KV head) units.  Inputs:
+seeded N(0,1) bf16, 1% of K rows scaled x8; 27 GB per rank, far larger than
+L2.  With N ranks each rank decodes its own 64 sequences (weak scaling, no
+collective on the data path).
+
+Eviction: the single-layer fp32 configuration, K [8, 8192, 128], window
+queries Q [24, 32, 128], window 32, kernel 63, budget 1024; L2 is flushed
+before every timed call.
+
+`--impl reference` times the reference rocket.cpp (oracle/_ref, OpenMP build)
+on a sample of the same workload on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [os.path.join(ROOT, "rocketkv-cpp_b200"), os.path.join(ROOT, "tests"), os.path.join(ROOT, "oracle")]
+
+METRIC = "sparse-decode steps/s (28L, 8k ctx, budget 1024) + eviction ms/layer, % roofline"
+SEQS, LAYERS, H, HK, D = 64, 28, 24, 8, 128
+PROMPT, MAX_NEW, BUDGET = 8192, 32, 1024
+WINDOW = 32
+
+
+def decode_params():
+    import rocketkv_b200 as rkv
+    p = rkv.compute_rocket_params(BUDGET, PROMPT, MAX_NEW, D)  # 3685 / 512 / 2 / 71
+    cache = p.prompt_budget + WINDOW
+    cfg = rkv.RocketConfig(num_heads=H, num_heads_kv=HK, dim_head=D, topk_decode=p.k, chunk_size=p.chunk_size,
+                           r_dim=p.r, compression_ratio=p.compression_ratio, prompt_budget=p.prompt_budget)
+    return p, cache, cfg
+
+
+def unit_bytes(cache: int, k: int, w: int) -> int:
+    """Algorithmic HBM bytes of one (item, KV head) decode unit: the group's
+    query, every scored K row (the page min/max needs all of them), the
+    selected V rows, the window's K and V rows, O and the selected indices."""
+    G = H // HK
+    Lc = cache - w
+    return G * D * 2 + Lc * D * 2 + k * D * 2 + 2 * w * D * 2 + G * D * 4 + (k + w) * 4
+
+
+EVICT_BYTES = 8 * 8160 * 128 * 4 + 24 * 32 * 128 * 4 + 1024 * 4  # 33,820,672
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def traffic_per_unit(kernel: str):
+    """ncu DRAM bytes per unit from the committed profile summary, or None."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(kernel)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in self.lines:
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(n_gpus):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def allreduce_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    import torch
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# ---------------------------------------------------------------------------
+# CPU reference (oracle/_ref: the reference rocket.cpp built from its sources)
+# ---------------------------------------------------------------------------
+def ref_lib_available():
+    import oracle
+    return oracle.have_ref(omp=True)
+
+
+def cpu_decode_sample(n_items: int, seed: int = 1):
+    """Seconds per (sequence, layer) item for rocket.cpp on the host cores.
+    rocket.cpp has no recent window: it runs its selection over all len_k
+    tokens, the same amount of work."""
+    import numpy as np
+    import oracle
+    import rkvgen
+    p, cache, _ = decode_params()
+    cfg = oracle.Config(num_heads=H, num_heads_kv=HK, dim_head=D, topk_decode=p.k, chunk_size=p.chunk_size,
+                        r_dim=p.r, compression_ratio=p.compression_ratio)
+    L = oracle.ref(omp=True)
+    threads = min(os.cpu_count() or 1, 8)  # the reference parallelises over the 8 KV heads only
+    L.rkvref_set_threads(threads)
+    items = [rkvgen.stage2_inputs(seed + 3 * i, H, HK, D, cache) for i in range(min(n_items, 4))]
+    t0 = time.perf_counter()
+    for i in range(n_items):
+        q, K, V = items[i % len(items)]
+        oracle.ref_hsa_decode(q, K, V, cache, cfg, omp=True)
+    dt = (time.perf_counter() - t0) / n_items
+    return dt, threads
+
+
+def cpu_evict_sample(n_calls: int):
+    import oracle
+    import rkvgen
+    cfg = oracle.Config(num_heads=H, num_heads_kv=HK, dim_head=D, prompt_budget=BUDGET)
+    Q, K = rkvgen.stage1_inputs(11, H, HK, D, 32, PROMPT)
+    threads = min(os.cpu_count() or 1, 8)
+    oracle.ref(omp=True).rkvref_set_threads(threads)
+    t0 = time.perf_counter()
+    for _ in range(n_calls):
+        oracle.ref_prefill_eviction(Q, K, 32, PROMPT, cfg, omp=True)
+    return (time.perf_counter() - t0) / n_calls, threads
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    _, cache, _ = decode_params()
+    if not ref_lib_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/librocket_ref_omp.so was not built "
+                          "(reference sources absent when build() ran)"}))
+        return
+    items_per_step = 16
+    per_item = []
+    for i in range(args.warmup + args.steps):
+        dt, threads = cpu_decode_sample(items_per_step, seed=1000 + i)
+        if i >= args.warmup:
+            per_item.append(dt)
+    t_item = statistics.mean(per_item)
+    step_s = t_item * SEQS * LAYERS
+    value = 1.0 / step_s
+    ev_s, _ = cpu_evict_sample(2)
+    sample = (f"{items_per_step} (sequence, layer) items per step of rocket.cpp compute_hybrid_sparse_decode "
+              f"(len_k {cache}, top-k 512, page 2, r 71), extrapolated x{SEQS * LAYERS // items_per_step} "
+              f"to the 64-sequence x 28-layer step")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(cache),
+        "cpu_baseline": {"value": value, "unit": "steps/s", "cores": threads, "kind": "reference", "sample": sample},
+        "e2e": {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "eviction": {"ms_per_layer": ev_s * 1e3, "cores": threads},
+    }))
+
+
+def workload_config(cache):
+    return {"workload": "hsa_decode_28L_8k_budget1024", "seqs_per_gpu": SEQS, "layers": LAYERS,
+            "cache_tokens": cache, "recent_window": WINDOW, "topk": 512, "page": 2, "r": 71,
+            "heads_q": H, "heads_kv": HK, "dim_head": D, "kv_dtype": "bf16", "parallelism": "sequence-sharded",
+            "l2": "inputs (27 GB/rank) larger than L2; eviction flushes L2 per call",
+            "eviction_workload": "stage1 fp32 K[8,8192,128] Q[24,32,128] w32 ks63 budget1024"}
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def make_decode_inputs(device, seed, cache):
+    """Q [items, 24, 128], K/V [items, 8, cache, 128] bf16, 1% K rows x8."""
+    import torch
+    items = SEQS * LAYERS
+    g = torch.Generator(device=device).manual_seed(seed)
+    Qs = [torch.randn((items, H, D), generator=g, device=device).to(torch.bfloat16) for _ in range(4)]
+    K = torch.empty((items, HK, cache, D), dtype=torch.bfloat16, device=device)
+    V = torch.empty_like(K)
+    chunk = 64
+    for i in range(0, items, chunk):
+        j = min(items, i + chunk)
+        K[i:j] = torch.randn((j - i, HK, cache, D), generator=g, device=device)
+        V[i:j] = torch.randn((j - i, HK, cache, D), generator=g, device=device)
+        rows = torch.rand((j - i, HK, cache, 1), generator=g, device=device) < 0.01
+        K[i:j] = torch.where(rows, K[i:j] * 8, K[i:j])
+    return Qs, K, V
+
+
+def time_decode(dec, Qs, K, V, steps, warmup, world, gpu_index):
+    import torch
+    st = torch.cuda.current_stream()
+    for i in range(warmup):
+        dec(Qs[i % len(Qs)], K, V, want_sel=True)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_index) as cs:
+        e0.record(st)
+        for i in range(steps):
+            dec(Qs[i % len(Qs)], K, V, want_sel=True)
+        e1.record(st)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    barrier(world)
+    return ms, cs.summary()
+
+
+def time_evict(device, steps, warmup):
+    import torch
+    import rkvgen
+    import rocketkv_b200 as rkv
+    cfg = rkv.RocketConfig(num_heads=H, num_heads_kv=HK, dim_head=D, prompt_budget=BUDGET)
+    Q, K = rkvgen.stage1_inputs(11, H, HK, D, 32, PROMPT)
+    Qt = torch.from_numpy(Q)[None].to(device)
+    Kt = torch.from_numpy(K)[None].to(device)
+    ev = rkv.Evictor(cfg, 32, PROMPT, 1, rkv.F32, device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    st = torch.cuda.current_stream()
+    for _ in range(warmup):
+        ev(Qt, Kt)
+    times = []
+    for _ in range(steps):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        ev(Qt, Kt)
+        e1.record(st)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    # end-to-end through the rocket.h host path (pinned host buffers)
+    Qh, Kh = torch.from_numpy(Q).pin_memory().numpy(), torch.from_numpy(K).pin_memory().numpy()
+    rkv.compute_prefill_eviction(Qh, Kh, 32, PROMPT, cfg)
+    e2e = []
+    for _ in range(max(3, steps // 2)):
+        t0 = time.perf_counter()
+        rkv.compute_prefill_eviction(Qh, Kh, 32, PROMPT, cfg)
+        e2e.append(time.perf_counter() - t0)
+    return statistics.mean(times), statistics.median(e2e) * 1e3, 3  # 3 kernels per call
+
+
+def e2e_decode(cfg, cache, Qs, K, V, steps):
+    """Same step through the host-buffer C ABI: pinned host Q/K/V in, O out."""
+    import torch
+    import rocketkv_b200 as rkv
+
+    def pinned(t):
+        h = torch.empty(t.shape, dtype=torch.int16, pin_memory=True)
+        h.copy_(t.view(torch.int16))
+        return h
+
+    Qh, Kh, Vh = pinned(Qs[0]), pinned(K), pinned(V)
+    qn, kn, vn = Qh.numpy(), Kh.numpy(), Vh.numpy()
+    rkv.hsa_decode_host(qn, kn, vn, rkv.BF16, cache, cfg, recent_window=WINDOW)  # warm: device buffers
+    ts = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        rkv.hsa_decode_host(qn, kn, vn, rkv.BF16, cache, cfg, recent_window=WINDOW)
+        ts.append(time.perf_counter() - t0)
+    h2d = Qh.numel() * 2 + Kh.numel() * 2 + Vh.numel() * 2
+    d2h = K.shape[0] * H * D * 4
+    return sum(ts), len(ts), h2d, d2h
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, world, rank)
+        return
+
+    import torch
+    import rocketkv_b200 as rkv
+    world, rank, local = dist_setup(args.gpus)
+    device = torch.device("cuda", local if world > 1 else 0)
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    slot = local if world > 1 else 0
+    gpu_index = vis.split(",")[slot].strip() if vis else str(slot)
+
+    p, cache, cfg = decode_params()
+    Qs, K, V = make_decode_inputs(device, 1234 + rank, cache)
+    items = SEQS * LAYERS
+    dec = rkv.HsaDecoder(cfg, cache, items, device, recent_window=WINDOW)
+    ms, clocks = time_decode(dec, Qs, K, V, args.steps, args.warmup, world, gpu_index)
+    assert dec.status() == 0, "in-kernel wait timed out"
+    ms_max = allreduce_max(ms, world)
+    step_ms = ms_max / args.steps
+    value = world * args.steps / (ms_max / 1e3)
+
+    peak, peak_kind = peaks()
+    units = items * HK
+    ub = unit_bytes(cache, p.k, WINDOW)
+    achieved = units * ub / (ms / args.steps / 1e3) / 1e9
+    tr = traffic_per_unit("hsa_kernel")
+    roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
+            "traffic": (tr * units if tr else None), "algorithmic_bytes_per_launch": units * ub,
+            "kernel": "hsa_kernel<bf16,128,4>"}
+
+    ev_ms, ev_e2e_ms, ev_kernels = time_evict(device, max(args.steps, 5), args.warmup)
+    ev_ms = allreduce_max(ev_ms, world)
+    ev_ach = EVICT_BYTES / (ev_ms / 1e3) / 1e9
+    eviction = {"ms_per_layer": round(ev_ms, 4), "e2e_ms_per_layer": round(ev_e2e_ms, 3),
+                "roofline": {"bound": "hbm", "achieved": round(ev_ach, 1), "peak": peak, "unit": "GB/s",
+                             "frac": round(ev_ach / peak, 4), "algorithmic_bytes": EVICT_BYTES},
+                "engine": "simt-fp32", "kernels_per_call": ev_kernels}
+
+    e2e = None
+    if not args.no_e2e:
+        n_e2e = max(1, min(args.steps, 3))
+        tot, cnt, h2d, d2h = e2e_decode(cfg, cache, Qs, K, V, n_e2e)
+        tot = allreduce_max(tot, world)
+        e2e = {"value": world * cnt / tot, "unit": "steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "path": "rkv_hsa_decode_host_ex (pinned host Q/K/V -> device -> O back), steps=%d" % cnt}
+        eviction["cpu_baseline_ms"] = None
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu and ref_lib_available():
+        n_items = 24
+        t_item, threads = cpu_decode_sample(n_items)
+        cpu = {"value": 1.0 / (t_item * items), "unit": "steps/s", "cores": threads, "kind": "reference",
+               "sample": f"{n_items} (sequence, layer) items of rocket.cpp (OpenMP build) at len_k {cache}, "
+                         f"extrapolated to {items} items per step"}
+        ev_cpu, _ = cpu_evict_sample(2)
+        eviction["cpu_baseline_ms"] = round(ev_cpu * 1e3, 2)
+        eviction["cpu_cores"] = threads
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "steps/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded N(0,1) bf16 K/V/Q, 1% of K rows x8 (no public dataset on this path)",
+            "config": workload_config(cache), "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": args.steps, "clocks": clocks, "eviction": eviction,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

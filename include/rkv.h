@@ -1,0 +1,189 @@
+/*
+ * rkv.h -- C ABI of the B200 (sm_100a) implementation of RocketKV's two
+ * kernels: stage-1 prefill eviction and stage-2 hybrid sparse decode.
+ *
+ * Every entry point is extern "C", takes plain pointers and sizes, and
+ * returns an rkv_status (0 = success).  None of them aborts the process.
+ * "stream" arguments are cudaStream_t values passed as void* (NULL = the
+ * legacy default stream), so this header needs no CUDA include.
+ *
+ * Each entry point names the reference interface it replaces
+ * (Rishit2000/RocketKV-cpp, rocket.h / rocket.cpp).  The reference is a CPU
+ * C++ library with no FFI of its own; rocket.h (next to this file) keeps its
+ * C++ API unchanged and is implemented on top of this ABI.
+ *
+ * Layouts (row-major, as the reference reads them):
+ *   stage 1: Q [num_heads][len_q][dim_head], K [num_heads_kv][len_k][dim_head]
+ *   stage 2: Q [num_heads][dim_head],        K, V [num_heads_kv][len_k][dim_head]
+ * Batched device entry points take `batch` such items, `*_item_stride`
+ * bytes apart.  Element types: rkv_dtype.  q8_0 rows are dim_head/32 blocks
+ * of {fp16 scale; int8 q[32]} (34 bytes), the ggml block_q8_0 layout.
+ *
+ * Device pointers must be 16-byte aligned, and so must every item stride and
+ * (for stage 2) every K/V row.
+ */
+#ifndef RKV_H
+#define RKV_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RKV_ABI_VERSION 1
+
+typedef enum rkv_status {
+    RKV_OK = 0,
+    RKV_ERR_INVALID_ARG = 1,    /* bad size, pointer, alignment or config      */
+    RKV_ERR_UNSUPPORTED = 2,    /* valid for the reference, not built here      */
+    RKV_ERR_CUDA = 3,           /* a CUDA runtime call failed                   */
+    RKV_ERR_WORKSPACE = 4,      /* workspace missing or too small               */
+    RKV_ERR_DEVICE_TIMEOUT = 5, /* a bounded in-kernel wait ran out             */
+    RKV_ERR_NO_DEVICE = 6       /* no CUDA device / library built without one   */
+} rkv_status;
+
+typedef enum rkv_dtype {
+    RKV_F32 = 0,
+    RKV_BF16 = 1,
+    RKV_Q8_0 = 2
+} rkv_dtype;
+
+/* Stage-1 scoring engine. */
+typedef enum rkv_evict_engine {
+    RKV_EVICT_AUTO = 0,   /* the fastest engine built for the inputs          */
+    RKV_EVICT_SIMT = 1    /* fp32 CUDA-core scoring                            */
+} rkv_evict_engine;
+
+/* Field-for-field image of RocketConfig (rocket.h:18-34). */
+typedef struct rkv_config {
+    int num_heads;
+    int num_heads_kv;
+    int dim_head;
+    int window_size;        /* rocket.h:25, default 32 */
+    int kernel_size;        /* rocket.h:26, default 63 */
+    int prompt_budget;
+    int topk_decode;
+    int chunk_size;
+    int r_dim;
+    float compression_ratio;
+} rkv_config;
+
+/* Field-for-field image of RocketBudgetParams (rocket.h:5-15). */
+typedef struct rkv_budget_params {
+    int token_budget;
+    int sequence_length;
+    int max_new_tokens;
+    int capacity_budget;
+    int prompt_budget;
+    int chunk_size;
+    int r;
+    int k;
+    float compression_ratio;
+} rkv_budget_params;
+
+/* ---- library ------------------------------------------------------------ */
+int rkv_abi_version(void);
+const char* rkv_status_string(int status);
+
+/* Fills cfg with the rocket.h defaults (window_size 32, kernel_size 63) and
+ * zeros elsewhere, as `RocketConfig cfg{};` does. */
+void rkv_config_init(rkv_config* cfg);
+
+/* ---- budget derivation ----------------------------------------------------
+ * Replaces compute_rocket_params (rocket.h:36-41, rocket.cpp:14-59).
+ * Host arithmetic only; no device is touched. */
+int rkv_compute_params(int token_budget, int sequence_length, int max_new_tokens,
+                       int head_dim, int window_size, rkv_budget_params* out);
+
+/* ---- stage 1: prefill eviction -------------------------------------------
+ * Replaces compute_prefill_eviction (rocket.h:43-46, rocket.cpp:61-169).
+ * Output: ascending kept token indices, ONE set shared by all KV heads (the
+ * pooled scores are summed over KV heads, rocket.cpp:142-148).  Score ties
+ * go to the lower token index. */
+
+/* Number of ints one item's kept list can need (the kept_stride minimum). */
+int rkv_evict_max_kept(const rkv_config* cfg, int len_q, int len_k);
+
+/* Workspace bytes rkv_evict needs for `batch` items. */
+int rkv_evict_workspace_size(const rkv_config* cfg, int dtype, int len_q, int len_k,
+                             int batch, size_t* bytes);
+
+/* Device-resident, batched stage 1.  kept: [batch][kept_stride] ints,
+ * n_kept: [batch] ints, both device memory.  Asynchronous on `stream`. */
+int rkv_evict(const void* Q, const void* K, int dtype, int len_q, int len_k, int batch,
+              long long q_item_stride, long long k_item_stride, const rkv_config* cfg,
+              int* kept, int kept_stride, int* n_kept,
+              void* workspace, size_t workspace_bytes, int engine, void* stream);
+
+/* Head-sharded stage 1, part 1 (rocket.cpp:82-130 for KV heads
+ * [head_begin, head_begin+head_count)): pooled scores
+ * pooled[batch][head_count][len_k - min(window_size, len_q)] (device). */
+int rkv_evict_pool_heads(const void* Q, const void* K, int dtype, int len_q, int len_k,
+                         int batch, long long q_item_stride, long long k_item_stride,
+                         const rkv_config* cfg, int head_begin, int head_count,
+                         float* pooled, void* workspace, size_t workspace_bytes,
+                         int engine, void* stream);
+
+/* Head-sharded stage 1, part 2 (rocket.cpp:132-168): sums all num_heads_kv
+ * pooled rows in head order 0..HK-1 (pooled[batch][HK][nk], device) and
+ * selects.  Bit-identical to rkv_evict on the same pooled rows. */
+int rkv_evict_select_pooled(const float* pooled, int len_q, int len_k, int batch,
+                            const rkv_config* cfg, int* kept, int kept_stride, int* n_kept,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
+/* Host-buffer stage 1, the rocket.h drop-in path: fp32 host Q and K as
+ * compute_prefill_eviction takes them; copies in, runs on the current
+ * device, copies the kept indices back (kept_out holds kept_capacity ints).
+ * Synchronous. */
+int rkv_prefill_eviction_host(const float* Q, const float* K, int len_q, int len_k,
+                              const rkv_config* cfg, int* kept_out, int kept_capacity,
+                              int* n_kept);
+
+/* ---- stage 2: hybrid sparse decode ----------------------------------------
+ * Replaces compute_hybrid_sparse_decode (rocket.h:48-50, rocket.cpp:171-382).
+ * recent_window = 0 is the reference behaviour.  recent_window = w > 0 runs
+ * the reference selection over the first len_k - w tokens and always attends
+ * the last w tokens as well.  Selected indices (ascending) are reported per
+ * KV head; the reference computes them but does not return them. */
+
+/* Selected tokens per KV head: min(topk_decode, len_k - w) + w (w clamped). */
+int rkv_hsa_sel_capacity(const rkv_config* cfg, int len_k, int recent_window);
+
+int rkv_hsa_workspace_size(const rkv_config* cfg, int len_k, int recent_window,
+                           int batch, int head_count, size_t* bytes);
+
+/* Device-resident, batched stage 2 for KV heads [head_begin, head_begin+head_count).
+ * O: [batch][num_heads][dim_head] fp32 (only the query heads of the listed KV
+ * heads are written); sel: nullable [batch][head_count][sel_stride] ints;
+ * n_sel: nullable [batch][head_count] ints.  dtype: RKV_F32 or RKV_BF16. */
+int rkv_hsa_decode(const void* Q, const void* K, const void* V, int dtype, int len_k,
+                   int recent_window, int batch, long long q_item_stride,
+                   long long kv_item_stride, const rkv_config* cfg, int head_begin,
+                   int head_count, float* O, int* sel, int sel_stride, int* n_sel,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* Host-buffer stage 2, the rocket.h drop-in path: fp32 host Q [H][D] and
+ * K, V [HK][len_k][D]; O receives [H][D] (zeros where the reference leaves
+ * zeros).  Synchronous. */
+int rkv_hybrid_sparse_decode_host(const float* Q, const float* K, const float* V,
+                                  int len_k, const rkv_config* cfg, float* O);
+
+/* Host-buffer stage 2, general form (any dtype, batch, recent window): the
+ * inputs are host buffers laid out as for rkv_hsa_decode; copies in, runs,
+ * copies O (and sel/n_sel when non-NULL) back.  Synchronous. */
+int rkv_hsa_decode_host_ex(const void* Q, const void* K, const void* V, int dtype,
+                           int len_k, int recent_window, int batch,
+                           long long q_item_stride, long long kv_item_stride,
+                           const rkv_config* cfg, float* O, int* sel, int sel_stride,
+                           int* n_sel);
+
+/* ---- errors raised inside kernels ----------------------------------------
+ * Kernels record a failed bounded wait in the workspace.  This synchronises
+ * `stream`, returns RKV_OK or the recorded status, and clears it. */
+int rkv_workspace_status(void* workspace, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RKV_H */

@@ -1,0 +1,397 @@
+// evict.cu -- stage-1 prefill eviction on sm_100a (rocket.cpp:61-169).
+//
+// Three kernels per call, each batched over items (layers / sequences):
+//   evict_logits_kernel  grid (key tiles, KV heads, items)
+//       logits l[r][k] = (q_r . k_k) / sqrt(D) for the R = G * obs_w window
+//       rows of the KV head's query group (rocket.cpp:97-105), stored to the
+//       workspace, plus per-(row, tile) max and sum of exp(l - max).  The last
+//       CTA of a head folds the tile statistics into the row max M_r and
+//       1 / (sum_r + 1e-9) (rocket.cpp:108-113).
+//   evict_pool_kernel    grid (position tiles, items)
+//       head score hs[k] = sum_r exp(l[r][k] - M_r) * inv_r in row order
+//       (rocket.cpp:114-116), max-pool over [k - pad, k + pad] clipped to
+//       the sequence (rocket.cpp:120-129) by a doubling sparse table in
+//       shared memory, and the sum over KV heads in head order
+//       (rocket.cpp:142-148) -- or the per-head pooled rows for head sharding.
+//   evict_select_kernel  grid (items)
+//       top target_keep by (score desc, index asc) via a 4 x 8-bit radix
+//       select on order-preserving float keys, stable compaction into
+//       ascending order, then the observation window (rocket.cpp:150-166).
+#include "evict.cuh"
+
+#include <float.h>
+
+namespace rkv {
+namespace {
+
+constexpr int kNT = 256;      // threads of the scoring CTAs
+constexpr int kKT = 128;      // keys per logits tile
+constexpr int kRC = 32;       // query rows per pass (8 warps x 4 rows)
+constexpr int kPoolKT = 1024; // positions per pooling CTA
+constexpr int kSelNT = 1024;  // threads of the selection CTA
+
+__global__ void __launch_bounds__(kNT) evict_logits_kernel(EvictArgs a) {
+    extern __shared__ __align__(16) float sm[];
+    const int DP = a.D + 4;
+    float* Ks = sm;              // [kKT][DP]
+    float* Qs = sm + kKT * DP;   // [kRC][DP]
+    __shared__ int s_last;
+
+    const int tile = blockIdx.x, hc = blockIdx.y, b = blockIdx.z;
+    const int hk = a.head_begin + hc;
+    const int k0 = tile * kKT;
+    const int nkeys = min(kKT, a.nk - k0);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint8_t* Kb = a.K + (size_t)b * a.k_stride;
+    const uint8_t* Qb = a.Q + (size_t)b * a.q_stride;
+
+    // K tile -> fp32 shared memory (exact conversion for bf16 and q8_0).
+    const size_t krow0 = (size_t)hk * a.k_head_rows + k0;
+    for (int e = tid; e < kKT * a.D; e += kNT) {
+        const int kr = e / a.D, d = e - kr * a.D;
+        float v = 0.0f;
+        if (kr < nkeys) v = load_elem(Kb, a.dtype, (krow0 + kr) * a.D + d);
+        Ks[kr * DP + d] = v;
+    }
+
+    const size_t row_base = ((size_t)b * a.head_count + hc) * a.R;
+    for (int rc0 = 0; rc0 < a.R; rc0 += kRC) {
+        __syncthreads();
+        for (int e = tid; e < kRC * a.D; e += kNT) {
+            const int rr = e / a.D, d = e - rr * a.D;
+            const int r = rc0 + rr;
+            float v = 0.0f;
+            if (r < a.R) {
+                const int h = hk * a.G + r / a.obs_w;
+                const int pos = a.q_row0 + r % a.obs_w;
+                v = load_elem(Qb, a.dtype, ((size_t)h * a.q_head_rows + pos) * a.D + d);
+            }
+            Qs[rr * DP + d] = v;
+        }
+        __syncthreads();
+
+        float acc[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+        const float* qw = Qs + (warp * 4) * DP;
+#pragma unroll 2
+        for (int d = 0; d < a.D; d += 4) {
+            float4 kv[4], qv[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) kv[j] = *reinterpret_cast<const float4*>(Ks + (lane + 32 * j) * DP + d);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) qv[i] = *reinterpret_cast<const float4*>(qw + i * DP + d);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float t = acc[i][j];
+                    t = fmaf(qv[i].x, kv[j].x, t);
+                    t = fmaf(qv[i].y, kv[j].y, t);
+                    t = fmaf(qv[i].z, kv[j].z, t);
+                    t = fmaf(qv[i].w, kv[j].w, t);
+                    acc[i][j] = t;
+                }
+        }
+
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int r = rc0 + warp * 4 + i;
+            if (r >= a.R) break;  // warp-uniform
+            float l[4];
+            float m = -INFINITY;
+            float* lrow = a.logits + (row_base + r) * (size_t)a.nk + k0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int key = lane + 32 * j;
+                l[j] = acc[i][j] * a.inv_sqrt_d;
+                if (key < nkeys) {
+                    lrow[key] = l[j];
+                    m = fmaxf(m, l[j]);
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            float s = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (lane + 32 * j < nkeys) s += expf(l[j] - m);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            if (lane == 0) a.tstats[(row_base + r) * a.ntiles + tile] = make_float2(m, s);
+        }
+    }
+
+    // The last CTA of this (item, head) folds the tile statistics.
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        const unsigned prev = atomicAdd(&a.counters[(size_t)b * a.head_count + hc], 1u);
+        s_last = (prev == (unsigned)a.ntiles - 1u);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int r = tid; r < a.R; r += kNT) {
+        const float2* ts = a.tstats + (row_base + r) * a.ntiles;
+        float M = -INFINITY;
+        for (int t = 0; t < a.ntiles; ++t) M = fmaxf(M, __ldcg(&ts[t].x));
+        float S = 0.0f;
+        for (int t = 0; t < a.ntiles; ++t) {
+            const float2 v = __ldcg(ts + t);
+            S += v.y * expf(v.x - M);
+        }
+        a.rstats[row_base + r] = make_float2(M, 1.0f / (S + 1e-9f));
+    }
+    if (tid == 0) a.counters[(size_t)b * a.head_count + hc] = 0u;
+}
+
+__global__ void __launch_bounds__(kNT) evict_pool_kernel(PoolArgs a) {
+    extern __shared__ __align__(16) float sm[];
+    const int pe = a.pad_eff;
+    const int NA = kPoolKT + 2 * pe;
+    float* bufA = sm;
+    float* bufB = sm + NA;
+    float2* rs = reinterpret_cast<float2*>(sm + 2 * NA);  // [R]
+    const int tid = threadIdx.x, b = blockIdx.y;
+    const int k0 = blockIdx.x * kPoolKT;
+    const int x0 = k0 - pe;
+    constexpr int kPer = kPoolKT / kNT;
+    float tot[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) tot[i] = 0.0f;
+
+    for (int hc = 0; hc < a.head_count; ++hc) {
+        const size_t row_base = ((size_t)b * a.head_count + hc) * a.R;
+        __syncthreads();
+        for (int r = tid; r < a.R; r += kNT) rs[r] = a.rstats[row_base + r];
+        __syncthreads();
+        if (a.pad < 0) {
+            // Empty pooling window: every pooled score stays -FLT_MAX (rocket.cpp:122).
+#pragma unroll
+            for (int i = 0; i < kPer; ++i) {
+                const int k = k0 + tid + i * kNT;
+                if (k < a.nk) {
+                    if (a.pooled) a.pooled[(size_t)(b * a.head_count + hc) * a.nk + k] = -FLT_MAX;
+                    tot[i] = __fadd_rn(tot[i], -FLT_MAX);
+                }
+            }
+            continue;
+        }
+        for (int x = tid; x < NA; x += kNT) {
+            const int p = x0 + x;
+            float v = -INFINITY;
+            if (p >= 0 && p < a.nk) {
+                const float* lp = a.logits + row_base * (size_t)a.nk + p;
+                float hs = 0.0f;
+                for (int r = 0; r < a.R; ++r) {
+                    const float e = expf(lp[(size_t)r * a.nk] - rs[r].x);
+                    hs = __fadd_rn(hs, __fmul_rn(e, rs[r].y));
+                }
+                v = hs;
+            }
+            bufA[x] = v;
+        }
+        __syncthreads();
+        // Doubling: after step m, buf[x] = max(A[x .. x + 2^(m+1) - 1]).
+        float* src = bufA;
+        float* dst = bufB;
+        for (int m = 0; m < a.log2w; ++m) {
+            const int len = 1 << m;
+            const int lim = NA - 2 * len + 1;
+            for (int x = tid; x < lim; x += kNT) dst[x] = fmaxf(src[x], src[x + len]);
+            __syncthreads();
+            float* t = src; src = dst; dst = t;
+        }
+        const int off2 = 2 * pe - (1 << a.log2w) + 1;
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+            const int xi = tid + i * kNT;
+            const int k = k0 + xi;
+            if (k < a.nk) {
+                const float pooled = fmaxf(src[xi], src[xi + off2]);
+                if (a.pooled) a.pooled[(size_t)(b * a.head_count + hc) * a.nk + k] = pooled;
+                tot[i] = __fadd_rn(tot[i], pooled);
+            }
+        }
+    }
+    if (a.total) {
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+            const int k = k0 + tid + i * kNT;
+            if (k < a.nk) a.total[(size_t)b * a.nk + k] = tot[i];
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kSelNT) evict_select_kernel(SelectArgs a) {
+    __shared__ int hist[256];
+    __shared__ int scan_tmp[33];
+    __shared__ uint32_t s_prefix;
+    __shared__ int s_kk;
+    const int tid = threadIdx.x, b = blockIdx.x;
+    uint32_t* keys = a.keys + (size_t)b * a.nk;
+    int* kept = a.kept + (size_t)b * a.kept_stride;
+
+    for (int i = tid; i < a.nk; i += kSelNT) {
+        float v;
+        if (a.total) {
+            v = a.total[(size_t)b * a.nk + i];
+        } else {  // sum of the HK pooled rows in head order (rocket.cpp:143-146)
+            v = 0.0f;
+            for (int h = 0; h < a.HK; ++h) v = __fadd_rn(v, a.pooled[((size_t)b * a.HK + h) * a.nk + i]);
+        }
+        keys[i] = float_key(v);
+    }
+    if (tid == 0) { s_prefix = 0u; s_kk = a.target_keep; }
+    __syncthreads();
+
+    uint32_t mask = 0u;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int i = tid; i < 256; i += kSelNT) hist[i] = 0;
+        __syncthreads();
+        const uint32_t prefix = s_prefix;
+        for (int i = tid; i < a.nk; i += kSelNT) {
+            const uint32_t k = keys[i];
+            if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1);
+        }
+        __syncthreads();
+        if (tid == 0) {
+            int kk = s_kk, cum = 0, dg = 255;
+            for (; dg > 0; --dg) {
+                if (cum + hist[dg] >= kk) break;
+                cum += hist[dg];
+            }
+            s_kk = kk - cum;
+            s_prefix = prefix | ((uint32_t)dg << shift);
+        }
+        mask |= 255u << shift;
+        __syncthreads();
+    }
+    const uint32_t T = s_prefix;
+    const int need = s_kk;  // members of the threshold key to keep, lowest index first
+
+    int eq_base = 0, keep_base = 0;
+    for (int i0 = 0; i0 < a.nk; i0 += kSelNT) {
+        const int i = i0 + tid;
+        const uint32_t k = i < a.nk ? keys[i] : 0u;
+        const int eq = (i < a.nk && k == T) ? 1 : 0;
+        int eq_tot;
+        const int eq_rank = eq_base + block_exclusive_scan(eq, scan_tmp, &eq_tot);
+        const int keep = (i < a.nk && (k > T || (eq && eq_rank < need))) ? 1 : 0;
+        int keep_tot;
+        const int pos = keep_base + block_exclusive_scan(keep, scan_tmp, &keep_tot);
+        if (keep) kept[pos] = i;
+        eq_base += eq_tot;
+        keep_base += keep_tot;
+    }
+    for (int t = tid; t < a.obs_w; t += kSelNT) kept[a.target_keep + t] = a.nk + t;
+    if (tid == 0) a.n_kept[b] = a.target_keep + a.obs_w;
+}
+
+__global__ void evict_keep_all_kernel(int* kept, int kept_stride, int* n_kept, int len_k) {
+    const int b = blockIdx.y;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < len_k; i += gridDim.x * blockDim.x)
+        kept[(size_t)b * kept_stride + i] = i;
+    if (blockIdx.x == 0 && threadIdx.x == 0) n_kept[b] = len_k;
+}
+
+int floor_log2(int x) {
+    int j = 0;
+    while ((2 << j) <= x) ++j;
+    return j;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+EvictShape evict_shape(const rkv_config& c, int len_q, int len_k, int batch, int head_count) {
+    EvictShape s{};
+    s.G = c.num_heads / c.num_heads_kv;
+    s.obs_w = len_q < c.window_size ? len_q : c.window_size;
+    s.nk = len_k - s.obs_w;
+    s.R = s.G * s.obs_w;
+    s.ntiles = s.nk > 0 ? (s.nk + kKT - 1) / kKT : 0;
+    s.target_keep = c.prompt_budget - s.obs_w > 0 ? c.prompt_budget - s.obs_w : 0;
+    s.keep_all = (len_k <= c.prompt_budget) || (s.target_keep >= s.nk);
+    const size_t B = (size_t)batch, HC = (size_t)head_count, R = (size_t)s.R;
+    const size_t nk = s.nk > 0 ? (size_t)s.nk : 0;
+    size_t off = kWorkspaceHeader;
+    s.off_counters = off; off = align_up(off + B * HC * sizeof(unsigned), kWorkspaceAlign);
+    s.off_rstats = off;   off = align_up(off + B * HC * R * sizeof(float2), kWorkspaceAlign);
+    s.off_tstats = off;   off = align_up(off + B * HC * R * s.ntiles * sizeof(float2), kWorkspaceAlign);
+    s.off_logits = off;   off = align_up(off + B * HC * R * nk * sizeof(float), kWorkspaceAlign);
+    s.off_keys = off;     off = align_up(off + B * nk * sizeof(uint32_t), kWorkspaceAlign);
+    s.off_total = off;    off = align_up(off + B * nk * sizeof(float), kWorkspaceAlign);
+    s.ws_bytes = off;
+    return s;
+}
+
+static size_t logits_smem(int D) { return (size_t)(kKT + kRC) * (D + 4) * sizeof(float); }
+
+static int pool_smem(int pad_eff, int R, size_t* bytes) {
+    *bytes = (size_t)2 * (kPoolKT + 2 * (size_t)pad_eff) * sizeof(float) + (size_t)R * sizeof(float2);
+    return *bytes <= (size_t)200 * 1024 ? RKV_OK : RKV_ERR_UNSUPPORTED;
+}
+
+int evict_check_supported(const rkv_config& c, int dtype, const EvictShape& s) {
+    if (c.dim_head % 4 != 0 || c.dim_head > 256) return RKV_ERR_UNSUPPORTED;
+    if (dtype == RKV_Q8_0 && c.dim_head % 32 != 0) return RKV_ERR_INVALID_ARG;
+    if (!s.keep_all && c.kernel_size / 2 >= 0) {
+        const int pe = (c.kernel_size / 2 < s.nk - 1) ? c.kernel_size / 2 : s.nk - 1;
+        size_t b;
+        if (pool_smem(pe, s.R, &b) != RKV_OK) return RKV_ERR_UNSUPPORTED;
+    }
+    return RKV_OK;
+}
+
+static int set_smem_attr(const void* fn, size_t bytes) {
+    if (bytes <= 48 * 1024) return RKV_OK;
+    return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) == cudaSuccess
+               ? RKV_OK
+               : RKV_ERR_CUDA;
+}
+
+int launch_evict_scores(const EvictArgs& a, int batch, cudaStream_t st) {
+    if (a.R > 0 && a.ntiles > 0) {
+        const size_t smem = logits_smem(a.D);
+        if (set_smem_attr((const void*)evict_logits_kernel, smem) != RKV_OK) return RKV_ERR_CUDA;
+        if (cudaMemsetAsync(a.counters, 0, (size_t)batch * a.head_count * sizeof(unsigned), st) != cudaSuccess)
+            return RKV_ERR_CUDA;
+        dim3 grid(a.ntiles, a.head_count, batch);
+        evict_logits_kernel<<<grid, kNT, smem, st>>>(a);
+        if (cudaGetLastError() != cudaSuccess) return RKV_ERR_CUDA;
+    }
+    return RKV_OK;
+}
+
+int launch_evict_pool(const PoolArgs& in, int batch, cudaStream_t st) {
+    PoolArgs a = in;
+    if (a.nk <= 0) return RKV_OK;
+    a.pad_eff = a.pad < 0 ? 0 : (a.pad < a.nk - 1 ? a.pad : a.nk - 1);
+    a.log2w = floor_log2(2 * a.pad_eff + 1);
+    size_t smem;
+    if (pool_smem(a.pad_eff, a.R, &smem) != RKV_OK) return RKV_ERR_UNSUPPORTED;
+    if (set_smem_attr((const void*)evict_pool_kernel, smem) != RKV_OK) return RKV_ERR_CUDA;
+    dim3 grid((a.nk + kPoolKT - 1) / kPoolKT, batch);
+    evict_pool_kernel<<<grid, kNT, smem, st>>>(a);
+    return cudaGetLastError() == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
+}
+
+int launch_evict_select(const SelectArgs& a, int batch, cudaStream_t st) {
+    evict_select_kernel<<<batch, kSelNT, 0, st>>>(a);
+    return cudaGetLastError() == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
+}
+
+int launch_evict_keep_all(int* kept, int kept_stride, int* n_kept, int len_k, int batch, cudaStream_t st) {
+    const int blocks = len_k > 0 ? (len_k + 255) / 256 : 1;
+    dim3 grid(blocks < 1024 ? blocks : 1024, batch);
+    evict_keep_all_kernel<<<grid, 256, 0, st>>>(kept, kept_stride, n_kept, len_k);
+    return cudaGetLastError() == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
+}
+
+}  // namespace rkv

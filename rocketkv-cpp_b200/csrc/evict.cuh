@@ -1,0 +1,57 @@
+// evict.cuh -- stage-1 kernel arguments and launchers (see evict.cu).
+#pragma once
+
+#include "rkv_common.cuh"
+
+namespace rkv {
+
+struct EvictArgs {
+    const uint8_t* Q;
+    const uint8_t* K;
+    int dtype;
+    long long q_stride, k_stride;  // bytes between items
+    int len_q, len_k, H, HK, G, D, obs_w, nk, R, ntiles;
+    int q_head_rows;  // rows per query head in Q (len_q, or obs_w when compacted)
+    int q_row0;       // first window row inside a head (len_q - obs_w, or 0)
+    int k_head_rows;  // rows per KV head in K (len_k, or nk when compacted)
+    int head_begin, head_count;
+    float inv_sqrt_d;
+    float* logits;      // [batch][head_count][R][nk]
+    float2* tstats;     // [batch][head_count][R][ntiles]  (tile max, tile sum)
+    float2* rstats;     // [batch][head_count][R]          (row max, 1/(sum+1e-9))
+    unsigned* counters; // [batch][head_count]
+};
+
+struct PoolArgs {
+    const float* logits;
+    const float2* rstats;
+    int R, nk, head_count, pad;
+    int pad_eff, log2w;   // filled by the launcher
+    float* total;   // nullable: [batch][nk], sum over the head_count heads
+    float* pooled;  // nullable: [batch][head_count][nk]
+};
+
+struct SelectArgs {
+    const float* total;   // [batch][nk], or null to sum `pooled`
+    const float* pooled;  // [batch][HK][nk]
+    int HK, nk, obs_w, target_keep;
+    uint32_t* keys;       // workspace [batch][nk]
+    int* kept;
+    int kept_stride;
+    int* n_kept;
+};
+
+struct EvictShape {
+    int G, obs_w, nk, R, ntiles, target_keep;
+    bool keep_all;
+    size_t off_counters, off_rstats, off_tstats, off_logits, off_keys, off_total, ws_bytes;
+};
+
+EvictShape evict_shape(const rkv_config& c, int len_q, int len_k, int batch, int head_count);
+int evict_check_supported(const rkv_config& c, int dtype, const EvictShape& s);
+int launch_evict_scores(const EvictArgs& a, int batch, cudaStream_t st);
+int launch_evict_pool(const PoolArgs& a, int batch, cudaStream_t st);
+int launch_evict_select(const SelectArgs& a, int batch, cudaStream_t st);
+int launch_evict_keep_all(int* kept, int kept_stride, int* n_kept, int len_k, int batch, cudaStream_t st);
+
+}  // namespace rkv

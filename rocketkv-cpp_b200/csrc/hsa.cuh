@@ -1,0 +1,43 @@
+// hsa.cuh -- stage-2 hybrid sparse decode arguments and launcher (see hsa.cu).
+#pragma once
+
+#include "rkv_common.cuh"
+
+namespace rkv {
+
+struct HsaArgs {
+    const uint8_t* Q;
+    const uint8_t* K;
+    const uint8_t* V;
+    long long q_stride, kv_stride;  // bytes between items
+    int len_k, H, HK, G, D;
+    int C;          // chunk (page) size
+    int r;          // query dimensions kept
+    int w;          // recent window (tokens always attended)
+    int Lc;         // len_k - w: tokens eligible for the top-k
+    int final_k;    // min(topk, Lc)
+    int nchunks;    // ceil(Lc / C) when the chunk scoring runs, else 0
+    int head_begin, head_count;
+    int sel_stride;
+    float inv_sqrt_d;
+    float* O;        // [batch][H][D]
+    int* sel;        // [batch][head_count][sel_stride]
+    int* n_sel;      // nullable [batch][head_count]
+    float* wlogits;  // workspace [batch][head_count][G][nchunks]
+    int* err;        // workspace error word
+    // shared-memory plan (bytes), filled by the launcher
+    int stage_rows, nstages_ring, chunks_per_stage, carry_mode;
+    int off_bar, off_qf, off_sabs, off_qsum, off_qsel, off_sgn, off_R, off_flag, off_pst, off_part, off_misc;
+    int smem_bytes;
+};
+
+struct HsaShape {
+    int G, C, r, w, Lc, final_k, nchunks, sel_cap;
+    size_t off_logits, off_sel, ws_bytes;
+};
+
+HsaShape hsa_shape(const rkv_config& c, int len_k, int recent_window, int batch, int head_count);
+int hsa_check_supported(const rkv_config& c, int dtype);
+int launch_hsa(HsaArgs a, int dtype, int batch, cudaStream_t st);
+
+}  // namespace rkv

@@ -1,0 +1,176 @@
+// rkv_common.cuh -- shared device helpers for the RocketKV sm_100a kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "rkv.h"
+
+namespace rkv {
+
+constexpr int kWorkspaceAlign = 256;
+// First bytes of every workspace: the in-kernel error word.
+constexpr size_t kWorkspaceHeader = 256;
+
+// Clock-cycle budget of one bounded wait (about two seconds at 1.9 GHz).
+constexpr long long kWaitCycles = 4000000000LL;
+
+__host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// ---------------------------------------------------------------------------
+// Element loads.  bf16 -> fp32 and fp16-scaled int8 -> fp32 are exact.
+// ---------------------------------------------------------------------------
+struct Q8Block {  // ggml block_q8_0 layout: fp16 scale, 32 int8 values (34 bytes)
+    uint16_t d;
+    int8_t qs[32];
+};
+static_assert(sizeof(Q8Block) == 34, "q8_0 block must be 34 bytes");
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint32_t b) { return __uint_as_float(b << 16); }
+
+__device__ __forceinline__ float load_elem(const void* base, int dtype, size_t idx) {
+    if (dtype == RKV_F32) return static_cast<const float*>(base)[idx];
+    if (dtype == RKV_BF16) return bf16_bits_to_f32(static_cast<const uint16_t*>(base)[idx]);
+    const uint8_t* blk = static_cast<const uint8_t*>(base) + (idx / 32) * 34;
+    const uint16_t sbits = static_cast<uint16_t>(blk[0]) | (static_cast<uint16_t>(blk[1]) << 8);
+    const float s = __half2float(__ushort_as_half(sbits));
+    return s * static_cast<float>(static_cast<int8_t>(blk[2 + idx % 32]));
+}
+
+// Bytes of one row of `dim` elements.
+__host__ __device__ inline size_t row_bytes(int dtype, int dim) {
+    return dtype == RKV_F32 ? (size_t)dim * 4 : dtype == RKV_BF16 ? (size_t)dim * 2 : (size_t)dim / 32 * 34;
+}
+
+// ---------------------------------------------------------------------------
+// Deterministic exp for the stage-2 selection path (identical IEEE operation
+// sequence to the oracle's rkvo_expf): Cody & Waite reduction with ln2 split
+// into a short head and a tail, degree-7 Taylor polynomial (1/k!) by Horner
+// with fused multiply-adds, exact scaling by 2^n.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float det_expf(float x) {
+    if (x != x) return x;
+    if (x > 88.72283935546875f) return __int_as_float(0x7f800000);
+    if (x < -103.97208404541015625f) return 0.0f;
+    const float log2e = __int_as_float(0x3fb8aa3b);
+    const float ln2_hi = __int_as_float(0x3f317000);
+    const float ln2_lo = __int_as_float(0x3805fdf4);
+    const float n = rintf(__fmul_rn(x, log2e));
+    float r = __fmaf_rn(-n, ln2_hi, x);
+    r = __fmaf_rn(-n, ln2_lo, r);
+    float p = __int_as_float(0x39500d01);
+    p = __fmaf_rn(p, r, __int_as_float(0x3ab60b61));
+    p = __fmaf_rn(p, r, __int_as_float(0x3c088889));
+    p = __fmaf_rn(p, r, __int_as_float(0x3d2aaaab));
+    p = __fmaf_rn(p, r, __int_as_float(0x3e2aaaab));
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    const int ni = static_cast<int>(n);
+    if (ni > 127) return __fmul_rn(__fmul_rn(p, __int_as_float(0x7f000000)), 2.0f);
+    if (ni >= -126) return __fmul_rn(p, __int_as_float((ni + 127) << 23));
+    return __fmul_rn(__fmul_rn(p, __int_as_float((ni + 64 + 127) << 23)), __int_as_float(0x1f800000));
+}
+
+// Order-preserving map float -> uint32 (larger float, larger key).
+__device__ __forceinline__ uint32_t float_key(float f) {
+    const uint32_t b = __float_as_uint(f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier + bulk-copy (TMA, non-tensor) helpers.  No cluster multicast.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// One bulk global->shared copy; completion is signalled on `bar`.
+// dst, src 16-byte aligned; bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for phase `parity` of `bar`.  Returns false (and records
+// RKV_ERR_DEVICE_TIMEOUT in *err) if the clock budget runs out.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > kWaitCycles) {
+            atomicExch(err, (int)RKV_ERR_DEVICE_TIMEOUT);
+            return false;
+        }
+    }
+    return true;
+}
+
+// ---------------------------------------------------------------------------
+// Block-wide exclusive scan of one int per thread (blockDim.x threads,
+// blockDim.x a multiple of 32, at most 1024).  `tmp` holds 33 ints.
+// Returns the exclusive prefix; *total receives the block sum.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int block_exclusive_scan(int v, int* tmp, int* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) tmp[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < nwarps ? tmp[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += y;
+        }
+        if (lane < nwarps) tmp[lane] = w;  // inclusive warp totals
+        if (lane == nwarps - 1) tmp[32] = w;
+    }
+    __syncthreads();
+    const int before = (warp > 0 ? tmp[warp - 1] : 0) + x - v;
+    *total = tmp[32];
+    __syncthreads();  // tmp reusable after return
+    return before;
+}
+
+}  // namespace rkv

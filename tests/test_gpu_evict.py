@@ -1,0 +1,135 @@
+"""Stage-1 eviction on the GPU against the oracle (bit-exact kept indices,
+ties to the lower index) and against the reference's own outputs."""
+from concurrent.futures import ThreadPoolExecutor
+
+import numpy as np
+import pytest
+
+import cases
+import oracle as O
+import rkvgen
+import rocketkv_b200 as rkv
+from gpuutil import boundary_report, dev
+
+pytestmark = pytest.mark.gpu
+GOLD = np.load(__import__("os").path.join(__import__("os").path.dirname(__file__), "golden", "golden.npz"))
+KIND = {"f32": rkv.F32, "bf16": rkv.BF16, "q8_0": rkv.Q8_0}
+
+
+def to_rkv(cfg):
+    return rkv.RocketConfig(**{f: getattr(cfg, f) for f in cfg.__dataclass_fields__})
+
+
+def run_gpu(Qd, Kd, kind, len_q, len_k, cfg, device):
+    import torch
+    Qt = dev(Qd, kind, device).unsqueeze(0).contiguous()
+    Kt = dev(Kd, kind, device).unsqueeze(0).contiguous()
+    ev = rkv.Evictor(to_rkv(cfg), len_q, len_k, 1, KIND[kind], device)
+    kept, n = ev(Qt, Kt)
+    torch.cuda.synchronize()
+    return kept[0, : int(n[0])].cpu().numpy()
+
+
+@pytest.mark.parametrize("name", [n for n, _ in cases.STAGE1])
+def test_stage1_cases(name, cuda):
+    p = dict(cases.STAGE1)[name]
+    Q, K, (kind, Qd, Kd) = cases.stage1_build(p)
+    cfg = cases.stage1_config(p)
+    want, total = O.prefill_eviction(Q, K, p["len_q"], p["len_k"], cfg, want_total=True)
+    got = run_gpu(Qd, Kd, kind, p["len_q"], p["len_k"], cfg, cuda)
+    assert np.array_equal(got, want), boundary_report(total, got, want)
+    # and the reference's own output, up to its unspecified tie members
+    ref = GOLD[f"{name}/kept"]
+    diff = set(got.tolist()) ^ set(ref.tolist())
+    assert len(got) == len(ref) and len({float(total[i]) for i in diff}) <= 1
+
+
+def test_stage1_config0_full_size(cuda):
+    """K [8, 8192, 128] fp32, Q [24, 32, 128] window, budget 1024, ks 63."""
+    cfg = O.Config(num_heads=24, num_heads_kv=8, dim_head=128, prompt_budget=1024)
+    Q, K = rkvgen.stage1_inputs(42, 24, 8, 128, 32, 8192)
+    want, total = O.prefill_eviction(Q, K, 32, 8192, cfg, want_total=True)
+    got = run_gpu(Q, K, "f32", 32, 8192, cfg, cuda)
+    assert len(got) == 1024
+    assert np.array_equal(got, want), boundary_report(total, got, want)
+    if O.have_ref():
+        ref = O.ref_prefill_eviction(Q, K, 32, 8192, cfg)
+        diff = set(got.tolist()) ^ set(ref.tolist())
+        assert len({float(total[i]) for i in diff}) <= 1
+
+
+def test_stage1_batched_q8_layers(cuda):
+    """Several q8_0 layers in one launch (the 28-layer configuration's shape,
+    fewer layers and a shorter prefix); every layer against the oracle."""
+    import torch
+    L, S, budget = 6, 4096, 1024
+    cfg = O.Config(num_heads=24, num_heads_kv=8, dim_head=128, prompt_budget=budget)
+    items = [(rkvgen.q8_0_inputs(900 + 2 * l, (24, 32), 128), rkvgen.q8_0_inputs(901 + 2 * l, (8, S), 128))
+             for l in range(L)]
+    Qt = torch.stack([torch.from_numpy(q[0]) for q, _ in items]).to(cuda)
+    Kt = torch.stack([torch.from_numpy(k[0]) for _, k in items]).to(cuda)
+    ev = rkv.Evictor(to_rkv(cfg), 32, S, L, rkv.Q8_0, cuda)
+    kept, n = ev(Qt, Kt)
+    kept, n = kept.cpu().numpy(), n.cpu().numpy()
+    with ThreadPoolExecutor(8) as ex:
+        wants = list(ex.map(lambda it: O.prefill_eviction(it[0][1], it[1][1], 32, S, cfg, want_total=True), items))
+    for l, (want, total) in enumerate(wants):
+        got = kept[l, : n[l]]
+        assert np.array_equal(got, want), (l, boundary_report(total, got, want))
+
+
+def test_stage1_head_sharded_equals_fused(cuda):
+    import torch
+    p = dict(cases.STAGE1)["s1_basic"]
+    Q, K, _ = cases.stage1_build(p)
+    cfg = cases.stage1_config(p)
+    Qt, Kt = dev(Q, "f32", cuda)[None], dev(K, "f32", cuda)[None]
+    ev = rkv.Evictor(to_rkv(cfg), p["len_q"], p["len_k"], 1, rkv.F32, cuda)
+    nk = p["len_k"] - min(p["window"], p["len_q"])
+    pooled = torch.empty((1, p["HK"], nk), dtype=torch.float32, device=cuda)
+    for h in range(p["HK"]):  # one head at a time, as one rank each would
+        part = torch.empty((1, 1, nk), dtype=torch.float32, device=cuda)
+        ev.pool_heads(Qt, Kt, h, 1, part)
+        pooled[:, h] = part[:, 0]
+    np.testing.assert_array_equal(pooled[0].cpu().numpy(), O.evict_pool_heads(Q, K, p["len_q"], p["len_k"], cfg, 0, p["HK"]))
+    k1, n1 = ev.select_pooled(pooled)
+    a = k1[0, : int(n1[0])].cpu().numpy().copy()
+    k2, n2 = ev(Qt, Kt)
+    np.testing.assert_array_equal(a, k2[0, : int(n2[0])].cpu().numpy())
+
+
+def test_stage1_host_dropin(cuda):
+    """rocket.h path: host fp32 buffers, copies inside the call."""
+    p = dict(cases.STAGE1)["s1_needle"]
+    Q, K, _ = cases.stage1_build(p)
+    cfg = cases.stage1_config(p)
+    got = rkv.compute_prefill_eviction(Q, K, p["len_q"], p["len_k"], to_rkv(cfg))
+    np.testing.assert_array_equal(got, O.prefill_eviction(Q, K, p["len_q"], p["len_k"], cfg))
+    assert {120, 450, 980, 1420} <= set(got.tolist()) and len(got) == 512
+
+
+@pytest.mark.parametrize("len_q,len_k,budget,ks,window", [
+    (300, 300, 300, 63, 32),    # len_k <= budget: keep all
+    (300, 300, 290, 63, 32),    # target_keep >= nk: keep all
+    (300, 300, 10, 63, 32),     # budget < window: only the window
+    (16, 300, 100, 63, 32),     # len_q < window
+    (300, 300, 100, 0, 32),     # kernel 0: no pooling
+    (300, 300, 100, 2, 32),     # even kernel
+    (300, 300, 100, -3, 32),    # negative kernel: empty windows, -FLT_MAX scores
+    (300, 300, 100, 4095, 32),  # window wider than the sequence
+    (300, 300, 100, 63, 0),     # no observation window: nothing scored
+    (129, 129, 40, 63, 1),      # one window row, odd tile edge
+])
+def test_stage1_edges(len_q, len_k, budget, ks, window, cuda):
+    cfg = O.Config(num_heads=6, num_heads_kv=2, dim_head=64, window_size=window, kernel_size=ks, prompt_budget=budget)
+    Q, K = rkvgen.stage1_inputs(77, 6, 2, 64, len_q, len_k)
+    want, total = O.prefill_eviction(Q, K, len_q, len_k, cfg, want_total=True)
+    got = run_gpu(Q, K, "f32", len_q, len_k, cfg, cuda)
+    assert np.array_equal(got, want), boundary_report(total, got, want)
+
+
+def test_stage1_invalid_sizes(cuda):
+    cfg = rkv.RocketConfig(num_heads=6, num_heads_kv=2, dim_head=64, prompt_budget=5)
+    with pytest.raises(rkv.RkvError) as e:  # len_k < window rows: rocket.cpp cannot size its buffer
+        rkv.compute_prefill_eviction(np.zeros((6, 64, 64), np.float32), np.zeros((2, 10, 64), np.float32), 64, 10, cfg)
+    assert e.value.status == rkv.RKV_ERR_INVALID_ARG

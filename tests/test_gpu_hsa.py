@@ -1,0 +1,132 @@
+"""Stage-2 hybrid sparse decode on the GPU: selected indices bit-identical to
+the oracle, O within 1e-3 relative / 1e-4 absolute of it and of the
+reference's own output."""
+import numpy as np
+import pytest
+
+import cases
+import oracle as O
+import rkvgen
+import rocketkv_b200 as rkv
+from gpuutil import dev
+
+pytestmark = pytest.mark.gpu
+GOLD = np.load(__import__("os").path.join(__import__("os").path.dirname(__file__), "golden", "golden.npz"))
+RTOL, ATOL = 1e-3, 1e-4
+
+
+def to_rkv(cfg):
+    return rkv.RocketConfig(**{f: getattr(cfg, f) for f in cfg.__dataclass_fields__})
+
+
+def run_gpu(qs, Ks, Vs, L, cfg, device, bf16=True, w=0, head_begin=0, head_count=None):
+    """qs [B, H, D], Ks/Vs [B, HK, L, D] float32 (exact bf16 values when bf16)."""
+    import torch
+    kind = "bf16" if bf16 else "f32"
+    conv = (lambda a: rkvgen.bf16_bits(a)) if bf16 else (lambda a: a)
+    Q = dev(conv(qs), kind, device)
+    K = dev(conv(Ks), kind, device)
+    V = dev(conv(Vs), kind, device)
+    d = rkv.HsaDecoder(to_rkv(cfg), L, qs.shape[0], device, recent_window=w, head_begin=head_begin,
+                       head_count=head_count)
+    d(Q, K, V)
+    torch.cuda.synchronize()
+    assert d.status() == 0
+    return d.O.cpu().numpy(), d.sel.cpu().numpy(), d.n_sel.cpu().numpy()
+
+
+def check_against_oracle(q, K, V, L, cfg, Og, sel, nsel, w=0, heads=None):
+    Oo, so = O.hsa_decode(q, K, V, L, cfg, recent_window=w)
+    G = max(1, cfg.num_heads // cfg.num_heads_kv)
+    heads = range(cfg.num_heads_kv) if heads is None else heads
+    for i, h in enumerate(heads):
+        got = sel[i, : nsel[i]]
+        assert np.array_equal(got, so[h]), (h, np.setdiff1d(got, so[h])[:5], np.setdiff1d(so[h], got)[:5])
+        np.testing.assert_allclose(Og[h * G:(h + 1) * G], Oo[h * G:(h + 1) * G], rtol=RTOL, atol=ATOL)
+    return Oo
+
+
+@pytest.mark.parametrize("name", [n for n, _ in cases.STAGE2])
+def test_stage2_cases(name, cuda):
+    p = dict(cases.STAGE2)[name]
+    q, K, V = cases.stage2_build(p)
+    cfg = cases.stage2_config(p)
+    Og, sel, nsel = run_gpu(q[None], K[None], V[None], p["L"], cfg, cuda, bf16=p["bf16"])
+    check_against_oracle(q, K, V, p["L"], cfg, Og[0], sel[0], nsel[0])
+    np.testing.assert_allclose(Og[0], GOLD[f"{name}/O"], rtol=RTOL, atol=ATOL)
+
+
+@pytest.mark.parametrize("name,w", [("s2_cfg1", 32), ("s2_headline", 32), ("s2_bigchunk", 7), ("s2_keepall", 50)])
+def test_stage2_recent_window(name, w, cuda):
+    p = dict(cases.STAGE2)[name]
+    q, K, V = cases.stage2_build(p)
+    cfg = cases.stage2_config(p)
+    Og, sel, nsel = run_gpu(q[None], K[None], V[None], p["L"], cfg, cuda, bf16=p["bf16"], w=w)
+    check_against_oracle(q, K, V, p["L"], cfg, Og[0], sel[0], nsel[0], w=w)
+    for h in range(cfg.num_heads_kv):
+        assert set(range(p["L"] - w, p["L"])) <= set(sel[0, h, : nsel[0, h]].tolist())
+
+
+def test_stage2_batched_head_subset(cuda):
+    p = dict(cases.STAGE2)["s2_cfg1"]
+    cfg = cases.stage2_config(p)
+    items = [rkvgen.stage2_inputs(500 + i, 24, 8, 128, 1111) for i in range(3)]
+    qs = np.stack([it[0] for it in items])
+    Ks = np.stack([it[1] for it in items])
+    Vs = np.stack([it[2] for it in items])
+    Og, sel, nsel = run_gpu(qs, Ks, Vs, 1111, cfg, cuda, head_begin=2, head_count=5)
+    for b in range(3):
+        check_against_oracle(qs[b], Ks[b], Vs[b], 1111, cfg, Og[b], sel[b], nsel[b], heads=range(2, 7))
+
+
+def test_stage2_host_dropin_matches_reference(cuda):
+    """rocket.h compute_hybrid_sparse_decode: fp32 host buffers, reference semantics."""
+    for name in ("s2_fallback", "s2_rfull", "s2_cfg1"):
+        p = dict(cases.STAGE2)[name]
+        q, K, V = cases.stage2_build(p)
+        cfg = cases.stage2_config(p)
+        out = rkv.compute_hybrid_sparse_decode(q, K, V, p["L"], to_rkv(cfg)).reshape(p["H"], p["D"])
+        np.testing.assert_allclose(out, GOLD[f"{name}/O"], rtol=RTOL, atol=ATOL)
+
+
+def test_stage2_host_ex_bf16_with_selection(cuda):
+    p = dict(cases.STAGE2)["s2_headline"]
+    q, K, V = cases.stage2_build(p)
+    cfg = cases.stage2_config(p)
+    Og, sel, nsel = rkv.hsa_decode_host(rkvgen.bf16_bits(q)[None], rkvgen.bf16_bits(K)[None],
+                                        rkvgen.bf16_bits(V)[None], rkv.BF16, p["L"], to_rkv(cfg),
+                                        recent_window=32, with_sel=True)
+    check_against_oracle(q, K, V, p["L"], cfg, Og[0], sel[0], nsel[0], w=32)
+
+
+@pytest.mark.parametrize("L,k,C,r", [(1, 1, 1, 1), (5, 0, 2, 8), (33, 32, 2, 8), (64, 1, 64, 128), (130, 17, 65, 3)])
+def test_stage2_edges(L, k, C, r, cuda):
+    cfg = O.Config(num_heads=6, num_heads_kv=2, dim_head=128, topk_decode=k, chunk_size=C, r_dim=r)
+    q, K, V = rkvgen.stage2_inputs(31 + L, 6, 2, 128, L)
+    for w in (0, 3):
+        Og, sel, nsel = run_gpu(q[None], K[None], V[None], L, cfg, cuda, w=w)
+        check_against_oracle(q, K, V, L, cfg, Og[0], sel[0], nsel[0], w=w)
+
+
+def test_stage2_headline_batch_properties(cuda):
+    """Headline geometry (3685 + 32 tokens, k 512, page 2, r 71) on a batch of
+    items: structural properties on every unit, the oracle on a sample."""
+    import torch
+    B, L, w = 24, 3717, 32
+    cfg = O.Config(num_heads=24, num_heads_kv=8, dim_head=128, topk_decode=512, chunk_size=2, r_dim=71,
+                   compression_ratio=3.6298828125)
+    g = torch.Generator(device=cuda).manual_seed(7)
+    Q = torch.randn((B, 24, 128), generator=g, device=cuda).to(torch.bfloat16)
+    K = torch.randn((B, 8, L, 128), generator=g, device=cuda).to(torch.bfloat16)
+    V = torch.randn((B, 8, L, 128), generator=g, device=cuda).to(torch.bfloat16)
+    d = rkv.HsaDecoder(to_rkv(cfg), L, B, cuda, recent_window=w)
+    d(Q, K, V)
+    torch.cuda.synchronize()
+    sel, nsel = d.sel.cpu().numpy(), d.n_sel.cpu().numpy()
+    assert np.all(nsel == 512 + w)
+    assert np.all(np.diff(sel, axis=2) > 0)
+    assert np.all(sel[:, :, -w:] == np.arange(L - w, L))
+    for b in (0, B // 2, B - 1):
+        q = Q[b].float().cpu().numpy()
+        Kb, Vb = K[b].float().cpu().numpy(), V[b].float().cpu().numpy()
+        check_against_oracle(q, Kb, Vb, L, cfg, d.O[b].cpu().numpy(), sel[b], nsel[b], w=w)
