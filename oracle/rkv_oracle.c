@@ -218,6 +218,21 @@ static float canonical_sum256(const float* v, int n) {
     return part[0];
 }
 
+/* Approximate page logit numerator sum_i q[R[i]] * P[i] (rocket.cpp:281-286),
+ * in the fixed order the GPU uses: 8 fused multiply-add chains over the list
+ * positions i = j, j+8, j+16, ... (j = 0..7, ascending), combined as
+ * ((p0+p4)+(p2+p6)) + ((p1+p5)+(p3+p7)). */
+static float chunk_dot(const float* q, const int* R, const float* P, int nr) {
+    float p[8];
+    for (int j = 0; j < 8; ++j) {
+        float a = 0.0f;
+        for (int i = j; i < nr; i += 8) a = fmaf(q[R[i]], P[i], a);
+        p[j] = a;
+    }
+    const float t0 = p[0] + p[4], t1 = p[1] + p[5], t2 = p[2] + p[6], t3 = p[3] + p[7];
+    return (t0 + t2) + (t1 + t3);
+}
+
 int rkvo_hsa_decode(const float* Q, const float* K, const float* V, int len_k,
                     int recent_window, const rkvo_config* cfg, float* O,
                     int* sel_out, int sel_stride, int* n_sel) {
@@ -306,11 +321,8 @@ int rkvo_hsa_decode(const float* Q, const float* K, const float* V, int len_k,
                         P[i] = mv;
                     }
                 }
-                for (int h = 0; h < G; ++h) {
-                    float a = 0.0f;
-                    for (int i = 0; i < nr; ++i) a += qg[h * D + R[i]] * P[i];
-                    logit[(size_t)h * nchunks + c] = a / cscale[h];
-                }
+                for (int h = 0; h < G; ++h)
+                    logit[(size_t)h * nchunks + c] = chunk_dot(qg + (size_t)h * D, R, P, nr) / cscale[h];
             }
             /* per-head softmax over chunks (:291-309), then the group sum (:311-323) */
             for (int c = 0; c < nchunks; ++c) gp[c] = 0.0f;

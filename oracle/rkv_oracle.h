@@ -16,10 +16,12 @@
  *     uses std::nth_element with a score-only comparator, so its tie members
  *     are unspecified);
  *   - stage 2 lists the top-r query dimensions in ascending order (rocket.cpp
- *     sums over them in std::nth_element's output order), uses rkvo_expf
- *     for the approximate chunk softmax, and sums that softmax in a fixed
- *     256-way interleaved order, so the GPU selection reproduces it bit for
- *     bit;
+ *     sums over them in std::nth_element's output order), ties to the lower
+ *     dimension; it forms each approximate page logit with 8 fused
+ *     multiply-add chains combined in a fixed tree, uses rkvo_expf for the
+ *     page softmax and sums that softmax in a fixed 256-way interleaved
+ *     order -- the float operations the GPU selection performs, so its
+ *     selected indices reproduce this oracle's bit for bit;
  *   - stage 2 optionally keeps a recent window of w tokens (w = 0 is the
  *     reference behaviour) and reports the selected token indices.
  */

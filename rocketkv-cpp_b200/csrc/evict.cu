@@ -7,13 +7,13 @@
 //       workspace, plus per-(row, tile) max and sum of exp(l - max).  The last
 //       CTA of a head folds the tile statistics into the row max M_r and
 //       1 / (sum_r + 1e-9) (rocket.cpp:108-113).
-//   evict_pool_kernel    grid (position tiles, items)
+//   evict_pool_kernel    grid (position tiles, KV heads, items)
 //       head score hs[k] = sum_r exp(l[r][k] - M_r) * inv_r in row order
-//       (rocket.cpp:114-116), max-pool over [k - pad, k + pad] clipped to
-//       the sequence (rocket.cpp:120-129) by a doubling sparse table in
-//       shared memory, and the sum over KV heads in head order
-//       (rocket.cpp:142-148) -- or the per-head pooled rows for head sharding.
+//       (rocket.cpp:114-116), then max-pool over [k - pad, k + pad] clipped
+//       to the sequence (rocket.cpp:120-129) by a doubling sparse table in
+//       shared memory; one pooled row per KV head.
 //   evict_select_kernel  grid (items)
+//       sum of the pooled rows over KV heads in head order (rocket.cpp:142-148),
 //       top target_keep by (score desc, index asc) via a 4 x 8-bit radix
 //       select on order-preserving float keys, stable compaction into
 //       ascending order, then the observation window (rocket.cpp:150-166).
@@ -27,7 +27,7 @@ namespace {
 constexpr int kNT = 256;      // threads of the scoring CTAs
 constexpr int kKT = 128;      // keys per logits tile
 constexpr int kRC = 32;       // query rows per pass (8 warps x 4 rows)
-constexpr int kPoolKT = 1024; // positions per pooling CTA
+constexpr int kPoolKT = 256;  // positions per pooling CTA
 constexpr int kSelNT = 1024;  // threads of the selection CTA
 
 __global__ void __launch_bounds__(kNT) evict_logits_kernel(EvictArgs a) {
@@ -148,6 +148,9 @@ __global__ void __launch_bounds__(kNT) evict_logits_kernel(EvictArgs a) {
     if (tid == 0) a.counters[(size_t)b * a.head_count + hc] = 0u;
 }
 
+// One CTA per (position tile, KV head, item): head scores for the tile plus
+// its +-pad halo, then the clipped window max.  The cross-head sum happens in
+// the select kernel, in head order.
 __global__ void __launch_bounds__(kNT) evict_pool_kernel(PoolArgs a) {
     extern __shared__ __align__(16) float sm[];
     const int pe = a.pad_eff;
@@ -155,75 +158,51 @@ __global__ void __launch_bounds__(kNT) evict_pool_kernel(PoolArgs a) {
     float* bufA = sm;
     float* bufB = sm + NA;
     float2* rs = reinterpret_cast<float2*>(sm + 2 * NA);  // [R]
-    const int tid = threadIdx.x, b = blockIdx.y;
+    const int tid = threadIdx.x, hc = blockIdx.y, b = blockIdx.z;
     const int k0 = blockIdx.x * kPoolKT;
     const int x0 = k0 - pe;
-    constexpr int kPer = kPoolKT / kNT;
-    float tot[kPer];
-#pragma unroll
-    for (int i = 0; i < kPer; ++i) tot[i] = 0.0f;
+    const size_t row_base = ((size_t)b * a.head_count + hc) * a.R;
+    float* out = a.pooled + ((size_t)b * a.head_count + hc) * a.nk;
 
-    for (int hc = 0; hc < a.head_count; ++hc) {
-        const size_t row_base = ((size_t)b * a.head_count + hc) * a.R;
-        __syncthreads();
-        for (int r = tid; r < a.R; r += kNT) rs[r] = a.rstats[row_base + r];
-        __syncthreads();
-        if (a.pad < 0) {
-            // Empty pooling window: every pooled score stays -FLT_MAX (rocket.cpp:122).
-#pragma unroll
-            for (int i = 0; i < kPer; ++i) {
-                const int k = k0 + tid + i * kNT;
-                if (k < a.nk) {
-                    if (a.pooled) a.pooled[(size_t)(b * a.head_count + hc) * a.nk + k] = -FLT_MAX;
-                    tot[i] = __fadd_rn(tot[i], -FLT_MAX);
-                }
-            }
-            continue;
-        }
-        for (int x = tid; x < NA; x += kNT) {
-            const int p = x0 + x;
-            float v = -INFINITY;
-            if (p >= 0 && p < a.nk) {
-                const float* lp = a.logits + row_base * (size_t)a.nk + p;
-                float hs = 0.0f;
-                for (int r = 0; r < a.R; ++r) {
-                    const float e = expf(lp[(size_t)r * a.nk] - rs[r].x);
-                    hs = __fadd_rn(hs, __fmul_rn(e, rs[r].y));
-                }
-                v = hs;
-            }
-            bufA[x] = v;
-        }
-        __syncthreads();
-        // Doubling: after step m, buf[x] = max(A[x .. x + 2^(m+1) - 1]).
-        float* src = bufA;
-        float* dst = bufB;
-        for (int m = 0; m < a.log2w; ++m) {
-            const int len = 1 << m;
-            const int lim = NA - 2 * len + 1;
-            for (int x = tid; x < lim; x += kNT) dst[x] = fmaxf(src[x], src[x + len]);
-            __syncthreads();
-            float* t = src; src = dst; dst = t;
-        }
-        const int off2 = 2 * pe - (1 << a.log2w) + 1;
-#pragma unroll
-        for (int i = 0; i < kPer; ++i) {
-            const int xi = tid + i * kNT;
-            const int k = k0 + xi;
-            if (k < a.nk) {
-                const float pooled = fmaxf(src[xi], src[xi + off2]);
-                if (a.pooled) a.pooled[(size_t)(b * a.head_count + hc) * a.nk + k] = pooled;
-                tot[i] = __fadd_rn(tot[i], pooled);
-            }
-        }
+    if (a.pad < 0) {
+        // Empty pooling window: every pooled score stays -FLT_MAX (rocket.cpp:122).
+        for (int i = tid; i < kPoolKT; i += kNT)
+            if (k0 + i < a.nk) out[k0 + i] = -FLT_MAX;
+        return;
     }
-    if (a.total) {
-#pragma unroll
-        for (int i = 0; i < kPer; ++i) {
-            const int k = k0 + tid + i * kNT;
-            if (k < a.nk) a.total[(size_t)b * a.nk + k] = tot[i];
+    for (int r = tid; r < a.R; r += kNT) rs[r] = a.rstats[row_base + r];
+    __syncthreads();
+    for (int x = tid; x < NA; x += kNT) {
+        const int p = x0 + x;
+        float v = -INFINITY;
+        if (p >= 0 && p < a.nk) {
+            const float* lp = a.logits + row_base * (size_t)a.nk + p;
+            float hs = 0.0f;
+#pragma unroll 8
+            for (int r = 0; r < a.R; ++r) {
+                const float e = expf(__ldg(lp + (size_t)r * a.nk) - rs[r].x);
+                hs = __fadd_rn(hs, __fmul_rn(e, rs[r].y));
+            }
+            v = hs;
         }
+        bufA[x] = v;
     }
+    __syncthreads();
+    // Doubling: after step m, buf[x] = max(A[x .. x + 2^(m+1) - 1]).
+    float* src = bufA;
+    float* dst = bufB;
+    for (int m = 0; m < a.log2w; ++m) {
+        const int len = 1 << m;
+        const int lim = NA - 2 * len + 1;
+        for (int x = tid; x < lim; x += kNT) dst[x] = fmaxf(src[x], src[x + len]);
+        __syncthreads();
+        float* t = src;
+        src = dst;
+        dst = t;
+    }
+    const int off2 = 2 * pe - (1 << a.log2w) + 1;
+    for (int i = tid; i < kPoolKT; i += kNT)
+        if (k0 + i < a.nk) out[k0 + i] = fmaxf(src[i], src[i + off2]);
 }
 
 __global__ void __launch_bounds__(kSelNT) evict_select_kernel(SelectArgs a) {
@@ -235,46 +214,46 @@ __global__ void __launch_bounds__(kSelNT) evict_select_kernel(SelectArgs a) {
     uint32_t* keys = a.keys + (size_t)b * a.nk;
     int* kept = a.kept + (size_t)b * a.kept_stride;
 
+    // total = sum of the HK pooled rows in head order (rocket.cpp:143-146)
     for (int i = tid; i < a.nk; i += kSelNT) {
-        float v;
-        if (a.total) {
-            v = a.total[(size_t)b * a.nk + i];
-        } else {  // sum of the HK pooled rows in head order (rocket.cpp:143-146)
-            v = 0.0f;
-            for (int h = 0; h < a.HK; ++h) v = __fadd_rn(v, a.pooled[((size_t)b * a.HK + h) * a.nk + i]);
-        }
+        float v = 0.0f;
+        for (int h = 0; h < a.HK; ++h) v = __fadd_rn(v, a.pooled[((size_t)b * a.HK + h) * a.nk + i]);
         keys[i] = float_key(v);
     }
-    if (tid == 0) { s_prefix = 0u; s_kk = a.target_keep; }
+    if (tid == 0) {
+        s_prefix = 0u;
+        s_kk = a.target_keep;
+    }
     __syncthreads();
 
+    // 4 x 8-bit radix select of the target_keep-th largest key.
     uint32_t mask = 0u;
-    for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int shift = 24; shift >= 0 && a.target_keep > 0; shift -= 8) {
         for (int i = tid; i < 256; i += kSelNT) hist[i] = 0;
         __syncthreads();
         const uint32_t prefix = s_prefix;
+        const int kk = s_kk;
         for (int i = tid; i < a.nk; i += kSelNT) {
             const uint32_t k = keys[i];
             if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1);
         }
         __syncthreads();
-        if (tid == 0) {
-            int kk = s_kk, cum = 0, dg = 255;
-            for (; dg > 0; --dg) {
-                if (cum + hist[dg] >= kk) break;
-                cum += hist[dg];
-            }
-            s_kk = kk - cum;
-            s_prefix = prefix | ((uint32_t)dg << shift);
+        // counts from the top digit down; the digit where the running count reaches kk
+        const int v = tid < 256 ? hist[255 - tid] : 0;
+        int tot;
+        const int before = block_exclusive_scan(v, scan_tmp, &tot);
+        if (tid < 256 && before < kk && before + v >= kk) {
+            s_kk = kk - before;
+            s_prefix = prefix | ((uint32_t)(255 - tid) << shift);
         }
         mask |= 255u << shift;
         __syncthreads();
     }
-    const uint32_t T = s_prefix;
-    const int need = s_kk;  // members of the threshold key to keep, lowest index first
+    const uint32_t T = a.target_keep > 0 ? s_prefix : 0xffffffffu;
+    const int need = a.target_keep > 0 ? s_kk : 0;  // threshold-key members kept, lowest index first
 
     int eq_base = 0, keep_base = 0;
-    for (int i0 = 0; i0 < a.nk; i0 += kSelNT) {
+    for (int i0 = 0; i0 < a.nk && a.target_keep > 0; i0 += kSelNT) {
         const int i = i0 + tid;
         const uint32_t k = i < a.nk ? keys[i] : 0u;
         const int eq = (i < a.nk && k == T) ? 1 : 0;
@@ -326,7 +305,7 @@ EvictShape evict_shape(const rkv_config& c, int len_q, int len_k, int batch, int
     s.off_tstats = off;   off = align_up(off + B * HC * R * s.ntiles * sizeof(float2), kWorkspaceAlign);
     s.off_logits = off;   off = align_up(off + B * HC * R * nk * sizeof(float), kWorkspaceAlign);
     s.off_keys = off;     off = align_up(off + B * nk * sizeof(uint32_t), kWorkspaceAlign);
-    s.off_total = off;    off = align_up(off + B * nk * sizeof(float), kWorkspaceAlign);
+    s.off_pooled = off;   off = align_up(off + B * (size_t)c.num_heads_kv * nk * sizeof(float), kWorkspaceAlign);
     s.ws_bytes = off;
     return s;
 }
@@ -377,7 +356,7 @@ int launch_evict_pool(const PoolArgs& in, int batch, cudaStream_t st) {
     size_t smem;
     if (pool_smem(a.pad_eff, a.R, &smem) != RKV_OK) return RKV_ERR_UNSUPPORTED;
     if (set_smem_attr((const void*)evict_pool_kernel, smem) != RKV_OK) return RKV_ERR_CUDA;
-    dim3 grid((a.nk + kPoolKT - 1) / kPoolKT, batch);
+    dim3 grid((a.nk + kPoolKT - 1) / kPoolKT, a.head_count, batch);
     evict_pool_kernel<<<grid, kNT, smem, st>>>(a);
     return cudaGetLastError() == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
 }

@@ -27,13 +27,11 @@ struct PoolArgs {
     const float2* rstats;
     int R, nk, head_count, pad;
     int pad_eff, log2w;   // filled by the launcher
-    float* total;   // nullable: [batch][nk], sum over the head_count heads
-    float* pooled;  // nullable: [batch][head_count][nk]
+    float* pooled;  // [batch][head_count][nk]
 };
 
 struct SelectArgs {
-    const float* total;   // [batch][nk], or null to sum `pooled`
-    const float* pooled;  // [batch][HK][nk]
+    const float* pooled;  // [batch][HK][nk], summed over heads in head order
     int HK, nk, obs_w, target_keep;
     uint32_t* keys;       // workspace [batch][nk]
     int* kept;
@@ -44,7 +42,7 @@ struct SelectArgs {
 struct EvictShape {
     int G, obs_w, nk, R, ntiles, target_keep;
     bool keep_all;
-    size_t off_counters, off_rstats, off_tstats, off_logits, off_keys, off_total, ws_bytes;
+    size_t off_counters, off_rstats, off_tstats, off_logits, off_keys, off_pooled, ws_bytes;
 };
 
 EvictShape evict_shape(const rkv_config& c, int len_q, int len_k, int batch, int head_count);

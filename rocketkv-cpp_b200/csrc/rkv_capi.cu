@@ -136,13 +136,11 @@ int evict_run(const EvictArgs& a, const rkv_config& c, const EvictShape& s, int 
     p.nk = s.nk;
     p.head_count = a.head_count;
     p.pad = c.kernel_size / 2;
-    p.total = pooled_out ? nullptr : reinterpret_cast<float*>(ws + s.off_total);
-    p.pooled = pooled_out;
+    p.pooled = pooled_out ? pooled_out : reinterpret_cast<float*>(ws + s.off_pooled);
     rc = launch_evict_pool(p, batch, st);
     if (rc || pooled_out) return rc;
     SelectArgs sa{};
-    sa.total = p.total;
-    sa.pooled = nullptr;
+    sa.pooled = p.pooled;
     sa.HK = c.num_heads_kv;
     sa.nk = s.nk;
     sa.obs_w = s.obs_w;
@@ -297,7 +295,6 @@ int rkv_evict_select_pooled(const float* pooled, int len_q, int len_k, int batch
     if (!pooled) return RKV_ERR_INVALID_ARG;
     if (!workspace || workspace_bytes < s.ws_bytes || !aligned16(workspace)) return RKV_ERR_WORKSPACE;
     SelectArgs sa{};
-    sa.total = nullptr;
     sa.pooled = pooled;
     sa.HK = cfg->num_heads_kv;
     sa.nk = s.nk;

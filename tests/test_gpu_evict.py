@@ -91,7 +91,9 @@ def test_stage1_head_sharded_equals_fused(cuda):
         part = torch.empty((1, 1, nk), dtype=torch.float32, device=cuda)
         ev.pool_heads(Qt, Kt, h, 1, part)
         pooled[:, h] = part[:, 0]
-    np.testing.assert_array_equal(pooled[0].cpu().numpy(), O.evict_pool_heads(Q, K, p["len_q"], p["len_k"], cfg, 0, p["HK"]))
+    # pooled scores are float sums in a different order than the oracle's
+    np.testing.assert_allclose(pooled[0].cpu().numpy(), O.evict_pool_heads(Q, K, p["len_q"], p["len_k"], cfg, 0, p["HK"]),
+                               rtol=2e-6, atol=1e-9)
     k1, n1 = ev.select_pooled(pooled)
     a = k1[0, : int(n1[0])].cpu().numpy().copy()
     k2, n2 = ev(Qt, Kt)
