@@ -1,27 +1,36 @@
 // hsa.cu -- stage-2 hybrid sparse decode on sm_100a (rocket.cpp:171-382).
 //
-// One CTA per (item, KV head) unit, three phases:
-//   0. query statistics of the GQA group: sum_h |q|, sign of sum_h q, the
-//      top-r dimensions (ties to the lower dimension, listed ascending) and
-//      the per-head variance scale (rocket.cpp:197-250);
-//   1. the K rows of the scored range stream through a 3-stage ring of 16 KB
-//      bulk copies (cp.async.bulk, full/empty mbarriers, no multicast; thread
-//      0 refills a slot once every warp has released it).  Each page (chunk
-//      of C rows) gets its sign-chosen max/min on the r dimensions and the
+// Two kernels per call; a unit is one (item, KV head):
+//
+// hsa_scan_kernel   grid (splits, KV heads, items)
+//   0. query statistics of the GQA group: sum_h |q|, the sign of sum_h q, the
+//      top-r dimensions (ties to the lower dimension, listed ascending) and the
+//      per-head variance scale (rocket.cpp:197-250);
+//   1. the K rows of the CTA's page range stream through a 4-stage ring of
+//      16 KB bulk copies (cp.async.bulk, full/empty mbarriers, no multicast;
+//      thread 0 refills a slot once every warp has released it).  Each page
+//      (C rows) gets its sign-chosen max/min on the r dimensions and the
 //      approximate logit per head (rocket.cpp:252-289): eight lanes per page,
 //      lane j runs a fused multiply-add chain over the selected-dimension list
-//      entries j, j+8, ..., and a fixed butterfly adds the eight.  The logits
-//      go to the workspace;
-//   2. per-head softmax over pages with the deterministic exp and a fixed
-//      256-way summation order, the group sum, and a weighted radix select of
-//      the top final_k tokens by (score desc, index asc) with stable
-//      compaction to ascending order (rocket.cpp:291-340), then the recent
-//      window.  Phases 0-2 repeat the oracle's float operations one for one,
-//      so the selected indices match it bit for bit;
-//   3. exact attention over the selected rows: the K/V rows are gathered into
-//      the same ring by per-row bulk copies, a lane group per token reads
-//      them, online softmax per head, and a cross-group merge in shared
-//      memory (rocket.cpp:342-378).
+//      entries j, j+8, ..., a fixed butterfly adds the eight, and an IEEE
+//      division applies the scale.  Logits go to the workspace.
+//      Large batches use one CTA per unit; small ones split a unit's pages
+//      over several CTAs so the grid still covers the GPU.
+//
+// hsa_tail_kernel   grid (KV heads, items)
+//   2. the unit's page logits are staged in shared memory: per-head softmax
+//      with the deterministic exp and a fixed 256-way summation order, the group
+//      sum, a weighted radix select of the top final_k tokens by (score desc,
+//      index asc) and a stable compaction to ascending order
+//      (rocket.cpp:291-340), then the recent window;
+//   3. exact attention over the selected rows (rocket.cpp:342-378): the
+//      selected K rows, then the V rows, stream through a 3-stage ring by
+//      per-row bulk copies; scores (eight lanes per token), per-head softmax
+//      statistics, then p * v with one thread per 4-byte V word.  Selected
+//      indices and scores stay in shared memory when they fit.
+//
+// Phases 0-2 repeat the oracle's float operations one for one, so the selected
+// indices equal the oracle's bit for bit; O is tolerance-checked.
 #include "hsa.cuh"
 
 #include <float.h>
@@ -31,7 +40,10 @@ namespace {
 
 constexpr int kNT = 256;
 constexpr int kStageBytes = 16384;
-constexpr int kNStage = 3;
+constexpr int kNStageS = 4;  // scan ring stages
+constexpr int kNStageT = 3;  // tail ring stages
+constexpr int kTailRing = kNStageT * kStageBytes;
+constexpr int kTailListMax = 48 * 1024;  // selected indices + scores kept in shared memory up to this
 
 template <typename T>
 __device__ __forceinline__ float to_f(T v);
@@ -63,30 +75,271 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// q values of one selected dimension for the group's heads, then the
-// dimension index with the sign of sum_h q in bit 31 (set = negative).
+// Per selected dimension: the group's q values, then the dimension index
+// with the sign of sum_h q in bit 31 (set = negative).
 template <int MAXG>
 struct QPack {
     static constexpr int kWords = (MAXG + 1 + 3) / 4 * 4;
 };
 
+template <int QW>
+__device__ __forceinline__ void load_qpk(const float* p, float* out) {
+#pragma unroll
+    for (int v = 0; v < QW / 4; ++v) {
+        const float4 x = reinterpret_cast<const float4*>(p)[v];
+        out[4 * v] = x.x;
+        out[4 * v + 1] = x.y;
+        out[4 * v + 2] = x.z;
+        out[4 * v + 3] = x.w;
+    }
+}
+
+// ===========================================================================
+// Scan kernel: phases 0 and 1
+// ===========================================================================
 template <typename T, int D, int MAXG>
-__global__ void __launch_bounds__(kNT, (MAXG <= 3 ? 3 : 2)) hsa_kernel(const HsaArgs a) {
+__global__ void __launch_bounds__(kNT, 3) hsa_scan_kernel(const HsaArgs a) {
     extern __shared__ __align__(128) uint8_t sm[];
     uint8_t* ring = sm;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sm + a.off_bar);
-    uint64_t* empty = full + kNStage;
-    float* pst = reinterpret_cast<float*>(sm + a.off_pst);  // carry mode only: [2][D + 1]
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + kNStageS * kStageBytes);
+    uint64_t* empty = full + kNStageS;
+    float* pst = reinterpret_cast<float*>(sm + kNStageS * kStageBytes + 128);  // carry mode: [2][D + 1]
 
     constexpr int QW = QPack<MAXG>::kWords;
-    __shared__ float qf[MAXG * D];
+    __shared__ __align__(16) float qf[MAXG * D];
     __shared__ __align__(16) float qpk[D * QW];
     __shared__ float sabs[D], qsum[D];
-    __shared__ int Rl[D], flag[D];
+    __shared__ int Rl[D];
+    __shared__ float sumall[MAXG], cscale[MAXG];
+    __shared__ int scan_tmp[33];
+
+    constexpr size_t RB = (size_t)D * sizeof(T);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int split = blockIdx.x, hc = blockIdx.y, b = blockIdx.z, hk = a.head_begin + hc;
+    const int G = a.G;
+    const int nch = a.nchunks;
+    const int p_beg = split * a.pages_per_split;
+    const int p_end = min(nch, p_beg + a.pages_per_split);
+    if (p_beg >= p_end) return;  // uniform
+    const uint8_t* Qg = a.Q + (size_t)b * a.q_stride + (size_t)hk * G * D * sizeof(T);
+    const uint8_t* Ku = a.K + (size_t)b * a.kv_stride + (size_t)hk * a.len_k * RB;
+    float* wl = a.wlogits + ((size_t)b * a.head_count + hc) * (size_t)G * nch;
+
+    if (tid == 0) {
+        for (int s = 0; s < kNStageS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kNT / 32);
+        }
+        fence_mbar_init();
+    }
+    for (int e = tid; e < G * D; e += kNT) qf[e] = to_f<T>(reinterpret_cast<const T*>(Qg)[e]);
+    __syncthreads();
+
+    // ---- phase 0: group query statistics (rocket.cpp:197-250) --------------
+    if (tid < D) {
+        float sa = 0.0f, sv = 0.0f;
+        for (int h = 0; h < G; ++h) {
+            const float qv = qf[h * D + tid];
+            sa = __fadd_rn(sa, fabsf(qv));
+            sv = __fadd_rn(sv, qv);
+        }
+        sabs[tid] = sa;
+        qsum[tid] = sv;
+    }
+    if (lane == 0 && warp < G) {  // sequential over d, as rocket.cpp:210 accumulates
+        const float4* q4 = reinterpret_cast<const float4*>(qf + warp * D);
+        float s = 0.0f;
+#pragma unroll 8
+        for (int v = 0; v < D / 4; ++v) {
+            const float4 x = q4[v];
+            s = __fadd_rn(s, fabsf(x.x));
+            s = __fadd_rn(s, fabsf(x.y));
+            s = __fadd_rn(s, fabsf(x.z));
+            s = __fadd_rn(s, fabsf(x.w));
+        }
+        sumall[warp] = s;
+    }
+    __syncthreads();
+    int flag = 0;
+    if (tid < D) {
+        int rank = 0;
+        const float me = sabs[tid];
+#pragma unroll 8
+        for (int e = 0; e < D; ++e) {
+            const float o = sabs[e];
+            rank += (o > me || (o == me && e < tid)) ? 1 : 0;
+        }
+        flag = (a.r >= D || rank < a.r) ? 1 : 0;
+    }
+    int nr;
+    const int pos = block_exclusive_scan(flag, scan_tmp, &nr);
+    if (flag) Rl[pos] = tid;
+    __syncthreads();
+    if (tid < G) {
+        float sk;
+        if (a.r >= D) {
+            sk = sumall[tid];
+        } else {
+            sk = 0.0f;
+            for (int i = 0; i < nr; ++i) sk = __fadd_rn(sk, fabsf(qf[tid * D + Rl[i]]));
+        }
+        cscale[tid] = __fsqrt_rn(__fmul_rn((float)D, __fdiv_rn(sk, __fadd_rn(sumall[tid], 1e-9f))));
+    }
+    for (int i = tid; i < nr; i += kNT) {
+        const int d = Rl[i];
+#pragma unroll
+        for (int h = 0; h < MAXG; ++h) qpk[i * QW + h] = h < G ? qf[h * D + d] : 0.0f;
+        qpk[i * QW + QW - 1] = __int_as_float(d | (qsum[d] >= 0.0f ? 0 : (int)0x80000000));
+    }
+    __syncthreads();
+
+    // ---- phase 1: stream K, page representatives, approximate logits ------
+    const int SR = a.stage_rows;
+    const int row_beg = p_beg * a.C, row_end = min(p_end * a.C, a.Lc);
+    const int nst = (row_end - row_beg + SR - 1) / SR;
+    if (tid == 0) {
+        for (int s = 0; s < kNStageS && s < nst; ++s) {
+            const int t0 = row_beg + s * SR;
+            const uint32_t bytes = (uint32_t)(min(SR, row_end - t0) * RB);
+            mbar_arrive_expect_tx(&full[s], bytes);
+            bulk_load(ring + (size_t)s * kStageBytes, Ku + (size_t)t0 * RB, bytes, &full[s]);
+        }
+    }
+    // lane h of each eight divides head h's sum (one division per lane)
+    const int s8 = lane & 7;
+    const float my_scale = s8 < G ? cscale[s8] : 1.0f;
+    float carry_mx = -INFINITY, carry_mn = INFINITY;  // carry mode: running extrema of list entry `tid`
+    for (int s = 0; s < nst; ++s) {
+        const int slot = s % kNStageS;
+        const bool ok = mbar_wait_bounded(&full[slot], (uint32_t)((s / kNStageS) & 1), a.err);
+        // A failed wait is uniform across the block (nobody passes an incomplete
+        // phase); carry mode also decides it with a block vote, as its loop syncs.
+        if (a.carry_mode ? __syncthreads_or(!ok) : !ok) break;
+        const int t0 = row_beg + s * SR, nrows = min(SR, row_end - t0);
+        const T* st = reinterpret_cast<const T*>(ring + (size_t)slot * kStageBytes);
+        const int c_lo = t0 / a.C;
+        const int c_hi = (t0 + nrows == row_end) ? p_end : (t0 + nrows) / a.C;
+        const int ntask = (c_hi - c_lo) * 8;
+        if (a.carry_mode) {
+            if (tid < nr) {
+                const int w = __float_as_int(qpk[tid * QW + QW - 1]);
+                const int d = w & 0x7fffffff;
+                for (int rr = 0; rr < nrows; ++rr) {
+                    const int t = t0 + rr;
+                    const float x = to_f<T>(st[rr * D + d]);
+                    carry_mx = fmaxf(carry_mx, x);
+                    carry_mn = fminf(carry_mn, x);
+                    if ((t + 1) % a.C == 0 || t == row_end - 1) {
+                        pst[(t / a.C - c_lo) * (D + 1) + tid] = w < 0 ? carry_mn : carry_mx;
+                        carry_mx = -INFINITY;
+                        carry_mn = INFINITY;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+        // tasks (page, slice): slice s8 sums list entries i = s8, s8+8, ...
+        for (int base = warp * 32; base < ntask; base += kNT) {
+            const int task = base + lane;
+            const int cl = task >> 3;
+            float acc[MAXG];
+#pragma unroll
+            for (int h = 0; h < MAXG; ++h) acc[h] = 0.0f;
+            if (task < ntask) {
+                if (a.carry_mode) {
+                    for (int i = s8; i < nr; i += 8) {
+                        const float P = pst[cl * (D + 1) + i];
+                        const float* qp = qpk + i * QW;
+#pragma unroll
+                        for (int h = 0; h < MAXG; ++h) acc[h] = __fmaf_rn(qp[h], P, acc[h]);
+                    }
+                } else {
+                    // stages start on page boundaries here
+                    const int r0 = cl * a.C, r1 = min(r0 + a.C, nrows);
+                    const T* row0 = st + r0 * D;
+                    if (r1 - r0 == 2) {
+                        // two-row page (the common page size): P = max or min of the pair
+#pragma unroll 4
+                        for (int i = s8; i < nr; i += 8) {
+                            float qv[QW];
+                            load_qpk<QW>(qpk + i * QW, qv);
+                            const int w = __float_as_int(qv[QW - 1]);
+                            const int d = w & 0x7fffffff;
+                            const float x0 = to_f<T>(row0[d]), x1 = to_f<T>(row0[D + d]);
+                            const float P = w < 0 ? fminf(x0, x1) : fmaxf(x0, x1);
+#pragma unroll
+                            for (int h = 0; h < MAXG; ++h) acc[h] = __fmaf_rn(qv[h], P, acc[h]);
+                        }
+                    } else {
+                        for (int i = s8; i < nr; i += 8) {
+                            float qv[QW];
+                            load_qpk<QW>(qpk + i * QW, qv);
+                            const int w = __float_as_int(qv[QW - 1]);
+                            const int d = w & 0x7fffffff;
+                            float mx = -INFINITY, mn = INFINITY;
+                            for (int rr = 0; rr < r1 - r0; ++rr) {
+                                const float x = to_f<T>(row0[rr * D + d]);
+                                mx = fmaxf(mx, x);
+                                mn = fminf(mn, x);
+                            }
+                            const float P = w < 0 ? mn : mx;
+#pragma unroll
+                            for (int h = 0; h < MAXG; ++h) acc[h] = __fmaf_rn(qv[h], P, acc[h]);
+                        }
+                    }
+                }
+            }
+            float mine = acc[0];
+#pragma unroll
+            for (int h = 0; h < MAXG; ++h) {
+                acc[h] = __fadd_rn(acc[h], __shfl_xor_sync(0xffffffffu, acc[h], 4));
+                acc[h] = __fadd_rn(acc[h], __shfl_xor_sync(0xffffffffu, acc[h], 2));
+                acc[h] = __fadd_rn(acc[h], __shfl_xor_sync(0xffffffffu, acc[h], 1));
+                if (h == s8) mine = acc[h];
+            }
+            // every lane of the eight holds the sums; lane h divides head h
+            if (task < ntask && s8 < G) wl[(size_t)s8 * nch + c_lo + cl] = __fdiv_rn(mine, my_scale);
+        }
+        if (a.carry_mode) __syncthreads();  // pst reuse
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        // producer: refill the slot of the previous stage once every warp released it
+        if (tid == 0 && s >= 1 && s - 1 + kNStageS < nst) {
+            const int sp = s - 1, ps = sp % kNStageS;
+            // On a failed wait there is no refill; the consumers' wait on that
+            // slot then runs out as well, and the error word is already set.
+            if (mbar_wait_bounded(&empty[ps], (uint32_t)((sp / kNStageS) & 1), a.err)) {
+                fence_proxy_async();
+                const int t2 = row_beg + (sp + kNStageS) * SR;
+                const uint32_t bytes = (uint32_t)(min(SR, row_end - t2) * RB);
+                mbar_arrive_expect_tx(&full[ps], bytes);
+                bulk_load(ring + (size_t)ps * kStageBytes, Ku + (size_t)t2 * RB, bytes, &full[ps]);
+            }
+        }
+    }
+}
+
+// ===========================================================================
+// Tail kernel: phases 2 and 3
+// ===========================================================================
+template <typename T, int D, int MAXG>
+__global__ void __launch_bounds__(kNT, 3) hsa_tail_kernel(const HsaArgs a) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    uint8_t* ring = sm;
+    uint64_t* full3 = reinterpret_cast<uint64_t*>(sm + kTailRing);
+    uint64_t* empty3 = full3 + kNStageT;
+    // selected indices and per-head scores live in shared memory when they fit
+    // (a.tail_smem_lists), else in the workspace
+    int* sel_s = a.tail_smem_lists ? reinterpret_cast<int*>(sm + kTailRing + 128) : nullptr;
+    float* sc_s = a.tail_smem_lists ? reinterpret_cast<float*>(sm + kTailRing + 128 + (size_t)a.score_stride * 4)
+                                    : nullptr;
+
+    __shared__ float qf[MAXG * D];
     __shared__ float part[MAXG][kNT];
-    __shared__ float sumall[MAXG], cscale[MAXG], hmax[MAXG], hinv[MAXG];
+    __shared__ float part_[MAXG][kNT / 32];
+    __shared__ float hmax[MAXG], hinv[MAXG];
     __shared__ int hist[256], scan_tmp[33];
-    __shared__ int s_nr, s_abort, s_kk;
+    __shared__ int s_abort, s_kk;
     __shared__ uint32_t s_prefix;
 
     constexpr size_t RB = (size_t)D * sizeof(T);
@@ -96,188 +349,30 @@ __global__ void __launch_bounds__(kNT, (MAXG <= 3 ? 3 : 2)) hsa_kernel(const Hsa
     const uint8_t* Qg = a.Q + (size_t)b * a.q_stride + (size_t)hk * G * D * sizeof(T);
     const uint8_t* Ku = a.K + (size_t)b * a.kv_stride + (size_t)hk * a.len_k * RB;
     const uint8_t* Vu = a.V + (size_t)b * a.kv_stride + (size_t)hk * a.len_k * RB;
-    int* sel = a.sel + ((size_t)b * a.head_count + hc) * a.sel_stride;
+    int* sel_g = a.sel + ((size_t)b * a.head_count + hc) * a.sel_stride;
+    int* sel = sel_s ? sel_s : sel_g;
     const int nch = a.nchunks;
-    float* wl = a.wlogits + ((size_t)b * a.head_count + hc) * (size_t)G * nch;
 
-    uint64_t* full3 = empty + kNStage;   // phase-3 ring barriers
-    uint64_t* empty3 = full3 + kNStage;
     if (tid == 0) {
         s_abort = 0;
-        for (int s = 0; s < kNStage; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kNT / 32);
+        for (int s = 0; s < kNStageT; ++s) {
             mbar_init(&full3[s], 1);
             mbar_init(&empty3[s], kNT / 32);
         }
         fence_mbar_init();
     }
     for (int e = tid; e < G * D; e += kNT) qf[e] = to_f<T>(reinterpret_cast<const T*>(Qg)[e]);
-    __syncthreads();
 
     int nfirst;  // selected tokens from the scored range
     if (nch > 0) {
-        // ---- phase 0: group query statistics (rocket.cpp:197-250) ----------
-        if (tid < D) {
-            float sa = 0.0f, sv = 0.0f;
-            for (int h = 0; h < G; ++h) {
-                const float qv = qf[h * D + tid];
-                sa = __fadd_rn(sa, fabsf(qv));
-                sv = __fadd_rn(sv, qv);
-            }
-            sabs[tid] = sa;
-            qsum[tid] = sv;
-        }
-        if (tid < G) {
-            float s = 0.0f;
-            for (int d = 0; d < D; ++d) s = __fadd_rn(s, fabsf(qf[tid * D + d]));
-            sumall[tid] = s;
-        }
-        __syncthreads();
-        if (tid < D) {
-            int rank = 0;
-            const float me = sabs[tid];
-            for (int e = 0; e < D; ++e) {
-                const float o = sabs[e];
-                rank += (o > me || (o == me && e < tid)) ? 1 : 0;
-            }
-            flag[tid] = (a.r >= D || rank < a.r) ? 1 : 0;
-        }
-        __syncthreads();
-        if (tid == 0) {
-            int nr = 0;
-            for (int d = 0; d < D; ++d)
-                if (flag[d]) Rl[nr++] = d;
-            s_nr = nr;
-        }
-        __syncthreads();
-        const int nr = s_nr;
-        if (tid < G) {
-            float sk;
-            if (a.r >= D) {
-                sk = sumall[tid];
-            } else {
-                sk = 0.0f;
-                for (int i = 0; i < nr; ++i) sk = __fadd_rn(sk, fabsf(qf[tid * D + Rl[i]]));
-            }
-            cscale[tid] = __fsqrt_rn(__fmul_rn((float)D, __fdiv_rn(sk, __fadd_rn(sumall[tid], 1e-9f))));
-        }
-        for (int i = tid; i < nr; i += kNT) {
-            const int d = Rl[i];
-#pragma unroll
-            for (int h = 0; h < MAXG; ++h) qpk[i * QW + h] = h < G ? qf[h * D + d] : 0.0f;
-            qpk[i * QW + QW - 1] = __int_as_float(d | (qsum[d] >= 0.0f ? 0 : (int)0x80000000));
-        }
-
-        // ---- phase 1: stream K, page representatives, approximate logits --
-        const int SR = a.stage_rows;
-        const int nst = (a.Lc + SR - 1) / SR;
-        __syncthreads();  // qpk, cscale ready
-        if (tid == 0) {
-            for (int s = 0; s < kNStage && s < nst; ++s) {
-                const int t0 = s * SR;
-                const uint32_t bytes = (uint32_t)(min(SR, a.Lc - t0) * RB);
-                mbar_arrive_expect_tx(&full[s], bytes);
-                bulk_load(ring + (size_t)s * kStageBytes, Ku + (size_t)t0 * RB, bytes, &full[s]);
-            }
-        }
-        float carry = -INFINITY;  // carry mode: running signed max of dimension list entry `tid`
-        bool timed_out = false;
-        for (int s = 0; s < nst; ++s) {
-            const int slot = s % kNStage;
-            const bool ok = mbar_wait_bounded(&full[slot], (uint32_t)((s / kNStage) & 1), a.err);
-            // A failed wait is uniform across the block (nobody passes an incomplete
-            // phase); carry mode also decides it with a block vote, as its loop syncs.
-            if (a.carry_mode ? __syncthreads_or(!ok) : !ok) {
-                timed_out = true;
-                break;
-            }
-            const int t0 = s * SR, nrows = min(SR, a.Lc - t0);
-            const T* st = reinterpret_cast<const T*>(ring + (size_t)slot * kStageBytes);
-            const int c_lo = t0 / a.C;
-            const int c_hi = (t0 + nrows == a.Lc) ? nch : (t0 + nrows) / a.C;
-            const int ntask = (c_hi - c_lo) * 8;
-            if (a.carry_mode) {
-                if (tid < nr) {
-                    const int w = __float_as_int(qpk[tid * QW + QW - 1]);
-                    const int d = w & 0x7fffffff;
-                    const bool neg = w < 0;
-                    for (int rr = 0; rr < nrows; ++rr) {
-                        const int t = t0 + rr;
-                        const float x = to_f<T>(st[rr * D + d]);
-                        carry = fmaxf(carry, neg ? -x : x);
-                        if ((t + 1) % a.C == 0 || t == a.Lc - 1) {
-                            pst[(t / a.C - c_lo) * (D + 1) + tid] = neg ? -carry : carry;
-                            carry = -INFINITY;
-                        }
-                    }
-                }
-                __syncthreads();
-            }
-            // tasks (page, slice): slice s8 sums list entries i = s8, s8+8, ...
-            for (int base = warp * 32; base < ntask; base += kNT) {
-                const int task = base + lane;
-                const int cl = task >> 3, s8 = task & 7;
-                float acc[MAXG];
-#pragma unroll
-                for (int h = 0; h < MAXG; ++h) acc[h] = 0.0f;
-                if (task < ntask) {
-                    const int r0 = cl * a.C, r1 = min(r0 + a.C, nrows);
-                    for (int i = s8; i < nr; i += 8) {
-                        const float* qp = qpk + i * QW;
-                        float P;
-                        if (!a.carry_mode) {
-                            const int w = __float_as_int(qp[QW - 1]);
-                            const int d = w & 0x7fffffff;
-                            const bool neg = w < 0;
-                            float m = -INFINITY;
-                            for (int rr = r0; rr < r1; ++rr) {
-                                const float x = to_f<T>(st[rr * D + d]);
-                                m = fmaxf(m, neg ? -x : x);
-                            }
-                            P = neg ? -m : m;
-                        } else {
-                            P = pst[cl * (D + 1) + i];
-                        }
-#pragma unroll
-                        for (int h = 0; h < MAXG; ++h) acc[h] = __fmaf_rn(qp[h], P, acc[h]);
-                    }
-                }
-#pragma unroll
-                for (int h = 0; h < MAXG; ++h) {
-                    acc[h] = __fadd_rn(acc[h], __shfl_xor_sync(0xffffffffu, acc[h], 4));
-                    acc[h] = __fadd_rn(acc[h], __shfl_xor_sync(0xffffffffu, acc[h], 2));
-                    acc[h] = __fadd_rn(acc[h], __shfl_xor_sync(0xffffffffu, acc[h], 1));
-                }
-                if (task < ntask && s8 == 0) {
-#pragma unroll
-                    for (int h = 0; h < MAXG; ++h)
-                        if (h < G) wl[(size_t)h * nch + c_lo + cl] = __fdiv_rn(acc[h], cscale[h]);
-                }
-            }
-            if (a.carry_mode) __syncthreads();  // pst reuse
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
-            // producer: refill the slot of the previous stage once every warp released it
-            if (tid == 0 && s >= 1 && s - 1 + kNStage < nst) {
-                const int sp = s - 1, ps = sp % kNStage;
-                if (mbar_wait_bounded(&empty[ps], (uint32_t)((sp / kNStage) & 1), a.err)) {
-                    fence_proxy_async();
-                    const int s2 = sp + kNStage, t2 = s2 * SR;
-                    const uint32_t bytes = (uint32_t)(min(SR, a.Lc - t2) * RB);
-                    mbar_arrive_expect_tx(&full[ps], bytes);
-                    bulk_load(ring + (size_t)ps * kStageBytes, Ku + (size_t)t2 * RB, bytes, &full[ps]);
-                } else {
-                    // no refill: the consumers' wait on this slot then runs out as well
-                    timed_out = true;
-                }
-            }
-        }
-        if (timed_out) s_abort = 1;
-        __syncthreads();
-        if (s_abort) return;
-
         // ---- phase 2: page softmax per head, group sum, weighted top-k ----
+        // The page logits are staged in the (still idle) ring when they fit.
+        float* wg = a.wlogits + ((size_t)b * a.head_count + hc) * (size_t)G * nch;
+        const bool staged = (size_t)G * nch * sizeof(float) <= (size_t)kTailRing;
+        float* wl = staged ? reinterpret_cast<float*>(ring) : wg;
+        if (staged)
+            for (int e = tid; e < G * nch; e += kNT) wl[e] = __ldcg(wg + e);
+        __syncthreads();
         float m[MAXG];
 #pragma unroll
         for (int h = 0; h < MAXG; ++h) m[h] = -INFINITY;
@@ -290,12 +385,12 @@ __global__ void __launch_bounds__(kNT, (MAXG <= 3 ? 3 : 2)) hsa_kernel(const Hsa
             float v = m[h];
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-            if (lane == 0) part[h][warp] = v;
+            if (lane == 0) part_[h][warp] = v;
         }
         __syncthreads();
         if (tid < G) {
             float v = -INFINITY;
-            for (int wi = 0; wi < kNT / 32; ++wi) v = fmaxf(v, part[tid][wi]);
+            for (int wi = 0; wi < kNT / 32; ++wi) v = fmaxf(v, part_[tid][wi]);
             hmax[tid] = v;
         }
         __syncthreads();
@@ -331,7 +426,7 @@ __global__ void __launch_bounds__(kNT, (MAXG <= 3 ? 3 : 2)) hsa_kernel(const Hsa
             }
         }
         __syncthreads();
-        uint32_t* keys = reinterpret_cast<uint32_t*>(wl);
+        uint32_t* keys = reinterpret_cast<uint32_t*>(wl);  // head-0 row, overwritten page by page
         for (int c = tid; c < nch; c += kNT) {
             float g = 0.0f;
             for (int h = 0; h < G; ++h) g = __fadd_rn(g, __fmul_rn(wl[(size_t)h * nch + c], hinv[h]));
@@ -403,122 +498,185 @@ __global__ void __launch_bounds__(kNT, (MAXG <= 3 ? 3 : 2)) hsa_kernel(const Hsa
     const int n = nfirst + a.w;
     if (tid == 0 && a.n_sel) a.n_sel[(size_t)b * a.head_count + hc] = n;
     __syncthreads();
+    if (sel_s)
+        for (int i = tid; i < n; i += kNT) sel_g[i] = sel_s[i];
 
     // ---- phase 3: exact attention over the selected rows -------------------
-    // The selected K and V rows are gathered into the ring by bulk copies
-    // (one per row, issued by the lanes of warp 0), TS tokens per 16 KB stage:
-    // K rows first, then V rows.  A lane group of LPT lanes handles a token:
-    // 16-byte shared-memory reads, the q.k dot per head reduced across the
-    // group, and an online softmax per head.
-    constexpr int TS = kStageBytes / (2 * (int)RB);
-    constexpr int EPV = 16 / (int)sizeof(T);
-    constexpr int NV = D / EPV;
-    constexpr int LPT = NV < 32 ? NV : 32;
-    constexpr int VPL = NV / LPT;
-    constexpr int EPL = VPL * EPV;
-    constexpr int TPW = 32 / LPT;
-    constexpr int NGROUPS = (kNT / 32) * TPW;
-    const int gl = lane % LPT;
-    const int grp = warp * TPW + lane / LPT;
-    const int nst3 = (n + TS - 1) / TS;
+    // One stream of 16 KB stages through the ring: first the selected K rows,
+    // then the selected V rows, one bulk copy per row issued by the lanes of
+    // warp 0.  Pass A: eight lanes per token form q.k for every head;
+    // pass B: per-head max, p = exp(s - max) and sum(p); pass C: each thread
+    // owns one 4-byte word of the V row and accumulates p * v per head.
+    constexpr int TS = kStageBytes / (int)RB;   // rows per stage
+    constexpr int EPV = 16 / (int)sizeof(T);    // elements per 16-byte chunk
+    constexpr int CPR = (int)RB / 16;           // 16-byte chunks per row
+    constexpr int NPART = 8;                    // pass-A lanes per token
+    constexpr int CPP = CPR / NPART;            // chunks per lane
+    constexpr int TPS = kNT / NPART;            // tokens per pass-A step
+    constexpr bool QREG = MAXG * CPP * EPV <= 48;
+    constexpr int NDP = (int)RB / 4;            // 4-byte words per row
+    constexpr int NGC = kNT / NDP;              // pass-C token groups
+    constexpr int EW = 4 / (int)sizeof(T);      // elements per word
+    static_assert(CPP >= 1 && NGC >= 1, "row layout");
+    const int nA = (n + TS - 1) / TS;
+    const int nS = 2 * nA;
+    float* sc = sc_s ? sc_s : a.wscore + ((size_t)b * a.head_count + hc) * (size_t)G * a.score_stride;  // [G][n]
 
-    auto issue3 = [&](int s) {  // called by all lanes of warp 0
-        const int slot = s % kNStage;
-        const int j0 = s * TS, nt = min(TS, n - j0);
-        if (lane == 0) mbar_arrive_expect_tx(&full3[slot], (uint32_t)(2 * nt * RB));
+    auto issue3 = [&](int s) {  // all lanes of warp 0
+        const int slot = s % kNStageT;
+        const bool is_v = s >= nA;
+        const int j0 = (is_v ? s - nA : s) * TS, nt = min(TS, n - j0);
+        if (lane == 0) mbar_arrive_expect_tx(&full3[slot], (uint32_t)(nt * RB));
         __syncwarp();
         uint8_t* dst = ring + (size_t)slot * kStageBytes;
-        for (int j = lane; j < nt; j += 32) {
-            const int t = sel[j0 + j];
-            bulk_load(dst + (size_t)j * RB, Ku + (size_t)t * RB, (uint32_t)RB, &full3[slot]);
-            bulk_load(dst + (size_t)(TS + j) * RB, Vu + (size_t)t * RB, (uint32_t)RB, &full3[slot]);
-        }
+        const uint8_t* src = is_v ? Vu : Ku;
+        for (int j = lane; j < nt; j += 32)
+            bulk_load(dst + (size_t)j * RB, src + (size_t)sel[j0 + j] * RB, (uint32_t)RB, &full3[slot]);
     };
     if (warp == 0) {
         fence_proxy_async();
-        for (int s = 0; s < kNStage && s < nst3; ++s) issue3(s);
+        for (int s = 0; s < kNStageT && s < nS; ++s) issue3(s);
     }
 
-    float qr[MAXG][EPL];
+    const int lp = tid % NPART, tok = tid / NPART;
+    float qreg[QREG ? MAXG : 1][QREG ? CPP * EPV : 1];
+    if constexpr (QREG) {
+#pragma unroll
+        for (int h = 0; h < MAXG; ++h)
+#pragma unroll
+            for (int c = 0; c < CPP; ++c)
+#pragma unroll
+                for (int e = 0; e < EPV; ++e)
+                    qreg[h][c * EPV + e] = h < G ? qf[h * D + (lp + c * NPART) * EPV + e] : 0.0f;
+    }
+    const int dw = tid % NDP, cg = tid / NDP;
+    float accv[MAXG][EW];
 #pragma unroll
     for (int h = 0; h < MAXG; ++h)
 #pragma unroll
-        for (int v = 0; v < VPL; ++v)
-#pragma unroll
-            for (int e = 0; e < EPV; ++e)
-                qr[h][v * EPV + e] = (h < G) ? qf[h * D + (gl + v * LPT) * EPV + e] : 0.0f;
-    float mrun[MAXG], lrun[MAXG], acc[MAXG][EPL];
-#pragma unroll
-    for (int h = 0; h < MAXG; ++h) {
-        mrun[h] = -INFINITY;
-        lrun[h] = 0.0f;
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) acc[h][e] = 0.0f;
-    }
+        for (int e = 0; e < EW; ++e) accv[h][e] = 0.0f;
+
     bool ok3 = true;
-    for (int s = 0; s < nst3; ++s) {
-        const int slot = s % kNStage;
-        if (!mbar_wait_bounded(&full3[slot], (uint32_t)((s / kNStage) & 1), a.err)) {
+    for (int s = 0; s < nS; ++s) {
+        if (s == nA) {
+            // ---- pass B: softmax statistics over the n scores per head ----
+            __syncthreads();
+            float m[MAXG];
+#pragma unroll
+            for (int h = 0; h < MAXG; ++h) m[h] = -INFINITY;
+            for (int i = tid; i < n; i += kNT)
+#pragma unroll
+                for (int h = 0; h < MAXG; ++h)
+                    if (h < G) m[h] = fmaxf(m[h], sc[(size_t)h * a.score_stride + i]);
+#pragma unroll
+            for (int h = 0; h < MAXG; ++h) {
+                float v = m[h];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+                if (lane == 0) part_[h][warp] = v;
+            }
+            __syncthreads();
+            if (tid < G) {
+                float v = -INFINITY;
+                for (int wi = 0; wi < kNT / 32; ++wi) v = fmaxf(v, part_[tid][wi]);
+                hmax[tid] = v;
+            }
+            __syncthreads();
+            float ssum[MAXG];
+#pragma unroll
+            for (int h = 0; h < MAXG; ++h) ssum[h] = 0.0f;
+            for (int i = tid; i < n; i += kNT)
+#pragma unroll
+                for (int h = 0; h < MAXG; ++h)
+                    if (h < G) {
+                        const float p = __expf(sc[(size_t)h * a.score_stride + i] - hmax[h]);
+                        sc[(size_t)h * a.score_stride + i] = p;
+                        ssum[h] += p;
+                    }
+#pragma unroll
+            for (int h = 0; h < MAXG; ++h) {
+                float v = ssum[h];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if (lane == 0) part_[h][warp] = v;
+            }
+            __syncthreads();
+            if (tid < G) {
+                float v = 0.0f;
+                for (int wi = 0; wi < kNT / 32; ++wi) v += part_[tid][wi];
+                hinv[tid] = 1.0f / v;
+            }
+            __syncthreads();
+        }
+        const int slot = s % kNStageT;
+        if (!mbar_wait_bounded(&full3[slot], (uint32_t)((s / kNStageT) & 1), a.err)) {
             ok3 = false;
             break;
         }
-        const int nt = min(TS, n - s * TS);
-        const uint8_t* kst = ring + (size_t)slot * kStageBytes;
-        const uint8_t* vst = kst + (size_t)TS * RB;
-        for (int jb = warp * TPW; jb < nt; jb += NGROUPS) {
-            const int j = jb + lane / LPT;
-            const bool okj = j < nt;
-            float kf[EPL], vf[EPL];
+        const uint8_t* st3 = ring + (size_t)slot * kStageBytes;
+        if (s < nA) {
+            // ---- pass A: scores of the tokens in this K stage ----
+            const int j0 = s * TS, nt = min(TS, n - j0);
+            for (int jb = 0; jb < nt; jb += TPS) {  // uniform trip count
+                const int j = jb + tok;
+                float dot[MAXG];
 #pragma unroll
-            for (int v = 0; v < VPL; ++v) {
-                if (okj) {
-                    const uint4 kw = *reinterpret_cast<const uint4*>(kst + (size_t)j * RB + (size_t)(gl + v * LPT) * 16);
-                    const uint4 vw = *reinterpret_cast<const uint4*>(vst + (size_t)j * RB + (size_t)(gl + v * LPT) * 16);
-                    vec_to_f<T>(kw, kf + v * EPV);
-                    vec_to_f<T>(vw, vf + v * EPV);
-                } else {
+                for (int h = 0; h < MAXG; ++h) dot[h] = 0.0f;
+                if (j < nt) {
 #pragma unroll
-                    for (int e = 0; e < EPV; ++e) {
-                        kf[v * EPV + e] = 0.0f;
-                        vf[v * EPV + e] = 0.0f;
+                    for (int c = 0; c < CPP; ++c) {
+                        const int ch = lp + c * NPART;
+                        const uint4 kw = *reinterpret_cast<const uint4*>(st3 + (size_t)j * RB + (size_t)ch * 16);
+                        float kf[EPV];
+                        vec_to_f<T>(kw, kf);
+#pragma unroll
+                        for (int h = 0; h < MAXG; ++h)
+#pragma unroll
+                            for (int e = 0; e < EPV; ++e) {
+                                const float qv = QREG ? qreg[QREG ? h : 0][QREG ? c * EPV + e : 0] : qf[h * D + ch * EPV + e];
+                                dot[h] = fmaf(qv, kf[e], dot[h]);
+                            }
                     }
                 }
+                float mine = dot[0];
+#pragma unroll
+                for (int h = 0; h < MAXG; ++h) {
+                    dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], 4);
+                    dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], 2);
+                    dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], 1);
+                    if (h == lp) mine = dot[h];
+                }
+                if (j < nt && lp < G) sc[(size_t)lp * a.score_stride + j0 + j] = mine * a.inv_sqrt_d;
             }
-            float sc[MAXG];
-#pragma unroll
-            for (int h = 0; h < MAXG; ++h) {
-                float t = 0.0f;
-#pragma unroll
-                for (int e = 0; e < EPL; ++e) t = fmaf(qr[h][e], kf[e], t);
-                sc[h] = t;
-            }
-#pragma unroll
-            for (int o = LPT / 2; o > 0; o >>= 1)
-#pragma unroll
-                for (int h = 0; h < MAXG; ++h) sc[h] += __shfl_xor_sync(0xffffffffu, sc[h], o);
-            if (okj) {
+        } else {
+            // ---- pass C: p * v for the tokens in this V stage ----
+            const int j0 = (s - nA) * TS, nt = min(TS, n - j0);
+            for (int j = cg; j < nt; j += NGC) {
+                const uint32_t vw = *reinterpret_cast<const uint32_t*>(st3 + (size_t)j * RB + (size_t)dw * 4);
+                float vf[EW];
+                if constexpr (EW == 2) {
+                    vf[0] = __uint_as_float(vw << 16);
+                    vf[1] = __uint_as_float(vw & 0xffff0000u);
+                } else {
+                    vf[0] = __uint_as_float(vw);
+                }
 #pragma unroll
                 for (int h = 0; h < MAXG; ++h) {
                     if (h < G) {
-                        const float x = sc[h] * a.inv_sqrt_d;
-                        const float mn = fmaxf(mrun[h], x);
-                        const float corr = __expf(mrun[h] - mn);
-                        const float p = __expf(x - mn);
-                        lrun[h] = fmaf(lrun[h], corr, p);
+                        const float p = sc[(size_t)h * a.score_stride + j0 + j];
 #pragma unroll
-                        for (int e = 0; e < EPL; ++e) acc[h][e] = fmaf(p, vf[e], acc[h][e] * corr);
-                        mrun[h] = mn;
+                        for (int e = 0; e < EW; ++e) accv[h][e] = fmaf(p, vf[e], accv[h][e]);
                     }
                 }
             }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty3[slot]);
-        if (warp == 0 && s >= 1 && s - 1 + kNStage < nst3) {
+        if (warp == 0 && s >= 1 && s - 1 + kNStageT < nS) {
             const int sp = s - 1;
-            if (mbar_wait_bounded(&empty3[sp % kNStage], (uint32_t)((sp / kNStage) & 1), a.err)) {
+            if (mbar_wait_bounded(&empty3[sp % kNStageT], (uint32_t)((sp / kNStageT) & 1), a.err)) {
                 fence_proxy_async();
-                issue3(sp + kNStage);
+                issue3(sp + kNStageT);
             } else {
                 ok3 = false;  // the consumers' wait on the unfilled slot runs out as well
             }
@@ -527,69 +685,68 @@ __global__ void __launch_bounds__(kNT, (MAXG <= 3 ? 3 : 2)) hsa_kernel(const Hsa
     if (!ok3) s_abort = 1;
     __syncthreads();
     if (s_abort) return;
-    float* comb = reinterpret_cast<float*>(ring);  // [NGROUPS][MAXG][D + 2]
+    // merge the NGC token groups: red[group][head][D]
+    float* red = reinterpret_cast<float*>(ring);
 #pragma unroll
-    for (int h = 0; h < MAXG; ++h) {
-        if (h < G) {
-            float* cg = comb + ((size_t)grp * MAXG + h) * (D + 2);
+    for (int h = 0; h < MAXG; ++h)
+        if (h < G)
 #pragma unroll
-            for (int v = 0; v < VPL; ++v)
-#pragma unroll
-                for (int e = 0; e < EPV; ++e) cg[(gl + v * LPT) * EPV + e] = acc[h][v * EPV + e];
-            if (gl == 0) {
-                cg[D] = mrun[h];
-                cg[D + 1] = lrun[h];
-            }
-        }
-    }
+            for (int e = 0; e < EW; ++e) red[((size_t)cg * MAXG + h) * D + dw * EW + e] = accv[h][e];
     __syncthreads();
     float* Ob = a.O + (size_t)b * a.H * D + (size_t)hk * G * D;
     for (int e = tid; e < G * D; e += kNT) {
         const int h = e / D, d = e - h * D;
-        float M = -INFINITY;
-        for (int g = 0; g < NGROUPS; ++g) M = fmaxf(M, comb[((size_t)g * MAXG + h) * (D + 2) + D]);
-        float L = 0.0f, o = 0.0f;
-        if (M != -INFINITY) {
-            for (int g = 0; g < NGROUPS; ++g) {
-                const float* cg = comb + ((size_t)g * MAXG + h) * (D + 2);
-                const float mg = cg[D];
-                if (mg == -INFINITY) continue;
-                const float f = __expf(mg - M);
-                L = fmaf(cg[D + 1], f, L);
-                o = fmaf(cg[d], f, o);
-            }
-        }
-        Ob[h * D + d] = L > 0.0f ? o / L : 0.0f;
+        float o = 0.0f;
+        for (int g = 0; g < NGC; ++g) o += red[((size_t)g * MAXG + h) * D + d];
+        Ob[h * D + d] = n > 0 ? o * hinv[h] : 0.0f;
     }
+}
+
+int num_sms() {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+        n = 148;
+    return n;
 }
 
 template <typename T, int D, int MAXG>
 int launch_t(HsaArgs a, int batch, cudaStream_t st) {
-    constexpr int EPV = 16 / (int)sizeof(T);
-    constexpr int NV = D / EPV;
-    constexpr int LPT = NV < 32 ? NV : 32;
-    constexpr int NGROUPS = (kNT / 32) * (32 / LPT);
-    const int sr_max = kStageBytes / (int)(D * sizeof(T));
-    if (a.C <= sr_max) {
-        a.carry_mode = 0;
-        a.stage_rows = a.C * (sr_max / a.C);
-        a.chunks_per_stage = a.stage_rows / a.C;
-    } else {
-        a.carry_mode = 1;
-        a.stage_rows = sr_max;
-        a.chunks_per_stage = 2;
+    constexpr int NGC = kNT / (int)(D * sizeof(T) / 4);
+    static_assert((size_t)NGC * MAXG * D * sizeof(float) <= (size_t)kTailRing, "tail merge buffer");
+    if (a.nchunks > 0) {
+        const int sr_max = kStageBytes / (int)(D * sizeof(T));
+        if (a.C <= sr_max) {
+            a.carry_mode = 0;
+            a.stage_rows = a.C * (sr_max / a.C);
+        } else {
+            a.carry_mode = 1;
+            a.stage_rows = sr_max;
+        }
+        // enough scan CTAs to cover the GPU; every split keeps at least 4 stages of pages
+        const long long units = (long long)batch * a.head_count;
+        const long long want = 3LL * num_sms();
+        int splits = units >= want ? 1 : (int)((want + units - 1) / units);
+        const int min_pages = a.carry_mode ? 1 : 4 * (a.stage_rows / a.C);
+        const int max_splits = (a.nchunks + min_pages - 1) / min_pages;
+        if (splits > max_splits) splits = max_splits;
+        if (splits < 1) splits = 1;
+        a.pages_per_split = (a.nchunks + splits - 1) / splits;
+        a.splits = (a.nchunks + a.pages_per_split - 1) / a.pages_per_split;
+        const size_t smem_s = (size_t)kNStageS * kStageBytes + 128 + (a.carry_mode ? (size_t)2 * (D + 1) * 4 : 0);
+        auto fs = hsa_scan_kernel<T, D, MAXG>;
+        if (cudaFuncSetAttribute(fs, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_s) != cudaSuccess)
+            return RKV_ERR_CUDA;
+        fs<<<dim3(a.splits, a.head_count, batch), kNT, smem_s, st>>>(a);
+        if (cudaGetLastError() != cudaSuccess) return RKV_ERR_CUDA;
     }
-    const size_t ring = (size_t)kNStage * kStageBytes;
-    const size_t comb = (size_t)NGROUPS * MAXG * (D + 2) * sizeof(float);
-    const size_t region0 = align_up(ring > comb ? ring : comb, 128);
-    a.off_bar = (int)region0;
-    a.off_pst = (int)(region0 + 128);
-    a.smem_bytes = (int)(a.off_pst + (a.carry_mode ? (size_t)2 * (D + 1) * sizeof(float) : 0));
-    auto fn = hsa_kernel<T, D, MAXG>;
-    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, a.smem_bytes) != cudaSuccess)
+    const size_t lists = (size_t)a.score_stride * 4 * (1 + a.G);
+    a.tail_smem_lists = lists <= (size_t)kTailListMax ? 1 : 0;
+    const size_t smem_t = (size_t)kTailRing + 128 + (a.tail_smem_lists ? lists : 0);
+    auto ft = hsa_tail_kernel<T, D, MAXG>;
+    if (cudaFuncSetAttribute(ft, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_t) != cudaSuccess)
         return RKV_ERR_CUDA;
-    dim3 grid(a.head_count, batch);
-    fn<<<grid, kNT, a.smem_bytes, st>>>(a);
+    ft<<<dim3(a.head_count, batch), kNT, smem_t, st>>>(a);
     return cudaGetLastError() == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
 }
 
@@ -648,6 +805,9 @@ HsaShape hsa_shape(const rkv_config& c, int len_k, int recent_window, int batch,
     off = align_up(off + (size_t)batch * head_count * s.G * (size_t)s.nchunks * sizeof(float), kWorkspaceAlign);
     s.off_sel = off;
     off = align_up(off + (size_t)batch * head_count * (size_t)(s.sel_cap > 0 ? s.sel_cap : 1) * sizeof(int),
+                   kWorkspaceAlign);
+    s.off_scores = off;
+    off = align_up(off + (size_t)batch * head_count * s.G * (size_t)(s.sel_cap > 0 ? s.sel_cap : 1) * sizeof(float),
                    kWorkspaceAlign);
     s.ws_bytes = off;
     return s;

@@ -16,7 +16,7 @@ struct HsaArgs {
     int w;          // recent window (tokens always attended)
     int Lc;         // len_k - w: tokens eligible for the top-k
     int final_k;    // min(topk, Lc)
-    int nchunks;    // ceil(Lc / C) when the chunk scoring runs, else 0
+    int nchunks;    // ceil(Lc / C) when the page scoring runs, else 0
     int head_begin, head_count;
     int sel_stride;
     float inv_sqrt_d;
@@ -24,16 +24,20 @@ struct HsaArgs {
     int* sel;        // [batch][head_count][sel_stride]
     int* n_sel;      // nullable [batch][head_count]
     float* wlogits;  // workspace [batch][head_count][G][nchunks]
+    float* wscore;   // workspace [batch][head_count][G][score_stride]: attention scores / p
+    int score_stride;
     int* err;        // workspace error word
-    // shared-memory plan (bytes), filled by the launcher
-    int stage_rows, nstages_ring, chunks_per_stage, carry_mode;
-    int off_bar, off_qf, off_sabs, off_qsum, off_qsel, off_sgn, off_R, off_flag, off_pst, off_part, off_misc;
-    int smem_bytes;
+    // launch plan, filled by the launcher
+    int splits;           // scan CTAs per unit
+    int pages_per_split;  // pages each scan CTA covers
+    int stage_rows;       // rows per scan stage
+    int carry_mode;       // a page spans more than one scan stage
+    int tail_smem_lists;  // the tail keeps selected indices and scores in shared memory
 };
 
 struct HsaShape {
     int G, C, r, w, Lc, final_k, nchunks, sel_cap;
-    size_t off_logits, off_sel, ws_bytes;
+    size_t off_logits, off_sel, off_scores, ws_bytes;
 };
 
 HsaShape hsa_shape(const rkv_config& c, int len_k, int recent_window, int batch, int head_count);

@@ -421,6 +421,8 @@ int rkv_hsa_decode(const void* Q, const void* K, const void* V, int dtype, int l
     }
     a.n_sel = n_sel;
     a.wlogits = reinterpret_cast<float*>(ws + s.off_logits);
+    a.wscore = reinterpret_cast<float*>(ws + s.off_scores);
+    a.score_stride = s.sel_cap > 0 ? s.sel_cap : 1;
     a.err = reinterpret_cast<int*>(ws);
     return launch_hsa(a, dtype, batch, st);
 }

@@ -129,10 +129,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait for phase `parity` of `bar`.  Returns false (and records
 // RKV_ERR_DEVICE_TIMEOUT in *err) if the clock budget runs out.
+// Backs off with a short sleep between polls so waiting warps leave the
+// issue slots to the warps that have work.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
+    unsigned ns = 32;
     while (!mbar_try_wait(bar, parity)) {
+        __nanosleep(ns);
+        if (ns < 256) ns <<= 1;
         if (clock64() - t0 > kWaitCycles) {
             atomicExch(err, (int)RKV_ERR_DEVICE_TIMEOUT);
             return false;
