@@ -39,6 +39,11 @@ PROMPT, MAX_NEW, BUDGET = 8192, 32, 1024
 WINDOW = 32
 
 
+def set_workload(seqs: int, layers: int) -> None:
+    global SEQS, LAYERS
+    SEQS, LAYERS = seqs, layers
+
+
 def decode_params():
     import rocketkv_b200 as rkv
     p = rkv.compute_rocket_params(BUDGET, PROMPT, MAX_NEW, D)  # 3685 / 512 / 2 / 71
@@ -351,7 +356,12 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--seqs", type=int, default=SEQS,
+                    help="sequences per GPU (smaller values are profiling cases, not the benchmark)")
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="layers per step (smaller values are profiling cases, not the benchmark)")
     args = ap.parse_args()
+    set_workload(args.seqs, args.layers)
     args.warmup = max(args.warmup, 3)
 
     if args.impl == "reference":
