@@ -178,6 +178,24 @@ int rkv_hsa_decode_host_ex(const void* Q, const void* K, const void* V, int dtyp
                            const rkv_config* cfg, float* O, int* sel, int sel_stride,
                            int* n_sel);
 
+/* No-allocation stage 2.  This entry point has no counterpart in the
+ * reference; it exists for callers that cannot allocate device memory (an
+ * inference server or plugin host whose allocator owns the device heap, or a
+ * hot loop that cannot take cudaMalloc's implicit synchronisation).  Same
+ * arguments and results as rkv_hsa_decode, without the workspace: the scratch
+ * is a fixed 4 MiB array of device memory inside the library, present on
+ * every GPU that loads it until the process exits.  A call whose
+ * rkv_hsa_workspace_size exceeds 4 MiB returns RKV_ERR_WORKSPACE and launches
+ * nothing.  No call allocates.  The first call on each device looks up that
+ * device's copy of the array (cudaGetSymbolAddress); make it before any
+ * stream capture.  All calls share the one array, so calls that overlap on
+ * the GPU (other streams, other host threads) race: serialise them. */
+int rkv_hsa_decode_noalloc(const void* Q, const void* K, const void* V, int dtype, int len_k,
+                           int recent_window, int batch, long long q_item_stride,
+                           long long kv_item_stride, const rkv_config* cfg, int head_begin,
+                           int head_count, float* O, int* sel, int sel_stride, int* n_sel,
+                           void* stream);
+
 /* ---- errors raised inside kernels ----------------------------------------
  * Kernels record a failed bounded wait in the workspace.  This synchronises
  * `stream`, returns RKV_OK or the recorded status, and clears it. */

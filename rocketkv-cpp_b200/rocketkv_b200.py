@@ -35,7 +35,7 @@ EXPORTS = [
     "rkv_evict_max_kept", "rkv_evict_workspace_size", "rkv_evict", "rkv_evict_pool_heads",
     "rkv_evict_select_pooled", "rkv_prefill_eviction_host", "rkv_hsa_sel_capacity",
     "rkv_hsa_workspace_size", "rkv_hsa_decode", "rkv_hybrid_sparse_decode_host",
-    "rkv_hsa_decode_host_ex", "rkv_workspace_status",
+    "rkv_hsa_decode_host_ex", "rkv_workspace_status", "rkv_hsa_decode_noalloc",
 ]
 
 
@@ -127,6 +127,8 @@ def lib() -> ctypes.CDLL:
         "rkv_hybrid_sparse_decode_host": ([_VP, _VP, _VP, _I, _CFGP, _VP], _I),
         "rkv_hsa_decode_host_ex": ([_VP, _VP, _VP, _I, _I, _I, _I, _LL, _LL, _CFGP, _VP, _VP, _I, _VP], _I),
         "rkv_workspace_status": ([_VP, _VP], _I),
+        "rkv_hsa_decode_noalloc": ([_VP, _VP, _VP, _I, _I, _I, _I, _LL, _LL, _CFGP, _I, _I, _VP, _VP, _I, _VP,
+                                    _VP], _I),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
