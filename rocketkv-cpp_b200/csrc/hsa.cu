@@ -18,16 +18,17 @@
 //      over several CTAs so the grid still covers the GPU.
 //
 // hsa_tail_kernel   grid (KV heads, items)
-//   2. the unit's page logits are staged in shared memory: per-head softmax
-//      with the deterministic exp and a fixed 256-way summation order, the group
-//      sum, a weighted radix select of the top final_k tokens by (score desc,
+//   2. the unit's page logits are staged in shared memory by one bulk copy;
+//      per-head softmax with the deterministic exp and a fixed 256-way
+//      summation order, the group sum, a weighted radix select of the top final_k tokens by (score desc,
 //      index asc) and a stable compaction to ascending order
 //      (rocket.cpp:291-340), then the recent window;
 //   3. exact attention over the selected rows (rocket.cpp:342-378): the
-//      selected K rows, then the V rows, stream through a 3-stage ring by
-//      per-row bulk copies; scores (eight lanes per token), per-head softmax
-//      statistics, then p * v with one thread per 4-byte V word.  Selected
-//      indices and scores stay in shared memory when they fit.
+//      selected K rows and then V rows are gathered with 16-byte read-only
+//      loads, several tokens in flight per thread; scores (eight lanes per
+//      token), per-head softmax statistics, then p * v with one thread per
+//      16-byte V vector.  Logits, selected indices and scores stay in shared
+//      memory when they fit.
 //
 // Phases 0-2 repeat the oracle's float operations one for one, so the selected
 // indices equal the oracle's bit for bit; O is tolerance-checked.
@@ -41,9 +42,7 @@ namespace {
 constexpr int kNT = 256;
 constexpr int kStageBytes = 16384;
 constexpr int kNStageS = 4;  // scan ring stages
-constexpr int kNStageT = 3;  // tail ring stages
-constexpr int kTailRing = kNStageT * kStageBytes;
-constexpr int kTailListMax = 48 * 1024;  // selected indices + scores kept in shared memory up to this
+constexpr int kTailSmemMax = 96 * 1024;  // staged logits + indices + scores kept in shared memory up to this
 
 template <typename T>
 __device__ __forceinline__ float to_f(T v);
@@ -123,7 +122,7 @@ __global__ void __launch_bounds__(kNT, 3) hsa_scan_kernel(const HsaArgs a) {
     if (p_beg >= p_end) return;  // uniform
     const uint8_t* Qg = a.Q + (size_t)b * a.q_stride + (size_t)hk * G * D * sizeof(T);
     const uint8_t* Ku = a.K + (size_t)b * a.kv_stride + (size_t)hk * a.len_k * RB;
-    float* wl = a.wlogits + ((size_t)b * a.head_count + hc) * (size_t)G * nch;
+    float* wl = a.wlogits + ((size_t)b * a.head_count + hc) * (size_t)G * a.nch_pad;
 
     if (tid == 0) {
         for (int s = 0; s < kNStageS; ++s) {
@@ -298,7 +297,7 @@ __global__ void __launch_bounds__(kNT, 3) hsa_scan_kernel(const HsaArgs a) {
                 if (h == s8) mine = acc[h];
             }
             // every lane of the eight holds the sums; lane h divides head h
-            if (task < ntask && s8 < G) wl[(size_t)s8 * nch + c_lo + cl] = __fdiv_rn(mine, my_scale);
+            if (task < ntask && s8 < G) wl[(size_t)s8 * a.nch_pad + c_lo + cl] = __fdiv_rn(mine, my_scale);
         }
         if (a.carry_mode) __syncthreads();  // pst reuse
         __syncwarp();
@@ -322,64 +321,68 @@ __global__ void __launch_bounds__(kNT, 3) hsa_scan_kernel(const HsaArgs a) {
 // ===========================================================================
 // Tail kernel: phases 2 and 3
 // ===========================================================================
-template <typename T, int D, int MAXG>
+// SMEM: the unit's page logits, selected indices and scores live in shared
+// memory (the common case); otherwise they stay in the workspace.
+template <typename T, int D, int MAXG, bool SMEM>
 __global__ void __launch_bounds__(kNT, 3) hsa_tail_kernel(const HsaArgs a) {
     extern __shared__ __align__(128) uint8_t sm[];
-    uint8_t* ring = sm;
-    uint64_t* full3 = reinterpret_cast<uint64_t*>(sm + kTailRing);
-    uint64_t* empty3 = full3 + kNStageT;
-    // selected indices and per-head scores live in shared memory when they fit
-    // (a.tail_smem_lists), else in the workspace
-    int* sel_s = a.tail_smem_lists ? reinterpret_cast<int*>(sm + kTailRing + 128) : nullptr;
-    float* sc_s = a.tail_smem_lists ? reinterpret_cast<float*>(sm + kTailRing + 128 + (size_t)a.score_stride * 4)
-                                    : nullptr;
+    uint64_t* lbar = reinterpret_cast<uint64_t*>(sm);            // logits bulk copy
+    float* r0 = reinterpret_cast<float*>(sm + 128);             // staged logits, later the merge buffer
+    int* sel_s = reinterpret_cast<int*>(sm + 128 + a.tail_r0_bytes);
+    float* sc_s = reinterpret_cast<float*>(sm + 128 + a.tail_r0_bytes + (size_t)a.score_stride * 4);
 
-    __shared__ float qf[MAXG * D];
+    __shared__ __align__(16) float qf[MAXG * D];
     __shared__ float part[MAXG][kNT];
     __shared__ float part_[MAXG][kNT / 32];
     __shared__ float hmax[MAXG], hinv[MAXG];
     __shared__ int hist[256], scan_tmp[33];
-    __shared__ int s_abort, s_kk;
+    __shared__ int s_kk;
     __shared__ uint32_t s_prefix;
 
     constexpr size_t RB = (size_t)D * sizeof(T);
+    constexpr int EPV = 16 / (int)sizeof(T);  // elements per 16-byte vector
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int hc = blockIdx.x, b = blockIdx.y, hk = a.head_begin + hc;
     const int G = a.G;
+    const size_t unit = (size_t)b * a.head_count + hc;
     const uint8_t* Qg = a.Q + (size_t)b * a.q_stride + (size_t)hk * G * D * sizeof(T);
     const uint8_t* Ku = a.K + (size_t)b * a.kv_stride + (size_t)hk * a.len_k * RB;
     const uint8_t* Vu = a.V + (size_t)b * a.kv_stride + (size_t)hk * a.len_k * RB;
-    int* sel_g = a.sel + ((size_t)b * a.head_count + hc) * a.sel_stride;
-    int* sel = sel_s ? sel_s : sel_g;
-    const int nch = a.nchunks;
+    int* sel_g = a.sel + unit * a.sel_stride;
+    int* sel = SMEM ? sel_s : sel_g;
+    float* sc = SMEM ? sc_s : a.wscore + unit * (size_t)G * a.score_stride;  // [G][score_stride]
+    const int nch = a.nchunks, NP = a.nch_pad;
+    float* wg = a.wlogits + unit * (size_t)G * NP;
+    float* wl = SMEM ? r0 : wg;  // [G][NP]
 
     if (tid == 0) {
-        s_abort = 0;
-        for (int s = 0; s < kNStageT; ++s) {
-            mbar_init(&full3[s], 1);
-            mbar_init(&empty3[s], kNT / 32);
-        }
+        mbar_init(lbar, 1);
         fence_mbar_init();
     }
     for (int e = tid; e < G * D; e += kNT) qf[e] = to_f<T>(reinterpret_cast<const T*>(Qg)[e]);
+    for (int i = tid; i < 256; i += kNT) hist[i] = 0;
+    __syncthreads();
+    bool ok = true;
+    if (SMEM && nch > 0) {
+        if (tid == 0) {  // the unit's logits are one contiguous, 16-byte aligned block
+            const uint32_t bytes = (uint32_t)((size_t)G * NP * sizeof(float));
+            mbar_arrive_expect_tx(lbar, bytes);
+            bulk_load(r0, wg, bytes, lbar);
+        }
+        ok = mbar_wait_bounded(lbar, 0, a.err);
+    }
+    if (__syncthreads_or(!ok)) return;  // uniform: nobody passes an incomplete copy
 
     int nfirst;  // selected tokens from the scored range
     if (nch > 0) {
         // ---- phase 2: page softmax per head, group sum, weighted top-k ----
-        // The page logits are staged in the (still idle) ring when they fit.
-        float* wg = a.wlogits + ((size_t)b * a.head_count + hc) * (size_t)G * nch;
-        const bool staged = (size_t)G * nch * sizeof(float) <= (size_t)kTailRing;
-        float* wl = staged ? reinterpret_cast<float*>(ring) : wg;
-        if (staged)
-            for (int e = tid; e < G * nch; e += kNT) wl[e] = __ldcg(wg + e);
-        __syncthreads();
         float m[MAXG];
 #pragma unroll
         for (int h = 0; h < MAXG; ++h) m[h] = -INFINITY;
         for (int c = tid; c < nch; c += kNT)
 #pragma unroll
             for (int h = 0; h < MAXG; ++h)
-                if (h < G) m[h] = fmaxf(m[h], wl[(size_t)h * nch + c]);
+                if (h < G) m[h] = fmaxf(m[h], wl[(size_t)h * NP + c]);
 #pragma unroll
         for (int h = 0; h < MAXG; ++h) {
             float v = m[h];
@@ -401,8 +404,8 @@ __global__ void __launch_bounds__(kNT, 3) hsa_tail_kernel(const HsaArgs a) {
 #pragma unroll
             for (int h = 0; h < MAXG; ++h)
                 if (h < G) {
-                    const float e = det_expf(__fsub_rn(wl[(size_t)h * nch + c], hmax[h]));
-                    wl[(size_t)h * nch + c] = e;
+                    const float e = det_expf(__fsub_rn(wl[(size_t)h * NP + c], hmax[h]));
+                    wl[(size_t)h * NP + c] = e;
                     ps[h] = __fadd_rn(ps[h], e);
                 }
 #pragma unroll
@@ -429,7 +432,7 @@ __global__ void __launch_bounds__(kNT, 3) hsa_tail_kernel(const HsaArgs a) {
         uint32_t* keys = reinterpret_cast<uint32_t*>(wl);  // head-0 row, overwritten page by page
         for (int c = tid; c < nch; c += kNT) {
             float g = 0.0f;
-            for (int h = 0; h < G; ++h) g = __fadd_rn(g, __fmul_rn(wl[(size_t)h * nch + c], hinv[h]));
+            for (int h = 0; h < G; ++h) g = __fadd_rn(g, __fmul_rn(wl[(size_t)h * NP + c], hinv[h]));
             keys[c] = float_key(g);
         }
         if (tid == 0) {
@@ -437,24 +440,47 @@ __global__ void __launch_bounds__(kNT, 3) hsa_tail_kernel(const HsaArgs a) {
             s_kk = a.final_k;
         }
         __syncthreads();
+        // 4 x 8-bit radix select of the final_k-th token (pages weighted by
+        // their token count).  Warp 0 scans the 256 bins from the top digit
+        // down and clears them for the next pass: two barriers per pass.
         uint32_t mask = 0u;
         for (int shift = 24; shift >= 0; shift -= 8) {
-            for (int i = tid; i < 256; i += kNT) hist[i] = 0;
-            __syncthreads();
             const uint32_t prefix = s_prefix;
             for (int c = tid; c < nch; c += kNT) {
                 const uint32_t k = keys[c];
                 if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], min(a.C, a.Lc - c * a.C));
             }
             __syncthreads();
-            // token counts from the top digit down; the digit where the running count reaches kk
-            const int kk = s_kk;
-            const int v = hist[255 - tid];
-            int tot;
-            const int before = block_exclusive_scan(v, scan_tmp, &tot);
-            if (before < kk && before + v >= kk) {
-                s_kk = kk - before;
-                s_prefix = prefix | ((uint32_t)(255 - tid) << shift);
+            if (warp == 0) {
+                int cnt[8], local = 0;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    cnt[j] = hist[255 - 8 * lane - j];
+                    local += cnt[j];
+                }
+                int incl = local;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += y;
+                }
+                const int before = incl - local;
+                const int kk = s_kk;
+                __syncwarp();
+                if (before < kk && before + local >= kk) {
+                    int run = before;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        if (run + cnt[j] >= kk) {
+                            s_kk = kk - run;
+                            s_prefix = prefix | ((uint32_t)(255 - 8 * lane - j) << shift);
+                            break;
+                        }
+                        run += cnt[j];
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) hist[255 - 8 * lane - j] = 0;
             }
             mask |= 255u << shift;
             __syncthreads();
@@ -496,146 +522,63 @@ __global__ void __launch_bounds__(kNT, 3) hsa_tail_kernel(const HsaArgs a) {
     }
     for (int t = tid; t < a.w; t += kNT) sel[nfirst + t] = a.Lc + t;
     const int n = nfirst + a.w;
-    if (tid == 0 && a.n_sel) a.n_sel[(size_t)b * a.head_count + hc] = n;
+    if (tid == 0 && a.n_sel) a.n_sel[unit] = n;
     __syncthreads();
-    if (sel_s)
+    if (SMEM)
         for (int i = tid; i < n; i += kNT) sel_g[i] = sel_s[i];
 
     // ---- phase 3: exact attention over the selected rows -------------------
-    // One stream of 16 KB stages through the ring: first the selected K rows,
-    // then the selected V rows, one bulk copy per row issued by the lanes of
-    // warp 0.  Pass A: eight lanes per token form q.k for every head;
-    // pass B: per-head max, p = exp(s - max) and sum(p); pass C: each thread
-    // owns one 4-byte word of the V row and accumulates p * v per head.
-    constexpr int TS = kStageBytes / (int)RB;   // rows per stage
-    constexpr int EPV = 16 / (int)sizeof(T);    // elements per 16-byte chunk
-    constexpr int CPR = (int)RB / 16;           // 16-byte chunks per row
-    constexpr int NPART = 8;                    // pass-A lanes per token
-    constexpr int CPP = CPR / NPART;            // chunks per lane
-    constexpr int TPS = kNT / NPART;            // tokens per pass-A step
-    constexpr bool QREG = MAXG * CPP * EPV <= 48;
-    constexpr int NDP = (int)RB / 4;            // 4-byte words per row
-    constexpr int NGC = kNT / NDP;              // pass-C token groups
-    constexpr int EW = 4 / (int)sizeof(T);      // elements per word
+    // Gathers are direct 16-byte read-only loads, several tokens in flight per
+    // thread.  Pass A: eight lanes per token form q.k for every head; pass B:
+    // per-head max, p = exp(s - max) and sum(p); pass C: each thread owns one
+    // 16-byte vector of the V row and accumulates p * v per head.
+    constexpr int CPR = (int)RB / 16;  // 16-byte vectors per row
+    constexpr int NPART = 8;           // pass-A lanes per token
+    constexpr int CPP = CPR / NPART;   // vectors per lane
+    constexpr int TPR = kNT / NPART;   // tokens per pass-A round
+    constexpr int UA = CPP >= 4 ? 1 : 4 / CPP;
+    constexpr int NGC = kNT / CPR;     // pass-C token groups
+    constexpr int UC = 4;
     static_assert(CPP >= 1 && NGC >= 1, "row layout");
-    const int nA = (n + TS - 1) / TS;
-    const int nS = 2 * nA;
-    float* sc = sc_s ? sc_s : a.wscore + ((size_t)b * a.head_count + hc) * (size_t)G * a.score_stride;  // [G][n]
-
-    auto issue3 = [&](int s) {  // all lanes of warp 0
-        const int slot = s % kNStageT;
-        const bool is_v = s >= nA;
-        const int j0 = (is_v ? s - nA : s) * TS, nt = min(TS, n - j0);
-        if (lane == 0) mbar_arrive_expect_tx(&full3[slot], (uint32_t)(nt * RB));
-        __syncwarp();
-        uint8_t* dst = ring + (size_t)slot * kStageBytes;
-        const uint8_t* src = is_v ? Vu : Ku;
-        for (int j = lane; j < nt; j += 32)
-            bulk_load(dst + (size_t)j * RB, src + (size_t)sel[j0 + j] * RB, (uint32_t)RB, &full3[slot]);
-    };
-    if (warp == 0) {
-        fence_proxy_async();
-        for (int s = 0; s < kNStageT && s < nS; ++s) issue3(s);
-    }
-
-    const int lp = tid % NPART, tok = tid / NPART;
-    float qreg[QREG ? MAXG : 1][QREG ? CPP * EPV : 1];
-    if constexpr (QREG) {
+    {
+        const int lp = tid % NPART, tok = tid / NPART;
+        for (int j0 = 0; j0 < n; j0 += TPR * UA) {  // uniform trip count
+            uint4 kw[UA][CPP];
 #pragma unroll
-        for (int h = 0; h < MAXG; ++h)
+            for (int u = 0; u < UA; ++u) {
+                const int j = j0 + u * TPR + tok;
+                if (j < n) {
+                    const uint4* kr = reinterpret_cast<const uint4*>(Ku + (size_t)sel[j] * RB);
 #pragma unroll
-            for (int c = 0; c < CPP; ++c)
-#pragma unroll
-                for (int e = 0; e < EPV; ++e)
-                    qreg[h][c * EPV + e] = h < G ? qf[h * D + (lp + c * NPART) * EPV + e] : 0.0f;
-    }
-    const int dw = tid % NDP, cg = tid / NDP;
-    float accv[MAXG][EW];
-#pragma unroll
-    for (int h = 0; h < MAXG; ++h)
-#pragma unroll
-        for (int e = 0; e < EW; ++e) accv[h][e] = 0.0f;
-
-    bool ok3 = true;
-    for (int s = 0; s < nS; ++s) {
-        if (s == nA) {
-            // ---- pass B: softmax statistics over the n scores per head ----
-            __syncthreads();
-            float m[MAXG];
-#pragma unroll
-            for (int h = 0; h < MAXG; ++h) m[h] = -INFINITY;
-            for (int i = tid; i < n; i += kNT)
-#pragma unroll
-                for (int h = 0; h < MAXG; ++h)
-                    if (h < G) m[h] = fmaxf(m[h], sc[(size_t)h * a.score_stride + i]);
-#pragma unroll
-            for (int h = 0; h < MAXG; ++h) {
-                float v = m[h];
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-                if (lane == 0) part_[h][warp] = v;
+                    for (int c = 0; c < CPP; ++c) kw[u][c] = __ldg(kr + lp + c * NPART);
+                }
             }
-            __syncthreads();
-            if (tid < G) {
-                float v = -INFINITY;
-                for (int wi = 0; wi < kNT / 32; ++wi) v = fmaxf(v, part_[tid][wi]);
-                hmax[tid] = v;
-            }
-            __syncthreads();
-            float ssum[MAXG];
 #pragma unroll
-            for (int h = 0; h < MAXG; ++h) ssum[h] = 0.0f;
-            for (int i = tid; i < n; i += kNT)
-#pragma unroll
-                for (int h = 0; h < MAXG; ++h)
-                    if (h < G) {
-                        const float p = __expf(sc[(size_t)h * a.score_stride + i] - hmax[h]);
-                        sc[(size_t)h * a.score_stride + i] = p;
-                        ssum[h] += p;
-                    }
-#pragma unroll
-            for (int h = 0; h < MAXG; ++h) {
-                float v = ssum[h];
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                if (lane == 0) part_[h][warp] = v;
-            }
-            __syncthreads();
-            if (tid < G) {
-                float v = 0.0f;
-                for (int wi = 0; wi < kNT / 32; ++wi) v += part_[tid][wi];
-                hinv[tid] = 1.0f / v;
-            }
-            __syncthreads();
-        }
-        const int slot = s % kNStageT;
-        if (!mbar_wait_bounded(&full3[slot], (uint32_t)((s / kNStageT) & 1), a.err)) {
-            ok3 = false;
-            break;
-        }
-        const uint8_t* st3 = ring + (size_t)slot * kStageBytes;
-        if (s < nA) {
-            // ---- pass A: scores of the tokens in this K stage ----
-            const int j0 = s * TS, nt = min(TS, n - j0);
-            for (int jb = 0; jb < nt; jb += TPS) {  // uniform trip count
-                const int j = jb + tok;
+            for (int u = 0; u < UA; ++u) {
+                const int j = j0 + u * TPR + tok;
                 float dot[MAXG];
 #pragma unroll
                 for (int h = 0; h < MAXG; ++h) dot[h] = 0.0f;
-                if (j < nt) {
+                if (j < n) {
 #pragma unroll
                     for (int c = 0; c < CPP; ++c) {
-                        const int ch = lp + c * NPART;
-                        const uint4 kw = *reinterpret_cast<const uint4*>(st3 + (size_t)j * RB + (size_t)ch * 16);
                         float kf[EPV];
-                        vec_to_f<T>(kw, kf);
+                        vec_to_f<T>(kw[u][c], kf);
+                        const int ch = lp + c * NPART;
 #pragma unroll
-                        for (int h = 0; h < MAXG; ++h)
+                        for (int h = 0; h < MAXG; ++h) {
+                            if (h < G) {
+                                const float4* q4 = reinterpret_cast<const float4*>(qf + h * D + ch * EPV);
 #pragma unroll
-                            for (int e = 0; e < EPV; ++e) {
-                                const float qv = QREG ? qreg[QREG ? h : 0][QREG ? c * EPV + e : 0] : qf[h * D + ch * EPV + e];
-                                dot[h] = fmaf(qv, kf[e], dot[h]);
+                                for (int e4 = 0; e4 < EPV / 4; ++e4) {
+                                    const float4 q = q4[e4];
+                                    dot[h] = fmaf(q.x, kf[4 * e4], dot[h]);
+                                    dot[h] = fmaf(q.y, kf[4 * e4 + 1], dot[h]);
+                                    dot[h] = fmaf(q.z, kf[4 * e4 + 2], dot[h]);
+                                    dot[h] = fmaf(q.w, kf[4 * e4 + 3], dot[h]);
+                                }
                             }
+                        }
                     }
                 }
                 float mine = dot[0];
@@ -646,52 +589,98 @@ __global__ void __launch_bounds__(kNT, 3) hsa_tail_kernel(const HsaArgs a) {
                     dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], 1);
                     if (h == lp) mine = dot[h];
                 }
-                if (j < nt && lp < G) sc[(size_t)lp * a.score_stride + j0 + j] = mine * a.inv_sqrt_d;
+                if (j < n && lp < G) sc[(size_t)lp * a.score_stride + j] = mine * a.inv_sqrt_d;
             }
-        } else {
-            // ---- pass C: p * v for the tokens in this V stage ----
-            const int j0 = (s - nA) * TS, nt = min(TS, n - j0);
-            for (int j = cg; j < nt; j += NGC) {
-                const uint32_t vw = *reinterpret_cast<const uint32_t*>(st3 + (size_t)j * RB + (size_t)dw * 4);
-                float vf[EW];
-                if constexpr (EW == 2) {
-                    vf[0] = __uint_as_float(vw << 16);
-                    vf[1] = __uint_as_float(vw & 0xffff0000u);
-                } else {
-                    vf[0] = __uint_as_float(vw);
+        }
+    }
+    __syncthreads();
+    // ---- pass B: softmax statistics over the n scores per head ----
+    {
+        float m[MAXG];
+#pragma unroll
+        for (int h = 0; h < MAXG; ++h) m[h] = -INFINITY;
+        for (int i = tid; i < n; i += kNT)
+#pragma unroll
+            for (int h = 0; h < MAXG; ++h)
+                if (h < G) m[h] = fmaxf(m[h], sc[(size_t)h * a.score_stride + i]);
+#pragma unroll
+        for (int h = 0; h < MAXG; ++h) {
+            float v = m[h];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+            if (lane == 0) part_[h][warp] = v;
+        }
+        __syncthreads();
+        if (tid < G) {
+            float v = -INFINITY;
+            for (int wi = 0; wi < kNT / 32; ++wi) v = fmaxf(v, part_[tid][wi]);
+            hmax[tid] = v;
+        }
+        __syncthreads();
+        float ssum[MAXG];
+#pragma unroll
+        for (int h = 0; h < MAXG; ++h) ssum[h] = 0.0f;
+        for (int i = tid; i < n; i += kNT)
+#pragma unroll
+            for (int h = 0; h < MAXG; ++h)
+                if (h < G) {
+                    const float p = __expf(sc[(size_t)h * a.score_stride + i] - hmax[h]);
+                    sc[(size_t)h * a.score_stride + i] = p;
+                    ssum[h] += p;
                 }
+#pragma unroll
+        for (int h = 0; h < MAXG; ++h) {
+            float v = ssum[h];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0) part_[h][warp] = v;
+        }
+        __syncthreads();
+        if (tid < G) {
+            float v = 0.0f;
+            for (int wi = 0; wi < kNT / 32; ++wi) v += part_[tid][wi];
+            hinv[tid] = 1.0f / v;
+        }
+        __syncthreads();
+    }
+    // ---- pass C: p * v ----
+    const int vi = tid % CPR, cg = tid / CPR;
+    float acc[MAXG][EPV];
+#pragma unroll
+    for (int h = 0; h < MAXG; ++h)
+#pragma unroll
+        for (int e = 0; e < EPV; ++e) acc[h][e] = 0.0f;
+    for (int j0 = cg; j0 < n; j0 += NGC * UC) {
+        uint4 vw[UC];
+#pragma unroll
+        for (int u = 0; u < UC; ++u) {
+            const int j = j0 + u * NGC;
+            if (j < n) vw[u] = __ldg(reinterpret_cast<const uint4*>(Vu + (size_t)sel[j] * RB) + vi);
+        }
+#pragma unroll
+        for (int u = 0; u < UC; ++u) {
+            const int j = j0 + u * NGC;
+            if (j < n) {
+                float vf[EPV];
+                vec_to_f<T>(vw[u], vf);
 #pragma unroll
                 for (int h = 0; h < MAXG; ++h) {
                     if (h < G) {
-                        const float p = sc[(size_t)h * a.score_stride + j0 + j];
+                        const float p = sc[(size_t)h * a.score_stride + j];
 #pragma unroll
-                        for (int e = 0; e < EW; ++e) accv[h][e] = fmaf(p, vf[e], accv[h][e]);
+                        for (int e = 0; e < EPV; ++e) acc[h][e] = fmaf(p, vf[e], acc[h][e]);
                     }
                 }
             }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty3[slot]);
-        if (warp == 0 && s >= 1 && s - 1 + kNStageT < nS) {
-            const int sp = s - 1;
-            if (mbar_wait_bounded(&empty3[sp % kNStageT], (uint32_t)((sp / kNStageT) & 1), a.err)) {
-                fence_proxy_async();
-                issue3(sp + kNStageT);
-            } else {
-                ok3 = false;  // the consumers' wait on the unfilled slot runs out as well
-            }
-        }
     }
-    if (!ok3) s_abort = 1;
-    __syncthreads();
-    if (s_abort) return;
-    // merge the NGC token groups: red[group][head][D]
-    float* red = reinterpret_cast<float*>(ring);
+    // merge the NGC token groups in r0 (the staged logits are no longer needed)
+    float* red = r0;  // [NGC][MAXG][D]
 #pragma unroll
     for (int h = 0; h < MAXG; ++h)
         if (h < G)
 #pragma unroll
-            for (int e = 0; e < EW; ++e) red[((size_t)cg * MAXG + h) * D + dw * EW + e] = accv[h][e];
+            for (int e = 0; e < EPV; ++e) red[((size_t)cg * MAXG + h) * D + vi * EPV + e] = acc[h][e];
     __syncthreads();
     float* Ob = a.O + (size_t)b * a.H * D + (size_t)hk * G * D;
     for (int e = tid; e < G * D; e += kNT) {
@@ -712,8 +701,6 @@ int num_sms() {
 
 template <typename T, int D, int MAXG>
 int launch_t(HsaArgs a, int batch, cudaStream_t st) {
-    constexpr int NGC = kNT / (int)(D * sizeof(T) / 4);
-    static_assert((size_t)NGC * MAXG * D * sizeof(float) <= (size_t)kTailRing, "tail merge buffer");
     if (a.nchunks > 0) {
         const int sr_max = kStageBytes / (int)(D * sizeof(T));
         if (a.C <= sr_max) {
@@ -740,10 +727,15 @@ int launch_t(HsaArgs a, int batch, cudaStream_t st) {
         fs<<<dim3(a.splits, a.head_count, batch), kNT, smem_s, st>>>(a);
         if (cudaGetLastError() != cudaSuccess) return RKV_ERR_CUDA;
     }
+    // tail shared memory: [barrier][r0: staged logits / merge buffer][indices][scores]
+    constexpr int NGC = kNT / (int)(D * sizeof(T) / 16);
+    const size_t merge = (size_t)NGC * MAXG * D * sizeof(float);
+    const size_t logits = (size_t)a.G * a.nch_pad * sizeof(float);
     const size_t lists = (size_t)a.score_stride * 4 * (1 + a.G);
-    a.tail_smem_lists = lists <= (size_t)kTailListMax ? 1 : 0;
-    const size_t smem_t = (size_t)kTailRing + 128 + (a.tail_smem_lists ? lists : 0);
-    auto ft = hsa_tail_kernel<T, D, MAXG>;
+    const bool smem_path = logits + lists <= (size_t)kTailSmemMax;
+    a.tail_r0_bytes = (int)align_up(smem_path && logits > merge ? logits : merge, 16);
+    const size_t smem_t = 128 + (size_t)a.tail_r0_bytes + (smem_path ? lists : 0);
+    auto ft = smem_path ? hsa_tail_kernel<T, D, MAXG, true> : hsa_tail_kernel<T, D, MAXG, false>;
     if (cudaFuncSetAttribute(ft, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_t) != cudaSuccess)
         return RKV_ERR_CUDA;
     ft<<<dim3(a.head_count, batch), kNT, smem_t, st>>>(a);
@@ -801,8 +793,9 @@ HsaShape hsa_shape(const rkv_config& c, int len_k, int recent_window, int batch,
     s.nchunks = (s.final_k > 0 && s.final_k < s.Lc) ? (s.Lc + s.C - 1) / s.C : 0;
     s.sel_cap = (s.final_k > 0 ? s.final_k : 0) + s.w;
     size_t off = kWorkspaceHeader;
+    s.nch_pad = (s.nchunks + 3) / 4 * 4;  // 16-byte rows, so a unit's logits are one aligned block
     s.off_logits = off;
-    off = align_up(off + (size_t)batch * head_count * s.G * (size_t)s.nchunks * sizeof(float), kWorkspaceAlign);
+    off = align_up(off + (size_t)batch * head_count * s.G * (size_t)s.nch_pad * sizeof(float), kWorkspaceAlign);
     s.off_sel = off;
     off = align_up(off + (size_t)batch * head_count * (size_t)(s.sel_cap > 0 ? s.sel_cap : 1) * sizeof(int),
                    kWorkspaceAlign);

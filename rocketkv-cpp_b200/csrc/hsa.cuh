@@ -32,11 +32,12 @@ struct HsaArgs {
     int pages_per_split;  // pages each scan CTA covers
     int stage_rows;       // rows per scan stage
     int carry_mode;       // a page spans more than one scan stage
-    int tail_smem_lists;  // the tail keeps selected indices and scores in shared memory
+    int tail_r0_bytes;    // tail shared memory for staged logits / the merge buffer
+    int nch_pad;          // row stride of the page logits (nchunks rounded up to 4)
 };
 
 struct HsaShape {
-    int G, C, r, w, Lc, final_k, nchunks, sel_cap;
+    int G, C, r, w, Lc, final_k, nchunks, nch_pad, sel_cap;
     size_t off_logits, off_sel, off_scores, ws_bytes;
 };
 

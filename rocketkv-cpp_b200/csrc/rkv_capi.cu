@@ -408,6 +408,7 @@ int rkv_hsa_decode(const void* Q, const void* K, const void* V, int dtype, int l
     a.Lc = s.Lc;
     a.final_k = s.final_k;
     a.nchunks = s.nchunks;
+    a.nch_pad = s.nch_pad;
     a.head_begin = head_begin;
     a.head_count = head_count;
     a.inv_sqrt_d = 1.0f / sqrtf((float)cfg->dim_head);
