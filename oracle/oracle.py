@@ -110,7 +110,7 @@ def lib() -> ctypes.CDLL:
                                                ctypes.POINTER(RocketConfigC), _I32P]
         L.rkvo_hsa_decode.argtypes = [_F32P, _F32P, _F32P, ctypes.c_int, ctypes.c_int,
                                       ctypes.POINTER(RocketConfigC), _F32P, _I32P,
-                                      ctypes.c_int, _I32P]
+                                      ctypes.c_int, _I32P, ctypes.c_int]
         _lib = L
     return _lib
 
@@ -164,8 +164,10 @@ def evict_select_pooled(pooled: np.ndarray, len_q: int, len_k: int, cfg: Config)
     return out[:n].copy()
 
 
-def hsa_decode(Q, K, V, len_k: int, cfg: Config, recent_window: int = 0):
-    """Stage 2 restated.  Returns (O [H, D], list of per-KV-head selected indices)."""
+def hsa_decode(Q, K, V, len_k: int, cfg: Config, recent_window: int = 0, kv_bytes: int = 2):
+    """Stage 2 restated.  Returns (O [H, D], list of per-KV-head selected indices).
+    kv_bytes: element size of K in the GPU run being checked (2 bf16, 4 fp32);
+    it fixes the page-logit summation order."""
     Q = np.ascontiguousarray(Q, np.float32)
     K = np.ascontiguousarray(K, np.float32)
     V = np.ascontiguousarray(V, np.float32)
@@ -174,8 +176,10 @@ def hsa_decode(Q, K, V, len_k: int, cfg: Config, recent_window: int = 0):
     sel = np.zeros((cfg.num_heads_kv, stride), np.int32)
     nsel = np.zeros(cfg.num_heads_kv, np.int32)
     c = cfg.c()
-    lib().rkvo_hsa_decode(_fp(Q), _fp(K), _fp(V), len_k, recent_window, ctypes.byref(c),
-                          _fp(O), _ip(sel), stride, _ip(nsel))
+    rc = lib().rkvo_hsa_decode(_fp(Q), _fp(K), _fp(V), len_k, recent_window, ctypes.byref(c),
+                               _fp(O), _ip(sel), stride, _ip(nsel), kv_bytes)
+    if rc != 0:
+        raise ValueError(f"unsupported stage-2 shape: dim_head {cfg.dim_head}, kv_bytes {kv_bytes}")
     return O, [sel[h, :nsel[h]].copy() for h in range(cfg.num_heads_kv)]
 
 

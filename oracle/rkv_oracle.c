@@ -219,23 +219,42 @@ static float canonical_sum256(const float* v, int n) {
 }
 
 /* Approximate page logit numerator sum_i q[R[i]] * P[i] (rocket.cpp:281-286),
- * in the fixed order the GPU uses: 8 fused multiply-add chains over the list
- * positions i = j, j+8, j+16, ... (j = 0..7, ascending), combined as
- * ((p0+p4)+(p2+p6)) + ((p1+p5)+(p3+p7)). */
-static float chunk_dot(const float* q, const int* R, const float* P, int nr) {
-    float p[8];
-    for (int j = 0; j < 8; ++j) {
-        float a = 0.0f;
-        for (int i = j; i < nr; i += 8) a = fmaf(q[R[i]], P[i], a);
-        p[j] = a;
+ * in the fixed order the GPU uses.  The D dimensions form chunks of cd (16
+ * bytes of K: 8 two-byte or 4 four-byte elements); "lane" j = 0..3 owns the
+ * chunks c = j + 4 i, i = 0 .. D / cd / 4 - 1.  Per chunk: one fused
+ * multiply-add chain over its selected even dimensions and one over its
+ * selected odd dimensions, ascending, value = even + odd.  The lane adds its
+ * chunk values pairwise (s0+s1, s2+s3, ..., then pairs of those, ...), and the
+ * four lanes are added as (l0 + l2) + (l1 + l3). */
+static float chunk_dot(const float* q, const int* R, const float* P, int nr, int D, int cd) {
+    float pd[RKVO_MAX_D];
+    unsigned char on[RKVO_MAX_D];
+    for (int d = 0; d < D; ++d) on[d] = 0;
+    for (int i = 0; i < nr; ++i) { on[R[i]] = 1; pd[R[i]] = P[i]; }
+    const int nsl = D / cd / 4;
+    float l[4];
+    for (int j = 0; j < 4; ++j) {
+        float sv[RKVO_MAX_D / 16];
+        for (int i = 0; i < nsl; ++i) {
+            const int c = j + 4 * i;
+            float ev = 0.0f, od = 0.0f;
+            for (int e = 0; e < cd; e += 2) {
+                const int d = c * cd + e;
+                if (on[d]) ev = fmaf(q[d], pd[d], ev);
+                if (on[d + 1]) od = fmaf(q[d + 1], pd[d + 1], od);
+            }
+            sv[i] = ev + od;
+        }
+        for (int w = 1; w < nsl; w *= 2)
+            for (int i = 0; i < nsl; i += 2 * w) sv[i] = sv[i] + sv[i + w];
+        l[j] = sv[0];
     }
-    const float t0 = p[0] + p[4], t1 = p[1] + p[5], t2 = p[2] + p[6], t3 = p[3] + p[7];
-    return (t0 + t2) + (t1 + t3);
+    return (l[0] + l[2]) + (l[1] + l[3]);
 }
 
 int rkvo_hsa_decode(const float* Q, const float* K, const float* V, int len_k,
                     int recent_window, const rkvo_config* cfg, float* O,
-                    int* sel_out, int sel_stride, int* n_sel) {
+                    int* sel_out, int sel_stride, int* n_sel, int kv_bytes) {
     const int H = cfg->num_heads, HK = cfg->num_heads_kv, D = cfg->dim_head;
     const int G = imax(1, H / HK);                                          /* :175 */
     const int C = (cfg->chunk_size > 0) ? cfg->chunk_size                   /* :177-178 */
@@ -246,6 +265,7 @@ int rkvo_hsa_decode(const float* Q, const float* K, const float* V, int len_k,
     const int w = imax(0, imin(recent_window, len_k));
     const int Lc = len_k - w;                 /* tokens eligible for the top-k */
     const int final_k = imin(cfg->topk_decode, Lc);                         /* :184 */
+    if (D <= 0 || D > RKVO_MAX_D || D % 64 != 0 || (kv_bytes != 2 && kv_bytes != 4)) return -1;
     memset(O, 0, sizeof(float) * (size_t)H * D);                            /* :185 */
     if (n_sel) for (int h = 0; h < HK; ++h) n_sel[h] = 0;
     if (len_k <= 0) return 0;                                               /* :186 */
@@ -322,7 +342,7 @@ int rkvo_hsa_decode(const float* Q, const float* K, const float* V, int len_k,
                     }
                 }
                 for (int h = 0; h < G; ++h)
-                    logit[(size_t)h * nchunks + c] = chunk_dot(qg + (size_t)h * D, R, P, nr) / cscale[h];
+                    logit[(size_t)h * nchunks + c] = chunk_dot(qg + (size_t)h * D, R, P, nr, D, 16 / kv_bytes) / cscale[h];
             }
             /* per-head softmax over chunks (:291-309), then the group sum (:311-323) */
             for (int c = 0; c < nchunks; ++c) gp[c] = 0.0f;

@@ -17,8 +17,9 @@
  *     are unspecified);
  *   - stage 2 lists the top-r query dimensions in ascending order (rocket.cpp
  *     sums over them in std::nth_element's output order), ties to the lower
- *     dimension; it forms each approximate page logit with 8 fused
- *     multiply-add chains combined in a fixed tree, uses rkvo_expf for the
+ *     dimension; it forms each approximate page logit with 16 fused
+ *     multiply-add chains (by 8-dimension group mod 8 and by dimension
+ *     parity) combined in a fixed tree, uses rkvo_expf for the
  *     page softmax and sums that softmax in a fixed 256-way interleaved
  *     order -- the float operations the GPU selection performs, so its
  *     selected indices reproduce this oracle's bit for bit;
@@ -66,13 +67,19 @@ int rkvo_evict_pool_heads(const float* Q, const float* K, int len_q, int len_k,
 int rkvo_evict_select_pooled(const float* pooled, int len_q, int len_k,
                              const rkvo_config* cfg, int* kept_out);
 
+/* Largest dim_head of the stage-2 restatement (and of the GPU kernels). */
+#define RKVO_MAX_D 256
+
 /* Stage 2 (rocket.cpp:171-382), canonical order, optional recent window.
  * O: [num_heads][dim_head] (zeroed first).  sel_out (nullable):
  * [num_heads_kv][sel_stride] ascending token indices; n_sel (nullable): per
- * KV head count.  Returns 0. */
+ * KV head count.  kv_bytes: the element size of K on the GPU (2 for bf16, 4
+ * for fp32), which fixes the page-logit summation order (16-byte chunks);
+ * dim_head must be a multiple of 64 and at most RKVO_MAX_D.  Returns 0, or
+ * -1 for an unsupported dim_head / kv_bytes. */
 int rkvo_hsa_decode(const float* Q, const float* K, const float* V, int len_k,
                     int recent_window, const rkvo_config* cfg, float* O,
-                    int* sel_out, int sel_stride, int* n_sel);
+                    int* sel_out, int sel_stride, int* n_sel, int kv_bytes);
 
 #ifdef __cplusplus
 }

@@ -101,7 +101,7 @@ __global__ void __launch_bounds__(kNT) evict_logits_kernel(EvictArgs a) {
             const int r = rc0 + warp * 4 + i;
             if (r >= a.R) break;  // warp-uniform
             float l[4];
-            float m = -INFINITY;
+            float m = -FLT_MAX;  // rocket.cpp:93 starts the row max here
             float* lrow = a.logits + (row_base + r) * (size_t)a.nk + k0;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -136,7 +136,7 @@ __global__ void __launch_bounds__(kNT) evict_logits_kernel(EvictArgs a) {
     __threadfence();
     for (int r = tid; r < a.R; r += kNT) {
         const float2* ts = a.tstats + (row_base + r) * a.ntiles;
-        float M = -INFINITY;
+        float M = -FLT_MAX;
         for (int t = 0; t < a.ntiles; ++t) M = fmaxf(M, __ldcg(&ts[t].x));
         float S = 0.0f;
         for (int t = 0; t < a.ntiles; ++t) {
@@ -174,7 +174,7 @@ __global__ void __launch_bounds__(kNT) evict_pool_kernel(PoolArgs a) {
     __syncthreads();
     for (int x = tid; x < NA; x += kNT) {
         const int p = x0 + x;
-        float v = -INFINITY;
+        float v = -FLT_MAX;  // rocket.cpp:122: NaN never wins the pool
         if (p >= 0 && p < a.nk) {
             const float* lp = a.logits + row_base * (size_t)a.nk + p;
             float hs = 0.0f;

@@ -6,16 +6,19 @@
 //   0. query statistics of the GQA group: sum_h |q|, the sign of sum_h q, the
 //      top-r dimensions (ties to the lower dimension, listed ascending) and the
 //      per-head variance scale (rocket.cpp:197-250);
-//   1. the K rows of the CTA's page range stream through a 4-stage ring of
-//      16 KB bulk copies (cp.async.bulk, full/empty mbarriers, no multicast;
-//      thread 0 refills a slot once every warp has released it).  Each page
+//   1. the K rows of the CTA's page range stream through a 5-stage ring of
+//      16 KB stages filled by 1-D bulk copies (cp.async.bulk, no multicast;
+//      full/empty mbarriers; thread 0 refills a slot once every warp has
+//      released it; the first stages are issued before phase 0).  Each page
 //      (C rows) gets its sign-chosen max/min on the r dimensions and the
 //      approximate logit per head (rocket.cpp:252-289): eight lanes per page,
-//      lane j runs a fused multiply-add chain over the selected-dimension list
-//      entries j, j+8, ..., a fixed butterfly adds the eight, and an IEEE
-//      division applies the scale.  Logits go to the workspace.
-//      Large batches use one CTA per unit; small ones split a unit's pages
-//      over several CTAs so the grid still covers the GPU.
+//      each owning fixed 8-dimension groups of the row.  The sign choice and
+//      the top-r selection are masks applied to packed bf16 pairs (one
+//      max.bf16x2 per pair and row), the multiply-adds are paired fp32 FMAs
+//      (two chains per lane: even and odd dimensions), a fixed butterfly adds
+//      the eight lanes and an IEEE division applies the scale.  Logits go to
+//      the workspace.  Large batches use one CTA per unit; small ones split a
+//      unit's pages over several CTAs so the grid still covers the GPU.
 //
 // hsa_tail_kernel   grid (KV heads, items)
 //   2. the unit's page logits are staged in shared memory by one bulk copy;
@@ -41,7 +44,7 @@ namespace {
 
 constexpr int kNT = 256;
 constexpr int kStageBytes = 16384;
-constexpr int kNStageS = 4;  // scan ring stages
+constexpr int kMaxScanStages = 8;  // scan ring stages at most (barrier slots)
 constexpr int kTailSmemMax = 96 * 1024;  // staged logits + indices + scores kept in shared memory up to this
 
 template <typename T>
@@ -74,64 +77,221 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Per selected dimension: the group's q values, then the dimension index
-// with the sign of sum_h q in bit 31 (set = negative).
-template <int MAXG>
-struct QPack {
-    static constexpr int kWords = (MAXG + 1 + 3) / 4 * 4;
-};
-
-template <int QW>
-__device__ __forceinline__ void load_qpk(const float* p, float* out) {
-#pragma unroll
-    for (int v = 0; v < QW / 4; ++v) {
-        const float4 x = reinterpret_cast<const float4*>(p)[v];
-        out[4 * v] = x.x;
-        out[4 * v + 1] = x.y;
-        out[4 * v + 2] = x.z;
-        out[4 * v + 3] = x.w;
-    }
-}
+// (d.x, d.y) += (a.x * b.x, a.y * b.y), each lane one fused multiply-add
+// rounded once (the paired fp32 FMA of sm_100).
+__device__ __forceinline__ void ffma2(float2& d, const float2 a, const float2 b) { d = __ffma2_rn(a, b, d); }
 
 // ===========================================================================
 // Scan kernel: phases 0 and 1
 // ===========================================================================
-template <typename T, int D, int MAXG>
-__global__ void __launch_bounds__(kNT, 3) hsa_scan_kernel(const HsaArgs a) {
-    extern __shared__ __align__(128) uint8_t sm[];
-    uint8_t* ring = sm;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sm + kNStageS * kStageBytes);
-    uint64_t* empty = full + kNStageS;
-    float* pst = reinterpret_cast<float*>(sm + kNStageS * kStageBytes + 128);  // carry mode: [2][D + 1]
+// A page is handled by a quad of four lanes.  A K row is a sequence of 16-byte
+// chunks (8 bf16 or 4 fp32 dimensions); lane j of the quad owns the chunks
+// j + 4 i (i < NSL, its slots).  Per chunk and head the lane runs a paired
+// fused multiply-add chain -- one lane of the pair over the chunk's even
+// dimensions, one over its odd ones, ascending -- and the chunk value is
+// even + odd; the lane adds its slot values pairwise ((s0+s1)+(s2+s3)...),
+// and the quad adds its lanes as (l0 + l2) + (l1 + l3).  Odd quads visit
+// their slots in the order i ^ 1, so the two quads that share a shared-memory
+// wavefront read opposite halves of the banks; every chunk has its own chain
+// and the slot tree adds pairs (i, i ^ 1) first, so the order of visits
+// changes no result.  The oracle's chunk_dot restates this order.
+//
+// Per chunk the shared table `tab` holds, in 16-byte units:
+//   q   per head the chunk's s q values (s = -1 where sum_h q < 0; zero on
+//       dimensions outside the top r);
+//   xm  per dimension the sign bit that turns a K value x into s x, so the
+//       page maximum of s x is s times the sign-chosen max / min;
+//   sm  all ones on the top-r dimensions, zero elsewhere;
+// with an odd unit stride so eight consecutive chunks fall in distinct banks.
 
-    constexpr int QW = QPack<MAXG>::kWords;
+constexpr int kScanConsumers = 256;                    // eight consumer warps
+constexpr int kScanThreads = kScanConsumers + 32;      // and one producer warp
+
+// Named barrier 1 over the consumer warps (the producer warp is not in it).
+__device__ __forceinline__ void consumer_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kScanConsumers) : "memory");
+}
+__device__ __forceinline__ bool consumer_any(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, 1, %2, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "n"(kScanConsumers)
+        : "memory");
+    return r != 0;
+}
+
+// Per-word operations on one 16-byte chunk of K (four 32-bit words).
+template <typename T>
+struct Chunk;
+template <>
+struct Chunk<uint16_t> {  // a word holds a bf16 dimension pair
+    static constexpr int NPC = 4;  // dimension pairs per chunk
+    static __device__ __forceinline__ uint32_t wmax(uint32_t a, uint32_t b) {
+        uint32_t d;
+        asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));  // NaN-ignoring, exact
+        return d;
+    }
+    static __device__ __forceinline__ float2 pair(const uint4& m, int k) {
+        const uint32_t w = k == 0 ? m.x : k == 1 ? m.y : k == 2 ? m.z : m.w;
+        return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+    }
+};
+template <>
+struct Chunk<float> {  // a word holds one fp32 dimension
+    static constexpr int NPC = 2;
+    static __device__ __forceinline__ uint32_t wmax(uint32_t a, uint32_t b) {
+        return __float_as_uint(fmaxf(__uint_as_float(a), __uint_as_float(b)));
+    }
+    static __device__ __forceinline__ float2 pair(const uint4& m, int k) {
+        return k == 0 ? make_float2(__uint_as_float(m.x), __uint_as_float(m.y))
+                      : make_float2(__uint_as_float(m.z), __uint_as_float(m.w));
+    }
+};
+
+__device__ __forceinline__ uint4 flip4(const uint4& x, const uint4& xm, const uint4& sm) {
+    return make_uint4((x.x ^ xm.x) & sm.x, (x.y ^ xm.y) & sm.y, (x.z ^ xm.z) & sm.z, (x.w ^ xm.w) & sm.w);
+}
+template <typename T>
+__device__ __forceinline__ uint4 max4(const uint4& a, const uint4& b) {
+    return make_uint4(Chunk<T>::wmax(a.x, b.x), Chunk<T>::wmax(a.y, b.y), Chunk<T>::wmax(a.z, b.z),
+                      Chunk<T>::wmax(a.w, b.w));
+}
+
+// The reference's sign-chosen page extremum starts from -FLT_MAX / +FLT_MAX
+// and skips NaN (rocket.cpp:261-278); in the flipped domain that is a clamp.
+// It only changes a representative that is -inf or NaN, and such a
+// representative on a selected dimension makes the page's sum non-finite
+// (inf and NaN propagate through the chains; 0 * inf is NaN), so pages are
+// first summed unclamped and a warp whose sums are not all finite recomputes
+// its pages with the clamp (CLAMP) -- the same result either way.
+__device__ __forceinline__ float2 clamp_rep(float2 m) {
+    return make_float2(fmaxf(m.x, -FLT_MAX), fmaxf(m.y, -FLT_MAX));
+}
+
+// This lane's value of one page per head.  MODE 0: the page is two rows of the
+// stage; MODE 1: prow >= 1 rows; MODE 2: the representatives are in pst (a
+// page longer than a stage).  Slot i reads chunk bytes at (i even ? rA : rB)
+// + 64 i, its table at (i even ? tA : tB) + 4 i QS, its representatives at
+// (i even ? pA : pB) + 4 i CD.
+template <typename T, int D, int MAXG, int MODE, bool CLAMP>
+__device__ __forceinline__ void lane_page(const uint8_t* rA, const uint8_t* rB, int prow, const uint4* tA,
+                                          const uint4* tB, const float* pA, const float* pB, float (&lv)[MAXG]) {
+    constexpr int ES = (int)sizeof(T), RB = D * ES;
+    constexpr int CD = 16 / ES, NSL = D / CD / 4, NPC = Chunk<T>::NPC;
+    constexpr int QU = (CD / 4) * MAXG, QS = (QU + 2) | 1;
+    float sv[NSL][MAXG];
+#pragma unroll
+    for (int i = 0; i < NSL; ++i) {
+        const uint4* tq = ((i & 1) ? tB : tA) + 4 * i * QS;
+        float2 P[NPC];
+        if constexpr (MODE == 2) {
+            const float* pp = ((i & 1) ? pB : pA) + 4 * i * CD;
+#pragma unroll
+            for (int k = 0; k < NPC; ++k) P[k] = *reinterpret_cast<const float2*>(pp + 2 * k);
+        } else {
+            const uint4 xm = tq[QU], sm = tq[QU + 1];
+            const uint8_t* rp = ((i & 1) ? rB : rA) + 64 * i;
+            uint4 m = flip4(*reinterpret_cast<const uint4*>(rp), xm, sm);
+            if constexpr (MODE == 0) {
+                m = max4<T>(m, flip4(*reinterpret_cast<const uint4*>(rp + RB), xm, sm));
+            } else {
+                for (int rr = 1; rr < prow; ++rr)
+                    m = max4<T>(m, flip4(*reinterpret_cast<const uint4*>(rp + rr * RB), xm, sm));
+            }
+#pragma unroll
+            for (int k = 0; k < NPC; ++k) P[k] = CLAMP ? clamp_rep(Chunk<T>::pair(m, k)) : Chunk<T>::pair(m, k);
+        }
+#pragma unroll
+        for (int h = 0; h < MAXG; ++h) {
+            const float4* qh = reinterpret_cast<const float4*>(tq + h * (CD / 4));
+            float2 acc = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int u = 0; u < CD / 4; ++u) {
+                const float4 qq = qh[u];
+                ffma2(acc, make_float2(qq.x, qq.y), P[2 * u]);
+                ffma2(acc, make_float2(qq.z, qq.w), P[2 * u + 1]);
+            }
+            sv[i][h] = __fadd_rn(acc.x, acc.y);
+        }
+    }
+#pragma unroll
+    for (int w = 1; w < NSL; w *= 2)
+#pragma unroll
+        for (int i = 0; i < NSL; i += 2 * w)
+#pragma unroll
+            for (int h = 0; h < MAXG; ++h) sv[i][h] = __fadd_rn(sv[i][h], sv[i + w][h]);
+#pragma unroll
+    for (int h = 0; h < MAXG; ++h) lv[h] = sv[0][h];
+}
+
+// (l0 + l2) + (l1 + l3) over the quad; every lane of the quad gets the sums.
+template <int MAXG>
+__device__ __forceinline__ void quad_sum(float (&v)[MAXG]) {
+#pragma unroll
+    for (int h = 0; h < MAXG; ++h) {
+        v[h] = __fadd_rn(v[h], __shfl_xor_sync(0xffffffffu, v[h], 2));
+        v[h] = __fadd_rn(v[h], __shfl_xor_sync(0xffffffffu, v[h], 1));
+    }
+}
+
+template <typename T, int D, int MAXG>
+__global__ void __launch_bounds__(kScanThreads, 2) hsa_scan_kernel(const HsaArgs a) {
+    constexpr int ES = (int)sizeof(T);
+    constexpr int RB = D * ES;           // bytes per K row
+    constexpr int CD = 16 / ES;          // dimensions per 16-byte chunk
+    constexpr int NCH = D / CD;          // chunks per row
+    constexpr int QU = (CD / 4) * MAXG;  // q units per chunk
+    constexpr int QS = (QU + 2) | 1;     // table units per chunk (odd)
+    constexpr int PST = D + 4;           // carry-mode row stride of pst (floats)
+
+    extern __shared__ __align__(128) uint8_t ring[];
+    const int NS = a.nstage;
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + (size_t)NS * kStageBytes);
+    uint64_t* empty = full + kMaxScanStages;
+    float* pst = reinterpret_cast<float*>(ring + (size_t)NS * kStageBytes + 16 * kMaxScanStages);  // carry: [2][PST]
+
     __shared__ __align__(16) float qf[MAXG * D];
-    __shared__ __align__(16) float qpk[D * QW];
+    __shared__ __align__(16) uint4 tab[NCH * QS];
     __shared__ float sabs[D], qsum[D];
     __shared__ int Rl[D];
+    __shared__ unsigned char dsel[D];
     __shared__ float sumall[MAXG], cscale[MAXG];
     __shared__ int scan_tmp[33];
 
-    constexpr size_t RB = (size_t)D * sizeof(T);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int split = blockIdx.x, hc = blockIdx.y, b = blockIdx.z, hk = a.head_begin + hc;
     const int G = a.G;
-    const int nch = a.nchunks;
     const int p_beg = split * a.pages_per_split;
-    const int p_end = min(nch, p_beg + a.pages_per_split);
+    const int p_end = min(a.nchunks, p_beg + a.pages_per_split);
     if (p_beg >= p_end) return;  // uniform
     const uint8_t* Qg = a.Q + (size_t)b * a.q_stride + (size_t)hk * G * D * sizeof(T);
     const uint8_t* Ku = a.K + (size_t)b * a.kv_stride + (size_t)hk * a.len_k * RB;
     float* wl = a.wlogits + ((size_t)b * a.head_count + hc) * (size_t)G * a.nch_pad;
+    const int SR = a.stage_rows;
+    const int row_beg = p_beg * a.C, row_end = min(p_end * a.C, a.Lc);
+    const int nst = (row_end - row_beg + SR - 1) / SR;
+    const bool producer = tid == kScanConsumers;
+    auto issue = [&](int s, int slot) {  // the producer lane
+        const int t0 = row_beg + s * SR;
+        const uint32_t bytes = (uint32_t)(min(SR, row_end - t0) * RB);
+        mbar_arrive_expect_tx(&full[slot], bytes);
+        bulk_load(ring + (size_t)slot * kStageBytes, Ku + (size_t)t0 * RB, bytes, &full[slot]);
+    };
 
-    if (tid == 0) {
-        for (int s = 0; s < kNStageS; ++s) {
+    if (producer) {
+        for (int s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kNT / 32);
+            mbar_init(&empty[s], a.wg);  // one arrival per consumer warp of the stage's group
         }
         fence_mbar_init();
+        // the first stages stream in while phase 0 runs
+        for (int s = 0; s < NS && s < nst; ++s) issue(s, s);
     }
-    for (int e = tid; e < G * D; e += kNT) qf[e] = to_f<T>(reinterpret_cast<const T*>(Qg)[e]);
+    for (int e = tid; e < G * D; e += kScanThreads) qf[e] = to_f<T>(reinterpret_cast<const T*>(Qg)[e]);
     __syncthreads();
 
     // ---- phase 0: group query statistics (rocket.cpp:197-250) --------------
@@ -173,6 +333,7 @@ __global__ void __launch_bounds__(kNT, 3) hsa_scan_kernel(const HsaArgs a) {
     int nr;
     const int pos = block_exclusive_scan(flag, scan_tmp, &nr);
     if (flag) Rl[pos] = tid;
+    if (tid < D) dsel[tid] = (unsigned char)flag;
     __syncthreads();
     if (tid < G) {
         float sk;
@@ -184,135 +345,176 @@ __global__ void __launch_bounds__(kNT, 3) hsa_scan_kernel(const HsaArgs a) {
         }
         cscale[tid] = __fsqrt_rn(__fmul_rn((float)D, __fdiv_rn(sk, __fadd_rn(sumall[tid], 1e-9f))));
     }
-    for (int i = tid; i < nr; i += kNT) {
-        const int d = Rl[i];
+    // the chunk table, one dimension pair per thread (rocket.cpp:263: sign >= 0 takes the max)
+    for (int p = tid; p < D / 2; p += kScanThreads) {
+        const int d0 = 2 * p, d1 = d0 + 1, c = d0 / CD, e0 = d0 % CD;
+        const bool s0 = !(qsum[d0] >= 0.0f), s1 = !(qsum[d1] >= 0.0f);
+        const bool n0 = dsel[d0] != 0, n1 = dsel[d1] != 0;
+        uint32_t* xw = reinterpret_cast<uint32_t*>(&tab[c * QS + QU]);
+        uint32_t* sw = reinterpret_cast<uint32_t*>(&tab[c * QS + QU + 1]);
+        if (ES == 2) {
+            xw[e0 / 2] = (s0 ? 0x8000u : 0u) | (s1 ? 0x80000000u : 0u);
+            sw[e0 / 2] = (n0 ? 0xffffu : 0u) | (n1 ? 0xffff0000u : 0u);
+        } else {
+            xw[e0] = s0 ? 0x80000000u : 0u;
+            xw[e0 + 1] = s1 ? 0x80000000u : 0u;
+            sw[e0] = n0 ? 0xffffffffu : 0u;
+            sw[e0 + 1] = n1 ? 0xffffffffu : 0u;
+        }
+        float* qa = reinterpret_cast<float*>(&tab[c * QS]);
 #pragma unroll
-        for (int h = 0; h < MAXG; ++h) qpk[i * QW + h] = h < G ? qf[h * D + d] : 0.0f;
-        qpk[i * QW + QW - 1] = __int_as_float(d | (qsum[d] >= 0.0f ? 0 : (int)0x80000000));
+        for (int h = 0; h < MAXG; ++h) {
+            float v0 = 0.0f, v1 = 0.0f;
+            if (h < G) {
+                const float q0 = qf[h * D + d0], q1 = qf[h * D + d1];
+                v0 = n0 ? (s0 ? -q0 : q0) : 0.0f;
+                v1 = n1 ? (s1 ? -q1 : q1) : 0.0f;
+            }
+            qa[h * CD + e0] = v0;
+            qa[h * CD + e0 + 1] = v1;
+        }
     }
     __syncthreads();
 
     // ---- phase 1: stream K, page representatives, approximate logits ------
-    const int SR = a.stage_rows;
-    const int row_beg = p_beg * a.C, row_end = min(p_end * a.C, a.Lc);
-    const int nst = (row_end - row_beg + SR - 1) / SR;
-    if (tid == 0) {
-        for (int s = 0; s < kNStageS && s < nst; ++s) {
-            const int t0 = row_beg + s * SR;
-            const uint32_t bytes = (uint32_t)(min(SR, row_end - t0) * RB);
-            mbar_arrive_expect_tx(&full[s], bytes);
-            bulk_load(ring + (size_t)s * kStageBytes, Ku + (size_t)t0 * RB, bytes, &full[s]);
+    if (warp == kScanConsumers / 32) {
+        // producer: refill a slot once its consumer warps released it
+        if (lane == 0) {
+            int slot = 0, ph = 0;  // slot of stage s, parity of its previous use
+            for (int s = NS; s < nst; ++s) {
+                if (!mbar_wait_bounded(&empty[slot], (uint32_t)ph, a.err)) break;
+                fence_proxy_async();
+                issue(s, slot);
+                if (++slot == NS) {
+                    slot = 0;
+                    ph ^= 1;
+                }
+            }
         }
+        return;
     }
-    // lane h of each eight divides head h's sum (one division per lane)
-    const int s8 = lane & 7;
-    const float my_scale = s8 < G ? cscale[s8] : 1.0f;
-    float carry_mx = -INFINITY, carry_mn = INFINITY;  // carry mode: running extrema of list entry `tid`
-    for (int s = 0; s < nst; ++s) {
-        const int slot = s % kNStageS;
-        const bool ok = mbar_wait_bounded(&full[slot], (uint32_t)((s / kNStageS) & 1), a.err);
-        // A failed wait is uniform across the block (nobody passes an incomplete
-        // phase); carry mode also decides it with a block vote, as its loop syncs.
-        if (a.carry_mode ? __syncthreads_or(!ok) : !ok) break;
-        const int t0 = row_beg + s * SR, nrows = min(SR, row_end - t0);
-        const T* st = reinterpret_cast<const T*>(ring + (size_t)slot * kStageBytes);
-        const int c_lo = t0 / a.C;
-        const int c_hi = (t0 + nrows == row_end) ? p_end : (t0 + nrows) / a.C;
-        const int ntask = (c_hi - c_lo) * 8;
-        if (a.carry_mode) {
-            if (tid < nr) {
-                const int w = __float_as_int(qpk[tid * QW + QW - 1]);
-                const int d = w & 0x7fffffff;
+    const int WG = a.wg, NGRP = a.ngrp, PPS = a.pps;
+    if (warp >= WG * NGRP) return;  // idle consumer warp (no barrier counts it)
+    const int g = warp / WG, wi = warp - g * WG;
+    const int j = lane & 3, qd = lane >> 2, qpar = qd & 1;
+    const int quad = wi * 8 + qd;  // page within the stage
+    // slot i of this lane reads chunk j + 4 (i ^ qpar)
+    const int offA = 16 * (j + 4 * qpar), offB = 16 * (j - 4 * qpar);
+    const uint4* tA = tab + (j + 4 * qpar) * QS;
+    const uint4* tB = tab + (j - 4 * qpar) * QS;
+    // lane j divides heads j, j + 4, ...
+    float my_scale[(MAXG + 3) / 4];
+#pragma unroll
+    for (int u = 0; u < (MAXG + 3) / 4; ++u) my_scale[u] = (j + 4 * u < G) ? cscale[j + 4 * u] : 1.0f;
+
+    if (!a.carry_mode) {
+        int slot = g, ph = 0;
+        for (int s = g; s < nst; s += NGRP) {
+            const bool ok = mbar_wait_bounded(&full[slot], (uint32_t)ph, a.err);
+            if (!__all_sync(0xffffffffu, ok)) break;  // the producer's wait then runs out too
+            const int c_lo = p_beg + s * PPS;
+            const int npg = min(PPS, p_end - c_lo);
+            const int t0 = row_beg + s * SR;
+            const uint8_t* st = ring + (size_t)slot * kStageBytes;
+            float v[MAXG];
+#pragma unroll
+            for (int h = 0; h < MAXG; ++h) v[h] = 0.0f;
+            const int r0 = quad * a.C;
+            const int prow = min(a.C, row_end - t0 - r0);
+            const uint8_t* rbase = st + (size_t)r0 * RB;
+            if (quad < npg) {
+                if (prow == 2)
+                    lane_page<T, D, MAXG, 0, false>(rbase + offA, rbase + offB, 2, tA, tB, nullptr, nullptr, v);
+                else
+                    lane_page<T, D, MAXG, 1, false>(rbase + offA, rbase + offB, prow, tA, tB, nullptr, nullptr, v);
+            }
+            quad_sum<MAXG>(v);
+            bool finite = true;
+#pragma unroll
+            for (int h = 0; h < MAXG; ++h) finite = finite && fabsf(v[h]) <= FLT_MAX;
+            if (!__all_sync(0xffffffffu, finite)) {
+                // a non-finite representative somewhere in the warp's pages: redo them clamped
+#pragma unroll
+                for (int h = 0; h < MAXG; ++h) v[h] = 0.0f;
+                if (quad < npg)
+                    lane_page<T, D, MAXG, 1, true>(rbase + offA, rbase + offB, prow, tA, tB, nullptr, nullptr, v);
+                quad_sum<MAXG>(v);
+            }
+            if (quad < npg) {
+#pragma unroll
+                for (int u = 0; u < (MAXG + 3) / 4; ++u) {
+                    const int h = j + 4 * u;
+                    float mine = 0.0f;
+#pragma unroll
+                    for (int hh = 0; hh < MAXG; ++hh)
+                        if (hh == h) mine = v[hh];
+                    if (h < G) wl[(size_t)h * a.nch_pad + c_lo + quad] = __fdiv_rn(mine, my_scale[u]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            slot += NGRP;
+            if (slot >= NS) {
+                slot -= NS;
+                ph ^= 1;
+            }
+        }
+    } else {
+        // a page spans several stages: all consumer warps take every stage;
+        // threads tid < D keep the running maximum of s x on dimension tid
+        const bool c_sg = tid < D && !(qsum[tid] >= 0.0f), c_en = tid < D && dsel[tid] != 0;
+        float carry = __int_as_float(0x7fffffff);  // NaN: nothing seen yet
+        int slot = 0, ph = 0;
+        for (int s = 0; s < nst; ++s) {
+            const bool ok = mbar_wait_bounded(&full[slot], (uint32_t)ph, a.err);
+            // uniform decision: the loop below meets named barriers
+            if (consumer_any(!ok)) break;
+            const int t0 = row_beg + s * SR, nrows = min(SR, row_end - t0);
+            const uint8_t* st = ring + (size_t)slot * kStageBytes;
+            const int c_lo = t0 / a.C;
+            const int c_hi = (t0 + nrows == row_end) ? p_end : (t0 + nrows) / a.C;
+            if (tid < D) {
                 for (int rr = 0; rr < nrows; ++rr) {
                     const int t = t0 + rr;
-                    const float x = to_f<T>(st[rr * D + d]);
-                    carry_mx = fmaxf(carry_mx, x);
-                    carry_mn = fminf(carry_mn, x);
+                    float x = to_f<T>(*reinterpret_cast<const T*>(st + (size_t)rr * RB + (size_t)tid * ES));
+                    x = c_en ? (c_sg ? -x : x) : 0.0f;
+                    carry = fmaxf(carry, x);
                     if ((t + 1) % a.C == 0 || t == row_end - 1) {
-                        pst[(t / a.C - c_lo) * (D + 1) + tid] = w < 0 ? carry_mn : carry_mx;
-                        carry_mx = -INFINITY;
-                        carry_mn = INFINITY;
+                        pst[(t / a.C - c_lo) * PST + tid] = fmaxf(carry, -FLT_MAX);
+                        carry = __int_as_float(0x7fffffff);
                     }
                 }
             }
-            __syncthreads();
-        }
-        // tasks (page, slice): slice s8 sums list entries i = s8, s8+8, ...
-        for (int base = warp * 32; base < ntask; base += kNT) {
-            const int task = base + lane;
-            const int cl = task >> 3;
-            float acc[MAXG];
+            consumer_sync();
+            if (warp == 0) {
+                float v[MAXG];
 #pragma unroll
-            for (int h = 0; h < MAXG; ++h) acc[h] = 0.0f;
-            if (task < ntask) {
-                if (a.carry_mode) {
-                    for (int i = s8; i < nr; i += 8) {
-                        const float P = pst[cl * (D + 1) + i];
-                        const float* qp = qpk + i * QW;
+                for (int h = 0; h < MAXG; ++h) v[h] = 0.0f;
+                const int npg = c_hi - c_lo;  // at most two pages end in a stage
+                if (quad < npg) {
+                    const float* pp = pst + quad * PST;
+                    lane_page<T, D, MAXG, 2, true>(nullptr, nullptr, 0, tA, tB, pp + (j + 4 * qpar) * CD,
+                                                   pp + (j - 4 * qpar) * CD, v);
+                }
+                quad_sum<MAXG>(v);
+                if (quad < npg) {
 #pragma unroll
-                        for (int h = 0; h < MAXG; ++h) acc[h] = __fmaf_rn(qp[h], P, acc[h]);
-                    }
-                } else {
-                    // stages start on page boundaries here
-                    const int r0 = cl * a.C, r1 = min(r0 + a.C, nrows);
-                    const T* row0 = st + r0 * D;
-                    if (r1 - r0 == 2) {
-                        // two-row page (the common page size): P = max or min of the pair
-#pragma unroll 4
-                        for (int i = s8; i < nr; i += 8) {
-                            float qv[QW];
-                            load_qpk<QW>(qpk + i * QW, qv);
-                            const int w = __float_as_int(qv[QW - 1]);
-                            const int d = w & 0x7fffffff;
-                            const float x0 = to_f<T>(row0[d]), x1 = to_f<T>(row0[D + d]);
-                            const float P = w < 0 ? fminf(x0, x1) : fmaxf(x0, x1);
+                    for (int u = 0; u < (MAXG + 3) / 4; ++u) {
+                        const int h = j + 4 * u;
+                        float mine = 0.0f;
 #pragma unroll
-                            for (int h = 0; h < MAXG; ++h) acc[h] = __fmaf_rn(qv[h], P, acc[h]);
-                        }
-                    } else {
-                        for (int i = s8; i < nr; i += 8) {
-                            float qv[QW];
-                            load_qpk<QW>(qpk + i * QW, qv);
-                            const int w = __float_as_int(qv[QW - 1]);
-                            const int d = w & 0x7fffffff;
-                            float mx = -INFINITY, mn = INFINITY;
-                            for (int rr = 0; rr < r1 - r0; ++rr) {
-                                const float x = to_f<T>(row0[rr * D + d]);
-                                mx = fmaxf(mx, x);
-                                mn = fminf(mn, x);
-                            }
-                            const float P = w < 0 ? mn : mx;
-#pragma unroll
-                            for (int h = 0; h < MAXG; ++h) acc[h] = __fmaf_rn(qv[h], P, acc[h]);
-                        }
+                        for (int hh = 0; hh < MAXG; ++hh)
+                            if (hh == h) mine = v[hh];
+                        if (h < G) wl[(size_t)h * a.nch_pad + c_lo + quad] = __fdiv_rn(mine, my_scale[u]);
                     }
                 }
             }
-            float mine = acc[0];
-#pragma unroll
-            for (int h = 0; h < MAXG; ++h) {
-                acc[h] = __fadd_rn(acc[h], __shfl_xor_sync(0xffffffffu, acc[h], 4));
-                acc[h] = __fadd_rn(acc[h], __shfl_xor_sync(0xffffffffu, acc[h], 2));
-                acc[h] = __fadd_rn(acc[h], __shfl_xor_sync(0xffffffffu, acc[h], 1));
-                if (h == s8) mine = acc[h];
-            }
-            // every lane of the eight holds the sums; lane h divides head h
-            if (task < ntask && s8 < G) wl[(size_t)s8 * a.nch_pad + c_lo + cl] = __fdiv_rn(mine, my_scale);
-        }
-        if (a.carry_mode) __syncthreads();  // pst reuse
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
-        // producer: refill the slot of the previous stage once every warp released it
-        if (tid == 0 && s >= 1 && s - 1 + kNStageS < nst) {
-            const int sp = s - 1, ps = sp % kNStageS;
-            // On a failed wait there is no refill; the consumers' wait on that
-            // slot then runs out as well, and the error word is already set.
-            if (mbar_wait_bounded(&empty[ps], (uint32_t)((sp / kNStageS) & 1), a.err)) {
-                fence_proxy_async();
-                const int t2 = row_beg + (sp + kNStageS) * SR;
-                const uint32_t bytes = (uint32_t)(min(SR, row_end - t2) * RB);
-                mbar_arrive_expect_tx(&full[ps], bytes);
-                bulk_load(ring + (size_t)ps * kStageBytes, Ku + (size_t)t2 * RB, bytes, &full[ps]);
+            consumer_sync();  // pst reuse
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (++slot == NS) {
+                slot = 0;
+                ph ^= 1;
             }
         }
     }
@@ -378,7 +580,7 @@ __global__ void __launch_bounds__(kNT, 3) hsa_tail_kernel(const HsaArgs a) {
         // ---- phase 2: page softmax per head, group sum, weighted top-k ----
         float m[MAXG];
 #pragma unroll
-        for (int h = 0; h < MAXG; ++h) m[h] = -INFINITY;
+        for (int h = 0; h < MAXG; ++h) m[h] = -FLT_MAX;  // the reference's start value: all -inf gives exp(-inf) = 0
         for (int c = tid; c < nch; c += kNT)
 #pragma unroll
             for (int h = 0; h < MAXG; ++h)
@@ -392,7 +594,7 @@ __global__ void __launch_bounds__(kNT, 3) hsa_tail_kernel(const HsaArgs a) {
         }
         __syncthreads();
         if (tid < G) {
-            float v = -INFINITY;
+            float v = -FLT_MAX;
             for (int wi = 0; wi < kNT / 32; ++wi) v = fmaxf(v, part_[tid][wi]);
             hmax[tid] = v;
         }
@@ -598,7 +800,7 @@ __global__ void __launch_bounds__(kNT, 3) hsa_tail_kernel(const HsaArgs a) {
     {
         float m[MAXG];
 #pragma unroll
-        for (int h = 0; h < MAXG; ++h) m[h] = -INFINITY;
+        for (int h = 0; h < MAXG; ++h) m[h] = -FLT_MAX;  // the reference's start value: all -inf gives exp(-inf) = 0
         for (int i = tid; i < n; i += kNT)
 #pragma unroll
             for (int h = 0; h < MAXG; ++h)
@@ -612,7 +814,7 @@ __global__ void __launch_bounds__(kNT, 3) hsa_tail_kernel(const HsaArgs a) {
         }
         __syncthreads();
         if (tid < G) {
-            float v = -INFINITY;
+            float v = -FLT_MAX;
             for (int wi = 0; wi < kNT / 32; ++wi) v = fmaxf(v, part_[tid][wi]);
             hmax[tid] = v;
         }
@@ -639,7 +841,7 @@ __global__ void __launch_bounds__(kNT, 3) hsa_tail_kernel(const HsaArgs a) {
         if (tid < G) {
             float v = 0.0f;
             for (int wi = 0; wi < kNT / 32; ++wi) v += part_[tid][wi];
-            hinv[tid] = 1.0f / v;
+            hinv[tid] = 1.0f / (v + 1e-9f);  // rocket.cpp:367
         }
         __syncthreads();
     }
@@ -702,29 +904,51 @@ int num_sms() {
 template <typename T, int D, int MAXG>
 int launch_t(HsaArgs a, int batch, cudaStream_t st) {
     if (a.nchunks > 0) {
+        auto fs = hsa_scan_kernel<T, D, MAXG>;
+        cudaFuncAttributes fa;
+        if (cudaFuncGetAttributes(&fa, fs) != cudaSuccess) return RKV_ERR_CUDA;
         const int sr_max = kStageBytes / (int)(D * sizeof(T));
         if (a.C <= sr_max) {
+            // pages per stage: a power of two times 8 (a warp's eight quads), at most 64
             a.carry_mode = 0;
-            a.stage_rows = a.C * (sr_max / a.C);
+            int pps = sr_max / a.C;
+            if (pps >= 8) {
+                int p2 = 1;
+                while (p2 * 2 <= (pps < 64 ? pps : 64) / 8) p2 *= 2;
+                pps = 8 * p2;
+            }
+            a.pps = pps;
+            a.stage_rows = pps * a.C;
+            a.wg = (pps + 7) / 8;
         } else {
             a.carry_mode = 1;
             a.stage_rows = sr_max;
+            a.pps = 0;
+            a.wg = kScanConsumers / 32;
         }
+        // ring depth for two CTAs per SM (113 KB of shared memory each, static part included)
+        const size_t extra = 16 * kMaxScanStages + (a.carry_mode ? (size_t)2 * (D + 4) * 4 : 0);
+        const size_t budget = 113 * 1024, fixed = fa.sharedSizeBytes + extra;
+        int ns = fixed < budget ? (int)((budget - fixed) / kStageBytes) : 0;
+        if (ns > 6) ns = 6;
+        if (ns < 3) ns = 3;
+        a.nstage = ns;
+        a.ngrp = a.carry_mode ? 1 : (kScanConsumers / 32) / a.wg;
+        if (a.ngrp > ns - 1) a.ngrp = ns - 1;
         // enough scan CTAs to cover the GPU; every split keeps at least 4 stages of pages
         const long long units = (long long)batch * a.head_count;
-        const long long want = 3LL * num_sms();
+        const long long want = 2LL * num_sms();
         int splits = units >= want ? 1 : (int)((want + units - 1) / units);
-        const int min_pages = a.carry_mode ? 1 : 4 * (a.stage_rows / a.C);
+        const int min_pages = a.carry_mode ? 1 : 4 * a.pps;
         const int max_splits = (a.nchunks + min_pages - 1) / min_pages;
         if (splits > max_splits) splits = max_splits;
         if (splits < 1) splits = 1;
         a.pages_per_split = (a.nchunks + splits - 1) / splits;
         a.splits = (a.nchunks + a.pages_per_split - 1) / a.pages_per_split;
-        const size_t smem_s = (size_t)kNStageS * kStageBytes + 128 + (a.carry_mode ? (size_t)2 * (D + 1) * 4 : 0);
-        auto fs = hsa_scan_kernel<T, D, MAXG>;
+        const size_t smem_s = (size_t)ns * kStageBytes + extra;
         if (cudaFuncSetAttribute(fs, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_s) != cudaSuccess)
             return RKV_ERR_CUDA;
-        fs<<<dim3(a.splits, a.head_count, batch), kNT, smem_s, st>>>(a);
+        fs<<<dim3(a.splits, a.head_count, batch), kScanThreads, smem_s, st>>>(a);
         if (cudaGetLastError() != cudaSuccess) return RKV_ERR_CUDA;
     }
     // tail shared memory: [barrier][r0: staged logits / merge buffer][indices][scores]

@@ -32,6 +32,10 @@ struct HsaArgs {
     int pages_per_split;  // pages each scan CTA covers
     int stage_rows;       // rows per scan stage
     int carry_mode;       // a page spans more than one scan stage
+    int pps;              // pages per scan stage (not carry mode)
+    int wg;               // consumer warps per stage (a group)
+    int ngrp;             // groups, taking stages in turn
+    int nstage;           // scan ring stages
     int tail_r0_bytes;    // tail shared memory for staged logits / the merge buffer
     int nch_pad;          // row stride of the page logits (nchunks rounded up to 4)
 };

@@ -127,6 +127,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// As mbar_try_wait, but the thread may be suspended up to ~100 us waiting for
+// the phase.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(100000u)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait for phase `parity` of `bar`.  Returns false (and records
 // RKV_ERR_DEVICE_TIMEOUT in *err) if the clock budget runs out.
 // Backs off with a short sleep between polls so waiting warps leave the
@@ -134,10 +148,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
-    unsigned ns = 32;
-    while (!mbar_try_wait(bar, parity)) {
-        __nanosleep(ns);
-        if (ns < 256) ns <<= 1;
+    // try_wait with a suspend-time hint parks the thread until the phase
+    // completes (woken then, not after a sleep) or the hint runs out
+    while (!mbar_try_wait_suspend(bar, parity)) {
         if (clock64() - t0 > kWaitCycles) {
             atomicExch(err, (int)RKV_ERR_DEVICE_TIMEOUT);
             return false;

@@ -35,8 +35,8 @@ def run_gpu(qs, Ks, Vs, L, cfg, device, bf16=True, w=0, head_begin=0, head_count
     return d.O.cpu().numpy(), d.sel.cpu().numpy(), d.n_sel.cpu().numpy()
 
 
-def check_against_oracle(q, K, V, L, cfg, Og, sel, nsel, w=0, heads=None):
-    Oo, so = O.hsa_decode(q, K, V, L, cfg, recent_window=w)
+def check_against_oracle(q, K, V, L, cfg, Og, sel, nsel, w=0, heads=None, bf16=True):
+    Oo, so = O.hsa_decode(q, K, V, L, cfg, recent_window=w, kv_bytes=2 if bf16 else 4)
     G = max(1, cfg.num_heads // cfg.num_heads_kv)
     heads = range(cfg.num_heads_kv) if heads is None else heads
     for i, h in enumerate(heads):
@@ -52,7 +52,7 @@ def test_stage2_cases(name, cuda):
     q, K, V = cases.stage2_build(p)
     cfg = cases.stage2_config(p)
     Og, sel, nsel = run_gpu(q[None], K[None], V[None], p["L"], cfg, cuda, bf16=p["bf16"])
-    check_against_oracle(q, K, V, p["L"], cfg, Og[0], sel[0], nsel[0])
+    check_against_oracle(q, K, V, p["L"], cfg, Og[0], sel[0], nsel[0], bf16=p["bf16"])
     np.testing.assert_allclose(Og[0], GOLD[f"{name}/O"], rtol=RTOL, atol=ATOL)
 
 
@@ -62,7 +62,7 @@ def test_stage2_recent_window(name, w, cuda):
     q, K, V = cases.stage2_build(p)
     cfg = cases.stage2_config(p)
     Og, sel, nsel = run_gpu(q[None], K[None], V[None], p["L"], cfg, cuda, bf16=p["bf16"], w=w)
-    check_against_oracle(q, K, V, p["L"], cfg, Og[0], sel[0], nsel[0], w=w)
+    check_against_oracle(q, K, V, p["L"], cfg, Og[0], sel[0], nsel[0], w=w, bf16=p["bf16"])
     for h in range(cfg.num_heads_kv):
         assert set(range(p["L"] - w, p["L"])) <= set(sel[0, h, : nsel[0, h]].tolist())
 
@@ -106,6 +106,35 @@ def test_stage2_edges(L, k, C, r, cuda):
     for w in (0, 3):
         Og, sel, nsel = run_gpu(q[None], K[None], V[None], L, cfg, cuda, w=w)
         check_against_oracle(q, K, V, L, cfg, Og[0], sel[0], nsel[0], w=w)
+
+
+@pytest.mark.parametrize("bf16,C", [(True, 2), (True, 3), (False, 2), (True, 65)])
+def test_stage2_nonfinite_keys(bf16, C, cuda):
+    """Pages whose representative the reference clamps (rocket.cpp:261-278:
+    the max starts at -FLT_MAX, the min at +FLT_MAX, NaN never wins): all rows
+    NaN or all rows infinite on a selected dimension, a single NaN row, and
+    NaN / inf on dimensions outside the top r.  Selected indices must equal the
+    oracle's; O is compared with NaN == NaN."""
+    L, r = 601, 40
+    cfg = O.Config(num_heads=6, num_heads_kv=2, dim_head=128, topk_decode=64, chunk_size=C, r_dim=r)
+    q, K, V = rkvgen.stage2_inputs(4242 + C, 6, 2, 128, L)
+    q = rkvgen.bf16_round(q * np.float32(0.05))  # keeps q * FLT_MAX finite
+    K = K.copy()
+    for hk in range(2):
+        qg = q[hk * 3:(hk + 1) * 3]
+        sabs = np.abs(qg).sum(0)
+        top = sorted(range(128), key=lambda d: (-sabs[d], d))
+        sd, ud = top[:r], top[r:]
+        pos = qg.sum(0) >= 0
+        rows = lambda p: slice(p * C, min(p * C + C, L))
+        K[hk, rows(2), sd[0]] = np.nan                                  # all NaN
+        K[hk, rows(4), sd[1]] = -np.inf if pos[sd[1]] else np.inf       # clamped to -/+FLT_MAX
+        K[hk, 6 * C, sd[2]] = np.nan                                    # one NaN row
+        K[hk, rows(7), ud[0]] = np.nan                                  # outside the top r
+        K[hk, 8 * C, ud[1]] = np.inf
+        K[hk, 8 * C, ud[2]] = -np.inf
+    Og, sel, nsel = run_gpu(q[None], K[None], V[None], L, cfg, cuda, bf16=bf16)
+    check_against_oracle(q, K, V, L, cfg, Og[0], sel[0], nsel[0], bf16=bf16)
 
 
 def test_stage2_headline_batch_properties(cuda):
