@@ -1,37 +1,38 @@
 // hsa.cu -- stage-2 hybrid sparse decode on sm_100a (rocket.cpp:171-382).
 //
-// Two kernels per call; a unit is one (item, KV head):
+// Three kernels per call; a unit is one (item, KV head):
 //
 // hsa_scan_kernel   grid (splits, KV heads, items)
 //   0. query statistics of the GQA group: sum_h |q|, the sign of sum_h q, the
 //      top-r dimensions (ties to the lower dimension, listed ascending) and the
 //      per-head variance scale (rocket.cpp:197-250);
-//   1. the K rows of the CTA's page range stream through a 5-stage ring of
-//      16 KB stages filled by 1-D bulk copies (cp.async.bulk, no multicast;
-//      full/empty mbarriers; thread 0 refills a slot once every warp has
-//      released it; the first stages are issued before phase 0).  Each page
-//      (C rows) gets its sign-chosen max/min on the r dimensions and the
-//      approximate logit per head (rocket.cpp:252-289): eight lanes per page,
-//      each owning fixed 8-dimension groups of the row.  The sign choice and
-//      the top-r selection are masks applied to packed bf16 pairs (one
+//   1. a producer warp streams the K rows of the CTA's page range through a
+//      ring of 16 KB stages with 1-D bulk copies (cp.async.bulk, no multicast;
+//      full/empty mbarriers; the first stages are issued before phase 0);
+//      groups of consumer warps take the stages in turn.  Each page (C rows)
+//      gets its sign-chosen max/min on the r dimensions and the approximate
+//      logit per head (rocket.cpp:252-289), four lanes per page: the sign
+//      choice and the top-r selection are masks on packed bf16 pairs (one
 //      max.bf16x2 per pair and row), the multiply-adds are paired fp32 FMAs
-//      (two chains per lane: even and odd dimensions), a fixed butterfly adds
-//      the eight lanes and an IEEE division applies the scale.  Logits go to
-//      the workspace.  Large batches use one CTA per unit; small ones split a
-//      unit's pages over several CTAs so the grid still covers the GPU.
+//      with one chain per 16-byte chunk, and an IEEE division applies the
+//      scale.  Logits go to the workspace.  Large batches use one CTA per
+//      unit; small ones split a unit's pages over several CTAs so the grid
+//      still covers the GPU.
 //
-// hsa_tail_kernel   grid (KV heads, items)
-//   2. the unit's page logits are staged in shared memory by one bulk copy;
-//      per-head softmax with the deterministic exp and a fixed 256-way
-//      summation order, the group sum, a weighted radix select of the top final_k tokens by (score desc,
-//      index asc) and a stable compaction to ascending order
-//      (rocket.cpp:291-340), then the recent window;
+// hsa_select_kernel one 128-thread CTA per unit
+//   2. per-head page softmax with the deterministic exp and a fixed 256-way
+//      summation order, the group sum, a weighted radix select of the top
+//      final_k tokens by (score desc, index asc) and a stable compaction to
+//      ascending order (rocket.cpp:291-340), then the recent window; the
+//      logits are staged in shared memory by one bulk copy;
+//
+// hsa_attn_kernel   grid (KV heads, items)
 //   3. exact attention over the selected rows (rocket.cpp:342-378): the
 //      selected K rows and then V rows are gathered with 16-byte read-only
 //      loads, several tokens in flight per thread; scores (eight lanes per
-//      token), per-head softmax statistics, then p * v with one thread per
-//      16-byte V vector.  Logits, selected indices and scores stay in shared
-//      memory when they fit.
+//      token, q in registers, paired FMAs), per-head softmax statistics, then
+//      p * v with one thread per 16-byte V vector.  Selected indices and
+//      scores stay in shared memory when they fit.
 //
 // Phases 0-2 repeat the oracle's float operations one for one, so the selected
 // indices equal the oracle's bit for bit; O is tolerance-checked.
@@ -45,7 +46,8 @@ namespace {
 constexpr int kNT = 256;
 constexpr int kStageBytes = 16384;
 constexpr int kMaxScanStages = 8;  // scan ring stages at most (barrier slots)
-constexpr int kTailSmemMax = 96 * 1024;  // staged logits + indices + scores kept in shared memory up to this
+constexpr int kTailSmemMax = 96 * 1024;  // attention: indices + scores kept in shared memory up to this
+constexpr int kSelSmemMax = 24 * 1024;   // selection: page logits staged in shared memory up to this
 
 template <typename T>
 __device__ __forceinline__ float to_f(T v);
@@ -521,67 +523,59 @@ __global__ void __launch_bounds__(kScanThreads, 2) hsa_scan_kernel(const HsaArgs
 }
 
 // ===========================================================================
-// Tail kernel: phases 2 and 3
+// Select kernel: phase 2, one 128-thread CTA per unit
 // ===========================================================================
-// SMEM: the unit's page logits, selected indices and scores live in shared
-// memory (the common case); otherwise they stay in the workspace.
-template <typename T, int D, int MAXG, bool SMEM>
-__global__ void __launch_bounds__(kNT, 3) hsa_tail_kernel(const HsaArgs a) {
-    extern __shared__ __align__(128) uint8_t sm[];
-    uint64_t* lbar = reinterpret_cast<uint64_t*>(sm);            // logits bulk copy
-    float* r0 = reinterpret_cast<float*>(sm + 128);             // staged logits, later the merge buffer
-    int* sel_s = reinterpret_cast<int*>(sm + 128 + a.tail_r0_bytes);
-    float* sc_s = reinterpret_cast<float*>(sm + 128 + a.tail_r0_bytes + (size_t)a.score_stride * 4);
+// The unit's page logits are staged in shared memory by one bulk copy (SMEM;
+// otherwise they are used in place in the workspace).  Per-head page softmax
+// (rocket.cpp:291-309) with the deterministic exp and the 256-way summation
+// order (thread t holds partials t and t + 128, partial j summing pages j,
+// j + 256, ... ascending; then the halving tree), the group sum
+// (rocket.cpp:311-323), a 4 x 8-bit radix select of the final_k-th token by
+// (score desc, index asc) with pages weighted by their token count, and a
+// stable compaction in ascending token order (rocket.cpp:325-340); then the
+// recent window.  Small CTAs with little shared memory, so several units
+// proceed side by side per SM.
+constexpr int kSelThreads = 128;
 
-    __shared__ __align__(16) float qf[MAXG * D];
-    __shared__ float part[MAXG][kNT];
-    __shared__ float part_[MAXG][kNT / 32];
+template <int MAXG, bool SMEM>
+__global__ void __launch_bounds__(kSelThreads, 8) hsa_select_kernel(const HsaArgs a) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    uint64_t* lbar = reinterpret_cast<uint64_t*>(sm);
+    float* r0 = reinterpret_cast<float*>(sm + 128);  // staged logits [G][NP]
+
+    __shared__ float part[MAXG][kSelThreads];
+    __shared__ float red_[MAXG][kSelThreads / 32];
     __shared__ float hmax[MAXG], hinv[MAXG];
     __shared__ int hist[256], scan_tmp[33];
     __shared__ int s_kk;
     __shared__ uint32_t s_prefix;
 
-    constexpr size_t RB = (size_t)D * sizeof(T);
-    constexpr int EPV = 16 / (int)sizeof(T);  // elements per 16-byte vector
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int hc = blockIdx.x, b = blockIdx.y, hk = a.head_begin + hc;
-    const int G = a.G;
-    const size_t unit = (size_t)b * a.head_count + hc;
-    const uint8_t* Qg = a.Q + (size_t)b * a.q_stride + (size_t)hk * G * D * sizeof(T);
-    const uint8_t* Ku = a.K + (size_t)b * a.kv_stride + (size_t)hk * a.len_k * RB;
-    const uint8_t* Vu = a.V + (size_t)b * a.kv_stride + (size_t)hk * a.len_k * RB;
-    int* sel_g = a.sel + unit * a.sel_stride;
-    int* sel = SMEM ? sel_s : sel_g;
-    float* sc = SMEM ? sc_s : a.wscore + unit * (size_t)G * a.score_stride;  // [G][score_stride]
-    const int nch = a.nchunks, NP = a.nch_pad;
-    float* wg = a.wlogits + unit * (size_t)G * NP;
-    float* wl = SMEM ? r0 : wg;  // [G][NP]
-
-    if (tid == 0) {
-        mbar_init(lbar, 1);
-        fence_mbar_init();
-    }
-    for (int e = tid; e < G * D; e += kNT) qf[e] = to_f<T>(reinterpret_cast<const T*>(Qg)[e]);
-    for (int i = tid; i < 256; i += kNT) hist[i] = 0;
-    __syncthreads();
-    bool ok = true;
-    if (SMEM && nch > 0) {
-        if (tid == 0) {  // the unit's logits are one contiguous, 16-byte aligned block
+    const size_t unit = blockIdx.x;
+    const int G = a.G, nch = a.nchunks, NP = a.nch_pad, C = a.C, Lc = a.Lc;
+    int* sel = a.sel + unit * a.sel_stride;
+    int nfirst;
+    if (nch > 0) {
+        float* wg = a.wlogits + unit * (size_t)G * NP;
+        float* wl = SMEM ? r0 : wg;  // [G][NP]
+        if (SMEM && tid == 0) {
+            mbar_init(lbar, 1);
+            fence_mbar_init();
+            // the unit's logits are one contiguous, 16-byte aligned block
             const uint32_t bytes = (uint32_t)((size_t)G * NP * sizeof(float));
             mbar_arrive_expect_tx(lbar, bytes);
             bulk_load(r0, wg, bytes, lbar);
         }
-        ok = mbar_wait_bounded(lbar, 0, a.err);
-    }
-    if (__syncthreads_or(!ok)) return;  // uniform: nobody passes an incomplete copy
+        for (int i = tid; i < 256; i += kSelThreads) hist[i] = 0;
+        __syncthreads();
+        const bool ok = SMEM ? mbar_wait_bounded(lbar, 0, a.err) : true;
+        if (__syncthreads_or(!ok)) return;  // uniform: nobody passes an incomplete copy
 
-    int nfirst;  // selected tokens from the scored range
-    if (nch > 0) {
-        // ---- phase 2: page softmax per head, group sum, weighted top-k ----
+        // per-head maximum (rocket.cpp:294: starts at -FLT_MAX)
         float m[MAXG];
 #pragma unroll
-        for (int h = 0; h < MAXG; ++h) m[h] = -FLT_MAX;  // the reference's start value: all -inf gives exp(-inf) = 0
-        for (int c = tid; c < nch; c += kNT)
+        for (int h = 0; h < MAXG; ++h) m[h] = -FLT_MAX;
+        for (int c = tid; c < nch; c += kSelThreads)
 #pragma unroll
             for (int h = 0; h < MAXG; ++h)
                 if (h < G) m[h] = fmaxf(m[h], wl[(size_t)h * NP + c]);
@@ -590,51 +584,61 @@ __global__ void __launch_bounds__(kNT, 3) hsa_tail_kernel(const HsaArgs a) {
             float v = m[h];
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-            if (lane == 0) part_[h][warp] = v;
+            if (lane == 0) red_[h][warp] = v;
         }
         __syncthreads();
         if (tid < G) {
             float v = -FLT_MAX;
-            for (int wi = 0; wi < kNT / 32; ++wi) v = fmaxf(v, part_[tid][wi]);
+            for (int wi = 0; wi < kSelThreads / 32; ++wi) v = fmaxf(v, red_[tid][wi]);
             hmax[tid] = v;
         }
         __syncthreads();
-        float ps[MAXG];
+        // p = exp(l - max) over the logits; partials t and t + 128
+        float P0[MAXG], P1[MAXG];
 #pragma unroll
-        for (int h = 0; h < MAXG; ++h) ps[h] = 0.0f;
-        for (int c = tid; c < nch; c += kNT)
+        for (int h = 0; h < MAXG; ++h) P0[h] = P1[h] = 0.0f;
+        for (int base = 0; base < nch; base += 256) {
 #pragma unroll
-            for (int h = 0; h < MAXG; ++h)
-                if (h < G) {
-                    const float e = det_expf(__fsub_rn(wl[(size_t)h * NP + c], hmax[h]));
-                    wl[(size_t)h * NP + c] = e;
-                    ps[h] = __fadd_rn(ps[h], e);
-                }
+            for (int hf = 0; hf < 2; ++hf) {
+                const int c = base + tid + hf * kSelThreads;
+                if (c < nch)
 #pragma unroll
-        for (int h = 0; h < MAXG; ++h) part[h][tid] = ps[h];
-        __syncthreads();
-        // halving tree part[j] += part[j + s], s = 128 ... 1: the first three
-        // steps cross warps (shared memory), the last five run in warp 0.
-        for (int s = kNT / 2; s >= 32; s >>= 1) {
-            if (tid < s)
-#pragma unroll
-                for (int h = 0; h < MAXG; ++h) part[h][tid] = __fadd_rn(part[h][tid], part[h][tid + s]);
-            __syncthreads();
+                    for (int h = 0; h < MAXG; ++h)
+                        if (h < G) {
+                            const float e = det_expf(__fsub_rn(wl[(size_t)h * NP + c], hmax[h]));
+                            wl[(size_t)h * NP + c] = e;
+                            if (hf == 0)
+                                P0[h] = __fadd_rn(P0[h], e);
+                            else
+                                P1[h] = __fadd_rn(P1[h], e);
+                        }
+            }
         }
+        // halving tree: s = 128 in the thread, 64 and 32 in shared memory, 16 ... 1 in warp 0
+#pragma unroll
+        for (int h = 0; h < MAXG; ++h) part[h][tid] = __fadd_rn(P0[h], P1[h]);
+        __syncthreads();
+        if (tid < 64)
+#pragma unroll
+            for (int h = 0; h < MAXG; ++h) part[h][tid] = __fadd_rn(part[h][tid], part[h][tid + 64]);
+        __syncthreads();
         if (warp == 0) {
 #pragma unroll
             for (int h = 0; h < MAXG; ++h) {
-                float v = part[h][lane];
+                float v = __fadd_rn(part[h][lane], part[h][lane + 32]);
 #pragma unroll
                 for (int s = 16; s > 0; s >>= 1) v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, s));
                 if (lane == 0 && h < G) hinv[h] = __fdiv_rn(1.0f, __fadd_rn(v, 1e-9f));
             }
         }
         __syncthreads();
-        uint32_t* keys = reinterpret_cast<uint32_t*>(wl);  // head-0 row, overwritten page by page
-        for (int c = tid; c < nch; c += kNT) {
+        // group score per page as an order-preserving key, over head 0's row
+        uint32_t* keys = reinterpret_cast<uint32_t*>(wl);
+        for (int c = tid; c < nch; c += kSelThreads) {
             float g = 0.0f;
-            for (int h = 0; h < G; ++h) g = __fadd_rn(g, __fmul_rn(wl[(size_t)h * NP + c], hinv[h]));
+#pragma unroll
+            for (int h = 0; h < MAXG; ++h)
+                if (h < G) g = __fadd_rn(g, __fmul_rn(wl[(size_t)h * NP + c], hinv[h]));
             keys[c] = float_key(g);
         }
         if (tid == 0) {
@@ -642,15 +646,14 @@ __global__ void __launch_bounds__(kNT, 3) hsa_tail_kernel(const HsaArgs a) {
             s_kk = a.final_k;
         }
         __syncthreads();
-        // 4 x 8-bit radix select of the final_k-th token (pages weighted by
-        // their token count).  Warp 0 scans the 256 bins from the top digit
-        // down and clears them for the next pass: two barriers per pass.
+        // 4 x 8-bit radix select of the final_k-th token.  Warp 0 scans the
+        // 256 bins from the top digit down and clears them: two barriers a pass.
         uint32_t mask = 0u;
         for (int shift = 24; shift >= 0; shift -= 8) {
             const uint32_t prefix = s_prefix;
-            for (int c = tid; c < nch; c += kNT) {
+            for (int c = tid; c < nch; c += kSelThreads) {
                 const uint32_t k = keys[c];
-                if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], min(a.C, a.Lc - c * a.C));
+                if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], min(C, Lc - c * C));
             }
             __syncthreads();
             if (warp == 0) {
@@ -689,51 +692,91 @@ __global__ void __launch_bounds__(kNT, 3) hsa_tail_kernel(const HsaArgs a) {
         }
         const uint32_t thr = s_prefix;
         const int need = s_kk;
-        // Stable compaction: thread tid owns the contiguous page range
-        // [c_beg, c_end); two block scans give its threshold-tie rank and its
-        // output position, so the selection lands in ascending token order.
-        const int per = (nch + kNT - 1) / kNT;
+        // stable compaction: thread t owns the contiguous page range [c_beg, c_end)
+        const int per = (nch + kSelThreads - 1) / kSelThreads;
         const int c_beg = min(nch, tid * per), c_end = min(nch, c_beg + per);
         int eqw = 0;
         for (int c = c_beg; c < c_end; ++c)
-            if (keys[c] == thr) eqw += min(a.C, a.Lc - c * a.C);
+            if (keys[c] == thr) eqw += min(C, Lc - c * C);
         int tot;
         int eq_rank = block_exclusive_scan(eqw, scan_tmp, &tot);
         int takes = 0;
         for (int c = c_beg, eb = eq_rank; c < c_end; ++c) {
             const uint32_t k = keys[c];
-            const int wt = min(a.C, a.Lc - c * a.C);
-            if (k > thr) takes += wt;
-            else if (k == thr) { takes += max(0, min(wt, need - eb)); eb += wt; }
+            const int wt = min(C, Lc - c * C);
+            if (k > thr) {
+                takes += wt;
+            } else if (k == thr) {
+                takes += max(0, min(wt, need - eb));
+                eb += wt;
+            }
         }
         int pos = block_exclusive_scan(takes, scan_tmp, &tot);
         for (int c = c_beg; c < c_end; ++c) {
             const uint32_t k = keys[c];
-            const int wt = min(a.C, a.Lc - c * a.C);
+            const int wt = min(C, Lc - c * C);
             int take = 0;
-            if (k > thr) take = wt;
-            else if (k == thr) { take = max(0, min(wt, need - eq_rank)); eq_rank += wt; }
-            for (int j = 0; j < take; ++j) sel[pos + j] = c * a.C + j;
+            if (k > thr) {
+                take = wt;
+            } else if (k == thr) {
+                take = max(0, min(wt, need - eq_rank));
+                eq_rank += wt;
+            }
+            for (int j = 0; j < take; ++j) sel[pos + j] = c * C + j;
             pos += take;
         }
         nfirst = a.final_k;
     } else {
-        // No scoring needed: every eligible token (final_k >= Lc) or none.
-        nfirst = a.final_k > 0 ? a.Lc : 0;
-        for (int t = tid; t < nfirst; t += kNT) sel[t] = t;
+        // no scoring needed: every eligible token (final_k >= Lc) or none
+        nfirst = a.final_k > 0 ? Lc : 0;
+        for (int t = tid; t < nfirst; t += kSelThreads) sel[t] = t;
     }
-    for (int t = tid; t < a.w; t += kNT) sel[nfirst + t] = a.Lc + t;
-    const int n = nfirst + a.w;
-    if (tid == 0 && a.n_sel) a.n_sel[unit] = n;
-    __syncthreads();
-    if (SMEM)
-        for (int i = tid; i < n; i += kNT) sel_g[i] = sel_s[i];
+    for (int t = tid; t < a.w; t += kSelThreads) sel[nfirst + t] = Lc + t;
+    if (tid == 0 && a.n_sel) a.n_sel[unit] = nfirst + a.w;
+}
 
-    // ---- phase 3: exact attention over the selected rows -------------------
-    // Gathers are direct 16-byte read-only loads, several tokens in flight per
-    // thread.  Pass A: eight lanes per token form q.k for every head; pass B:
-    // per-head max, p = exp(s - max) and sum(p); pass C: each thread owns one
-    // 16-byte vector of the V row and accumulates p * v per head.
+// ===========================================================================
+// Attention kernel: phase 3
+// ===========================================================================
+// Exact attention over the unit's selected rows (rocket.cpp:342-378).
+// Gathers are direct 16-byte read-only loads, several tokens in flight per
+// thread.  Pass A: eight lanes per token form q.k for every head (paired
+// FMAs, q held in registers); pass B: per-head max, p = exp(s - max) and
+// sum(p); pass C: each thread owns one 16-byte vector of the V row and
+// accumulates p * v per head; the token groups are merged in shared memory.
+// SMEM: the selected indices and scores live in shared memory (the common
+// case); otherwise in the workspace.
+template <typename T, int D, int MAXG, bool SMEM>
+__global__ void __launch_bounds__(kNT, 3) hsa_attn_kernel(const HsaArgs a) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    float* red = reinterpret_cast<float*>(sm);  // merge buffer [NGC][MAXG][D]
+    int* sel_s = reinterpret_cast<int*>(sm + a.tail_r0_bytes);
+    float* sc_s = reinterpret_cast<float*>(sm + a.tail_r0_bytes + (size_t)a.score_stride * 4);
+
+    __shared__ __align__(16) float qf[MAXG * D];
+    __shared__ float part_[MAXG][kNT / 32];
+    __shared__ float hmax[MAXG], hinv[MAXG];
+
+    constexpr size_t RB = (size_t)D * sizeof(T);
+    constexpr int EPV = 16 / (int)sizeof(T);  // elements per 16-byte vector
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int hc = blockIdx.x, b = blockIdx.y, hk = a.head_begin + hc;
+    const int G = a.G;
+    const size_t unit = (size_t)b * a.head_count + hc;
+    const uint8_t* Qg = a.Q + (size_t)b * a.q_stride + (size_t)hk * G * D * sizeof(T);
+    const uint8_t* Ku = a.K + (size_t)b * a.kv_stride + (size_t)hk * a.len_k * RB;
+    const uint8_t* Vu = a.V + (size_t)b * a.kv_stride + (size_t)hk * a.len_k * RB;
+    const int* sel_g = a.sel + unit * a.sel_stride;
+    const int nfirst = a.nchunks > 0 ? a.final_k : (a.final_k > 0 ? a.Lc : 0);
+    const int n = nfirst + a.w;
+    const int* sel = SMEM ? sel_s : sel_g;
+    float* sc = SMEM ? sc_s : a.wscore + unit * (size_t)G * a.score_stride;  // [G][score_stride]
+
+    for (int e = tid; e < G * D; e += kNT) qf[e] = to_f<T>(reinterpret_cast<const T*>(Qg)[e]);
+    if (SMEM)
+        for (int i = tid; i < n; i += kNT) sel_s[i] = sel_g[i];
+    __syncthreads();
+
     constexpr int CPR = (int)RB / 16;  // 16-byte vectors per row
     constexpr int NPART = 8;           // pass-A lanes per token
     constexpr int CPP = CPR / NPART;   // vectors per lane
@@ -741,9 +784,23 @@ __global__ void __launch_bounds__(kNT, 3) hsa_tail_kernel(const HsaArgs a) {
     constexpr int UA = CPP >= 4 ? 1 : 4 / CPP;
     constexpr int NGC = kNT / CPR;     // pass-C token groups
     constexpr int UC = 4;
+    constexpr bool QREG = CPP * EPV * MAXG <= 48;  // the lane's q values fit in registers
     static_assert(CPP >= 1 && NGC >= 1, "row layout");
+    // ---- pass A: scores ----
     {
         const int lp = tid % NPART, tok = tid / NPART;
+        float2 qr[QREG ? CPP * EPV / 2 : 1][MAXG];
+        if constexpr (QREG) {
+#pragma unroll
+            for (int c = 0; c < CPP; ++c)
+#pragma unroll
+                for (int e2 = 0; e2 < EPV / 2; ++e2)
+#pragma unroll
+                    for (int h = 0; h < MAXG; ++h)
+                        qr[c * (EPV / 2) + e2][h] =
+                            h < G ? *reinterpret_cast<const float2*>(qf + h * D + (lp + c * NPART) * EPV + 2 * e2)
+                                  : make_float2(0.0f, 0.0f);
+        }
         for (int j0 = 0; j0 < n; j0 += TPR * UA) {  // uniform trip count
             uint4 kw[UA][CPP];
 #pragma unroll
@@ -758,34 +815,34 @@ __global__ void __launch_bounds__(kNT, 3) hsa_tail_kernel(const HsaArgs a) {
 #pragma unroll
             for (int u = 0; u < UA; ++u) {
                 const int j = j0 + u * TPR + tok;
-                float dot[MAXG];
+                float2 acc[MAXG];
 #pragma unroll
-                for (int h = 0; h < MAXG; ++h) dot[h] = 0.0f;
+                for (int h = 0; h < MAXG; ++h) acc[h] = make_float2(0.0f, 0.0f);
                 if (j < n) {
 #pragma unroll
                     for (int c = 0; c < CPP; ++c) {
                         float kf[EPV];
                         vec_to_f<T>(kw[u][c], kf);
-                        const int ch = lp + c * NPART;
 #pragma unroll
-                        for (int h = 0; h < MAXG; ++h) {
-                            if (h < G) {
-                                const float4* q4 = reinterpret_cast<const float4*>(qf + h * D + ch * EPV);
+                        for (int e2 = 0; e2 < EPV / 2; ++e2) {
+                            const float2 kv = make_float2(kf[2 * e2], kf[2 * e2 + 1]);
 #pragma unroll
-                                for (int e4 = 0; e4 < EPV / 4; ++e4) {
-                                    const float4 q = q4[e4];
-                                    dot[h] = fmaf(q.x, kf[4 * e4], dot[h]);
-                                    dot[h] = fmaf(q.y, kf[4 * e4 + 1], dot[h]);
-                                    dot[h] = fmaf(q.z, kf[4 * e4 + 2], dot[h]);
-                                    dot[h] = fmaf(q.w, kf[4 * e4 + 3], dot[h]);
+                            for (int h = 0; h < MAXG; ++h) {
+                                if constexpr (QREG) {
+                                    ffma2(acc[h], qr[c * (EPV / 2) + e2][h], kv);
+                                } else if (h < G) {
+                                    const float2 q = *reinterpret_cast<const float2*>(
+                                        qf + h * D + (lp + c * NPART) * EPV + 2 * e2);
+                                    ffma2(acc[h], q, kv);
                                 }
                             }
                         }
                     }
                 }
-                float mine = dot[0];
+                float dot[MAXG], mine = 0.0f;
 #pragma unroll
                 for (int h = 0; h < MAXG; ++h) {
+                    dot[h] = acc[h].x + acc[h].y;
                     dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], 4);
                     dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], 2);
                     dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], 1);
@@ -800,7 +857,7 @@ __global__ void __launch_bounds__(kNT, 3) hsa_tail_kernel(const HsaArgs a) {
     {
         float m[MAXG];
 #pragma unroll
-        for (int h = 0; h < MAXG; ++h) m[h] = -FLT_MAX;  // the reference's start value: all -inf gives exp(-inf) = 0
+        for (int h = 0; h < MAXG; ++h) m[h] = -FLT_MAX;  // rocket.cpp:350: all -inf gives exp(-inf) = 0
         for (int i = tid; i < n; i += kNT)
 #pragma unroll
             for (int h = 0; h < MAXG; ++h)
@@ -876,8 +933,7 @@ __global__ void __launch_bounds__(kNT, 3) hsa_tail_kernel(const HsaArgs a) {
             }
         }
     }
-    // merge the NGC token groups in r0 (the staged logits are no longer needed)
-    float* red = r0;  // [NGC][MAXG][D]
+    // merge the NGC token groups
 #pragma unroll
     for (int h = 0; h < MAXG; ++h)
         if (h < G)
@@ -951,15 +1007,24 @@ int launch_t(HsaArgs a, int batch, cudaStream_t st) {
         fs<<<dim3(a.splits, a.head_count, batch), kScanThreads, smem_s, st>>>(a);
         if (cudaGetLastError() != cudaSuccess) return RKV_ERR_CUDA;
     }
-    // tail shared memory: [barrier][r0: staged logits / merge buffer][indices][scores]
+    // phase 2: one CTA per unit; the logits are staged when they fit
+    const int units = batch * a.head_count;
+    const size_t lg = (size_t)a.G * a.nch_pad * sizeof(float);
+    const bool sel_smem = a.nchunks > 0 && lg <= (size_t)kSelSmemMax;
+    const size_t smem_sel = sel_smem ? 128 + lg : 0;
+    auto fsel = sel_smem ? hsa_select_kernel<MAXG, true> : hsa_select_kernel<MAXG, false>;
+    if (cudaFuncSetAttribute(fsel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_sel) != cudaSuccess)
+        return RKV_ERR_CUDA;
+    fsel<<<units, kSelThreads, smem_sel, st>>>(a);
+    if (cudaGetLastError() != cudaSuccess) return RKV_ERR_CUDA;
+    // phase 3 shared memory: [merge buffer][indices][scores]
     constexpr int NGC = kNT / (int)(D * sizeof(T) / 16);
     const size_t merge = (size_t)NGC * MAXG * D * sizeof(float);
-    const size_t logits = (size_t)a.G * a.nch_pad * sizeof(float);
     const size_t lists = (size_t)a.score_stride * 4 * (1 + a.G);
-    const bool smem_path = logits + lists <= (size_t)kTailSmemMax;
-    a.tail_r0_bytes = (int)align_up(smem_path && logits > merge ? logits : merge, 16);
-    const size_t smem_t = 128 + (size_t)a.tail_r0_bytes + (smem_path ? lists : 0);
-    auto ft = smem_path ? hsa_tail_kernel<T, D, MAXG, true> : hsa_tail_kernel<T, D, MAXG, false>;
+    const bool smem_path = lists <= (size_t)kTailSmemMax;
+    a.tail_r0_bytes = (int)align_up(merge, 16);
+    const size_t smem_t = (size_t)a.tail_r0_bytes + (smem_path ? lists : 0);
+    auto ft = smem_path ? hsa_attn_kernel<T, D, MAXG, true> : hsa_attn_kernel<T, D, MAXG, false>;
     if (cudaFuncSetAttribute(ft, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_t) != cudaSuccess)
         return RKV_ERR_CUDA;
     ft<<<dim3(a.head_count, batch), kNT, smem_t, st>>>(a);

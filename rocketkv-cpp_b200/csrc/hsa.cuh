@@ -36,7 +36,7 @@ struct HsaArgs {
     int wg;               // consumer warps per stage (a group)
     int ngrp;             // groups, taking stages in turn
     int nstage;           // scan ring stages
-    int tail_r0_bytes;    // tail shared memory for staged logits / the merge buffer
+    int tail_r0_bytes;    // attention-kernel shared memory for the merge buffer
     int nch_pad;          // row stride of the page logits (nchunks rounded up to 4)
 };
 
