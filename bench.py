@@ -392,11 +392,11 @@ def main():
     units = items * HK
     ub = unit_bytes(cache, p.k, WINDOW)
     achieved = units * ub / (ms / args.steps / 1e3) / 1e9
-    tr = traffic_per_unit("hsa_kernel")
+    tr = traffic_per_unit("rkv_hsa_decode")
     roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
             "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
-            "traffic": (tr * units if tr else None), "algorithmic_bytes_per_launch": units * ub,
-            "kernel": "hsa_kernel<bf16,128,4>"}
+            "traffic": (round(tr * units) if tr else None), "algorithmic_bytes_per_launch": units * ub,
+            "kernel": "rkv_hsa_decode (hsa_scan_kernel + hsa_select_kernel + hsa_attn_kernel)"}
 
     ev_ms, ev_e2e_ms, ev_kernels = time_evict(device, max(args.steps, 5), args.warmup)
     ev_ms = allreduce_max(ev_ms, world)
