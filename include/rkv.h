@@ -52,7 +52,12 @@ typedef enum rkv_dtype {
 /* Stage-1 scoring engine. */
 typedef enum rkv_evict_engine {
     RKV_EVICT_AUTO = 0,   /* the fastest engine built for the inputs          */
-    RKV_EVICT_SIMT = 1    /* fp32 CUDA-core scoring                            */
+    RKV_EVICT_SIMT = 1,   /* fp32 CUDA-core scoring                            */
+    RKV_EVICT_TENSOR = 2  /* tcgen05 tensor-core scoring: fp32 K/Q as three
+                             TF32 products per step, bf16 directly; needs
+                             16-byte aligned rows and a row size that is a
+                             multiple of 32 bytes (else RKV_ERR_UNSUPPORTED);
+                             AUTO takes it whenever it applies               */
 } rkv_evict_engine;
 
 /* Field-for-field image of RocketConfig (rocket.h:18-34). */

@@ -9,7 +9,8 @@
 //       1 / (sum_r + 1e-9) (rocket.cpp:108-113).
 //   evict_pool_kernel    grid (position tiles, KV heads, items)
 //       head score hs[k] = sum_r exp(l[r][k] - M_r) * inv_r in row order
-//       (rocket.cpp:114-116), then max-pool over [k - pad, k + pad] clipped
+//       (rocket.cpp:114-116; the tensor-core engine of evict_mma.cu computes
+//       it there and this kernel reads it), then max-pool over [k - pad, k + pad] clipped
 //       to the sequence (rocket.cpp:120-129) by a doubling sparse table in
 //       shared memory; one pooled row per KV head.
 //   evict_select_kernel  grid (items)
@@ -170,20 +171,25 @@ __global__ void __launch_bounds__(kNT) evict_pool_kernel(PoolArgs a) {
             if (k0 + i < a.nk) out[k0 + i] = -FLT_MAX;
         return;
     }
-    for (int r = tid; r < a.R; r += kNT) rs[r] = a.rstats[row_base + r];
+    if (!a.hs_direct)
+        for (int r = tid; r < a.R; r += kNT) rs[r] = a.rstats[row_base + r];
     __syncthreads();
     for (int x = tid; x < NA; x += kNT) {
         const int p = x0 + x;
         float v = -FLT_MAX;  // rocket.cpp:122: NaN never wins the pool
         if (p >= 0 && p < a.nk) {
-            const float* lp = a.logits + row_base * (size_t)a.nk + p;
-            float hs = 0.0f;
+            if (a.hs_direct) {
+                v = __ldg(a.logits + ((size_t)b * a.head_count + hc) * a.nk + p);
+            } else {
+                const float* lp = a.logits + row_base * (size_t)a.nk + p;
+                float hs = 0.0f;
 #pragma unroll 8
-            for (int r = 0; r < a.R; ++r) {
-                const float e = expf(__ldg(lp + (size_t)r * a.nk) - rs[r].x);
-                hs = __fadd_rn(hs, __fmul_rn(e, rs[r].y));
+                for (int r = 0; r < a.R; ++r) {
+                    const float e = expf(__ldg(lp + (size_t)r * a.nk) - rs[r].x);
+                    hs = __fadd_rn(hs, __fmul_rn(e, rs[r].y));
+                }
+                v = hs;
             }
-            v = hs;
         }
         bufA[x] = v;
     }

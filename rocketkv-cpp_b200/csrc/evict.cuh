@@ -16,16 +16,18 @@ struct EvictArgs {
     int k_head_rows;  // rows per KV head in K (len_k, or nk when compacted)
     int head_begin, head_count;
     float inv_sqrt_d;
-    float* logits;      // [batch][head_count][R][nk]
+    float* logits;      // [batch][head_count][R][nk]; the tensor-core engine keeps head scores [batch][head_count][nk] here
     float2* tstats;     // [batch][head_count][R][ntiles]  (tile max, tile sum)
     float2* rstats;     // [batch][head_count][R]          (row max, 1/(sum+1e-9))
     unsigned* counters; // [batch][head_count]
+    int* err;           // workspace error word (bounded in-kernel waits)
 };
 
 struct PoolArgs {
-    const float* logits;
+    const float* logits;  // logits [batch][head_count][R][nk], or head scores [batch][head_count][nk] (hs_direct)
     const float2* rstats;
     int R, nk, head_count, pad;
+    int hs_direct;
     int pad_eff, log2w;   // filled by the launcher
     float* pooled;  // [batch][head_count][nk]
 };
@@ -48,6 +50,9 @@ struct EvictShape {
 EvictShape evict_shape(const rkv_config& c, int len_q, int len_k, int batch, int head_count);
 int evict_check_supported(const rkv_config& c, int dtype, const EvictShape& s);
 int launch_evict_scores(const EvictArgs& a, int batch, cudaStream_t st);
+// tcgen05 scoring (evict_mma.cu): statistics, then head scores for the pool kernel (hs_direct)
+bool evict_mma_supported(const EvictArgs& a);
+int launch_evict_mma(const EvictArgs& a, int batch, cudaStream_t st);
 int launch_evict_pool(const PoolArgs& a, int batch, cudaStream_t st);
 int launch_evict_select(const SelectArgs& a, int batch, cudaStream_t st);
 int launch_evict_keep_all(int* kept, int kept_stride, int* n_kept, int len_k, int batch, cudaStream_t st);

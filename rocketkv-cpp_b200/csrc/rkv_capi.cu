@@ -122,14 +122,19 @@ EvictArgs make_evict_args(const void* Q, const void* K, int dtype, int len_q, in
     a.tstats = reinterpret_cast<float2*>(ws + s.off_tstats);
     a.rstats = reinterpret_cast<float2*>(ws + s.off_rstats);
     a.counters = reinterpret_cast<unsigned*>(ws + s.off_counters);
+    a.err = reinterpret_cast<int*>(ws);
     return a;
 }
 
 int evict_run(const EvictArgs& a, const rkv_config& c, const EvictShape& s, int batch, uint8_t* ws,
-              float* pooled_out, int* kept, int kept_stride, int* n_kept, cudaStream_t st) {
-    int rc = launch_evict_scores(a, batch, st);
+              float* pooled_out, int* kept, int kept_stride, int* n_kept, int engine, cudaStream_t st) {
+    const bool tensor = engine != RKV_EVICT_SIMT && evict_mma_supported(a);
+    if (engine == RKV_EVICT_TENSOR && !tensor) return RKV_ERR_UNSUPPORTED;
+    if (cudaMemsetAsync(a.err, 0, sizeof(int), st) != cudaSuccess) return RKV_ERR_CUDA;
+    int rc = tensor ? launch_evict_mma(a, batch, st) : launch_evict_scores(a, batch, st);
     if (rc) return rc;
     PoolArgs p{};
+    p.hs_direct = tensor ? 1 : 0;
     p.logits = a.logits;
     p.rstats = a.rstats;
     p.R = s.R;
@@ -246,7 +251,7 @@ int rkv_evict(const void* Q, const void* K, int dtype, int len_q, int len_k, int
               long long q_item_stride, long long k_item_stride, const rkv_config* cfg, int* kept,
               int kept_stride, int* n_kept, void* workspace, size_t workspace_bytes, int engine,
               void* stream) {
-    (void)engine;
+    if (engine < RKV_EVICT_AUTO || engine > RKV_EVICT_TENSOR) return RKV_ERR_INVALID_ARG;
     if (check_cfg(cfg)) return RKV_ERR_INVALID_ARG;
     const EvictShape s = evict_shape(*cfg, len_q, len_k, batch, cfg->num_heads_kv);
     int rc = evict_validate(Q, K, dtype, len_q, len_k, batch, cfg, s);
@@ -259,14 +264,14 @@ int rkv_evict(const void* Q, const void* K, int dtype, int len_q, int len_k, int
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     const EvictArgs a = make_evict_args(Q, K, dtype, len_q, len_k, q_item_stride, k_item_stride, *cfg, s, 0,
                                         cfg->num_heads_kv, ws);
-    return evict_run(a, *cfg, s, batch, ws, nullptr, kept, kept_stride, n_kept, st);
+    return evict_run(a, *cfg, s, batch, ws, nullptr, kept, kept_stride, n_kept, engine, st);
 }
 
 int rkv_evict_pool_heads(const void* Q, const void* K, int dtype, int len_q, int len_k, int batch,
                          long long q_item_stride, long long k_item_stride, const rkv_config* cfg,
                          int head_begin, int head_count, float* pooled, void* workspace,
                          size_t workspace_bytes, int engine, void* stream) {
-    (void)engine;
+    if (engine < RKV_EVICT_AUTO || engine > RKV_EVICT_TENSOR) return RKV_ERR_INVALID_ARG;
     if (check_cfg(cfg)) return RKV_ERR_INVALID_ARG;
     if (head_begin < 0 || head_count < 0 || head_begin + head_count > cfg->num_heads_kv) return RKV_ERR_INVALID_ARG;
     EvictShape s = evict_shape(*cfg, len_q, len_k, batch, head_count);
@@ -279,7 +284,7 @@ int rkv_evict_pool_heads(const void* Q, const void* K, int dtype, int len_q, int
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     const EvictArgs a = make_evict_args(Q, K, dtype, len_q, len_k, q_item_stride, k_item_stride, *cfg, s,
                                         head_begin, head_count, ws);
-    return evict_run(a, *cfg, s, batch, ws, pooled, nullptr, 0, nullptr, static_cast<cudaStream_t>(stream));
+    return evict_run(a, *cfg, s, batch, ws, pooled, nullptr, 0, nullptr, engine, static_cast<cudaStream_t>(stream));
 }
 
 int rkv_evict_select_pooled(const float* pooled, int len_q, int len_k, int batch, const rkv_config* cfg,
@@ -349,7 +354,8 @@ int rkv_prefill_eviction_host(const float* Q, const float* K, int len_q, int len
     a.k_head_rows = s0.nk;
     int* dk = reinterpret_cast<int*>(base + o_kept);
     int* dn = reinterpret_cast<int*>(base + o_n);
-    if ((rc = evict_run(a, *cfg, s0, 1, base + o_ws, nullptr, dk, max_kept_of(s0, len_k), dn, st))) return rc;
+    if ((rc = evict_run(a, *cfg, s0, 1, base + o_ws, nullptr, dk, max_kept_of(s0, len_k), dn, RKV_EVICT_AUTO, st)))
+        return rc;
     const int nmax = max_kept_of(s0, len_k);
     if (cudaMemcpyAsync(kept_out, dk, (size_t)nmax * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
         cudaMemcpyAsync(n_kept, dn, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)

@@ -27,7 +27,7 @@ RKV_ERR_DEVICE_TIMEOUT = 5
 RKV_ERR_NO_DEVICE = 6
 
 F32, BF16, Q8_0 = 0, 1, 2
-ENGINE_AUTO, ENGINE_SIMT = 0, 1
+ENGINE_AUTO, ENGINE_SIMT, ENGINE_TENSOR = 0, 1, 2
 
 # Every symbol include/rkv.h declares.
 EXPORTS = [
@@ -295,11 +295,11 @@ class Evictor:
                                _ptr(self.ws), self.ws_bytes, engine, _stream(stream)), "rkv_evict")
         return self.kept, self.n_kept
 
-    def pool_heads(self, Q, K, head_begin: int, head_count: int, pooled, stream=None):
+    def pool_heads(self, Q, K, head_begin: int, head_count: int, pooled, stream=None, engine: int = ENGINE_AUTO):
         _check(lib().rkv_evict_pool_heads(_ptr(Q), _ptr(K), self.dtype, self.len_q, self.len_k,
                                           self.batch, Q[0].nbytes, K[0].nbytes, ctypes.byref(self.c),
                                           head_begin, head_count, _ptr(pooled), _ptr(self.ws),
-                                          self.ws_bytes, ENGINE_AUTO, _stream(stream)),
+                                          self.ws_bytes, engine, _stream(stream)),
                "rkv_evict_pool_heads")
         return pooled
 

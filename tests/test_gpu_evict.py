@@ -44,6 +44,34 @@ def test_stage1_cases(name, cuda):
     assert len(got) == len(ref) and len({float(total[i]) for i in diff}) <= 1
 
 
+@pytest.mark.parametrize("name", ["s1_basic", "s1_bf16", "s1_shortq", "s1_mha_ks1", "s1_evenks"])
+def test_stage1_tensor_engine_matches_cuda_cores(name, cuda):
+    """tcgen05 scoring (fp32 as three TF32 products, bf16 direct) against the
+    fp32 CUDA-core engine on the same inputs: pooled rows within 1e-4
+    relative, kept indices identical."""
+    import torch
+    p = dict(cases.STAGE1)[name]
+    Q, K, (kind, Qd, Kd) = cases.stage1_build(p)
+    cfg = to_rkv(cases.stage1_config(p))
+    Qt = dev(Qd, kind, cuda).unsqueeze(0).contiguous()
+    Kt = dev(Kd, kind, cuda).unsqueeze(0).contiguous()
+    ev = rkv.Evictor(cfg, p["len_q"], p["len_k"], 1, KIND[kind], cuda)
+    nk = p["len_k"] - min(p["window"], p["len_q"])
+    pooled = {}
+    for eng in (rkv.ENGINE_TENSOR, rkv.ENGINE_SIMT):
+        out = torch.empty((1, p["HK"], nk), dtype=torch.float32, device=cuda)
+        ev.pool_heads(Qt, Kt, 0, p["HK"], out, engine=eng)
+        torch.cuda.synchronize()
+        pooled[eng] = out[0].cpu().numpy()
+    np.testing.assert_allclose(pooled[rkv.ENGINE_TENSOR], pooled[rkv.ENGINE_SIMT], rtol=1e-4, atol=1e-7)
+    kept = {}
+    for eng in (rkv.ENGINE_TENSOR, rkv.ENGINE_SIMT):
+        k, n = ev(Qt, Kt, engine=eng)
+        kept[eng] = k[0, : int(n[0])].cpu().numpy().copy()
+    np.testing.assert_array_equal(kept[rkv.ENGINE_TENSOR], kept[rkv.ENGINE_SIMT])
+    assert rkv.lib().rkv_workspace_status(rkv._ptr(ev.ws), 0) == 0
+
+
 def test_stage1_config0_full_size(cuda):
     """K [8, 8192, 128] fp32, Q [24, 32, 128] window, budget 1024, ks 63."""
     cfg = O.Config(num_heads=24, num_heads_kv=8, dim_head=128, prompt_budget=1024)
@@ -91,9 +119,10 @@ def test_stage1_head_sharded_equals_fused(cuda):
         part = torch.empty((1, 1, nk), dtype=torch.float32, device=cuda)
         ev.pool_heads(Qt, Kt, h, 1, part)
         pooled[:, h] = part[:, 0]
-    # pooled scores are float sums in a different order than the oracle's
+    # pooled scores: float sums in another order than the oracle's, and (tensor
+    # engine) logits from three TF32 products per step, about 1e-6 relative
     np.testing.assert_allclose(pooled[0].cpu().numpy(), O.evict_pool_heads(Q, K, p["len_q"], p["len_k"], cfg, 0, p["HK"]),
-                               rtol=2e-6, atol=1e-9)
+                               rtol=1e-4, atol=1e-9)
     k1, n1 = ev.select_pooled(pooled)
     a = k1[0, : int(n1[0])].cpu().numpy().copy()
     k2, n2 = ev(Qt, Kt)
