@@ -322,7 +322,7 @@ def time_evict(device, steps, warmup):
         t0 = time.perf_counter()
         rkv.compute_prefill_eviction(Qh, Kh, 32, PROMPT, cfg)
         e2e.append(time.perf_counter() - t0)
-    return statistics.mean(times), statistics.median(e2e) * 1e3, 4  # 2 tcgen05 scoring passes, pool, select
+    return statistics.mean(times), statistics.median(e2e) * 1e3, 5  # 2 tcgen05 scoring passes, fold, pool, select
 
 
 def e2e_decode(cfg, cache, Qs, K, V, steps):

@@ -10,16 +10,17 @@
 //
 // Operands are staged by the threads in shared memory in the K-major,
 // no-swizzle layout of tcgen05 (8-row core matrices of 16-byte rows; the
-// 16-byte K unit u of row r at u * rows * 16 + r * 16), one 128-byte slice of
-// every row at a time, double-buffered; one thread issues the MMAs and a
+// 16-byte K unit u of row r at u * rows * 16 + r * 16), one 64-byte slice of
+// every row at a time, double-buffered, the next slice loaded into registers
+// meanwhile; one thread issues the MMAs and a
 // tcgen05.commit to an mbarrier releases each buffer.  Every wait is bounded;
 // tensor memory is freed on every path.
 //
-// Two launches per call (rocket.cpp:97-116):
+// Three launches per call (rocket.cpp:97-116):
 //   MODE 0  per (row, tile) max and sum of exp(l - max) of the logits
-//           l = (q . k) / sqrt(D); the last CTA of a head folds them into the
-//           row max M_r and 1 / (sum_r + 1e-9) (as the CUDA-core path);
-//   MODE 1  the logits again, then the head score of every key,
+//           l = (q . k) / sqrt(D);
+//   evict_fold_kernel folds those into the row max M_r and 1 / (sum_r + 1e-9);
+//   MODE 1  computes the logits again and the head score of every key,
 //           hs[k] = sum_r exp(l[r][k] - M_r) * inv_r in row order, written
 //           for the pooling kernel (the logits are never stored).
 #include "evict.cuh"
@@ -31,7 +32,7 @@ namespace {
 
 constexpr int kMT = 128;       // keys per tile: the MMA's M
 constexpr int kMmaNT = 128;    // threads: warp w reads tensor-memory lanes 32w .. 32w+31
-constexpr int kSliceB = 128;   // bytes of every row staged per slice (eight 16-byte K units)
+constexpr int kSliceB = 64;    // bytes of every row staged per slice (four 16-byte K units, two MMA K steps)
 constexpr int kTB = 129;       // row stride (floats) of the statistics transpose buffer
 
 // ---- tcgen05 / tensor memory (PTX ISA 8.7) --------------------------------
@@ -137,7 +138,6 @@ __global__ void __launch_bounds__(kMmaNT) evict_mma_kernel(const EvictArgs a) {
     const MmaLayout L = mma_layout(a.R, a.D, ES, MODE);
     uint64_t* done = reinterpret_cast<uint64_t*>(sm);  // [2]: MMAs of buffer 0 / 1 complete
     uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + 16);
-    __shared__ int s_last, s_fail;
 
     const int tile = blockIdx.x, hc = blockIdx.y, b = blockIdx.z;
     const int hk = a.head_begin + hc;
@@ -152,7 +152,6 @@ __global__ void __launch_bounds__(kMmaNT) evict_mma_kernel(const EvictArgs a) {
         mbar_init(&done[0], 1);
         mbar_init(&done[1], 1);
         fence_mbar_init();
-        s_fail = 0;
     }
     if (warp == 0) tmem_alloc(tslot, tcols);
     if (MODE == 1) {
@@ -170,7 +169,35 @@ __global__ void __launch_bounds__(kMmaNT) evict_mma_kernel(const EvictArgs a) {
     const size_t rowb = (size_t)a.D * ES;
     const uint8_t* krow = Kb + ((size_t)hk * a.k_head_rows + k0 + tid) * rowb;  // this thread's key row
     const uint32_t idesc = mma_idesc(TF32 ? 2u : 1u, (uint32_t)NP);
+    constexpr int UPS = kSliceB / 16;  // 16-byte units per row and slice
+    // this thread's Q rows: r = tid and r = tid + 128 (zero beyond R)
+    const uint8_t* qrow[2] = {nullptr, nullptr};
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int r = tid + i * kMmaNT;
+        if (r < a.R) {
+            const int h = hk * a.G + r / a.obs_w;
+            const int pos = a.q_row0 + r % a.obs_w;
+            qrow[i] = Qb + ((size_t)h * a.q_head_rows + pos) * rowb;
+        }
+    }
+    // the next slice's global data is loaded into registers while the current one is stored and multiplied
+    uint4 kx[UPS], qx[2][UPS];
+    auto fetch = [&](int s) {
+        const int u0 = s * UPS, nu = min(UPS, L.upr - u0);
+#pragma unroll
+        for (int u = 0; u < UPS; ++u) {
+            kx[u] = make_uint4(0u, 0u, 0u, 0u);
+            if (u < nu && tid < nkeys) kx[u] = __ldg(reinterpret_cast<const uint4*>(krow) + u0 + u);
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                qx[i][u] = make_uint4(0u, 0u, 0u, 0u);
+                if (u < nu && qrow[i]) qx[i][u] = __ldg(reinterpret_cast<const uint4*>(qrow[i]) + u0 + u);
+            }
+        }
+    };
     bool ok = true;
+    fetch(0);
     for (int s = 0; s < L.slices && ok; ++s) {
         const int bi = s & 1;
         uint8_t* buf = sm + 128 + bi * L.buf;
@@ -185,41 +212,33 @@ __global__ void __launch_bounds__(kMmaNT) evict_mma_kernel(const EvictArgs a) {
                 break;
             }
         }
-        const int u0 = s * (kSliceB / 16), nu = min(kSliceB / 16, L.upr - u0);  // units in this slice
-        // K: thread = key row
-        for (int u = 0; u < nu; ++u) {
-            uint4 x = make_uint4(0u, 0u, 0u, 0u);
-            if (tid < nkeys) x = __ldg(reinterpret_cast<const uint4*>(krow) + u0 + u);
+        const int nu = min(UPS, L.upr - s * UPS);  // units in this slice (even)
+#pragma unroll
+        for (int u = 0; u < UPS; ++u) {
+            if (u >= nu) break;
             if (TF32) {
                 uint4 h, l;
-                split_tf32(x, h, l);
+                split_tf32(kx[u], h, l);
                 *reinterpret_cast<uint4*>(khi + u * (kMT * 16) + tid * 16) = h;
                 *reinterpret_cast<uint4*>(klo + u * (kMT * 16) + tid * 16) = l;
             } else {
-                *reinterpret_cast<uint4*>(khi + u * (kMT * 16) + tid * 16) = x;
+                *reinterpret_cast<uint4*>(khi + u * (kMT * 16) + tid * 16) = kx[u];
             }
-        }
-        // Q: rows r = tid, tid + 128 (the group's window rows, zero beyond R)
-        for (int r = tid; r < NP; r += kMmaNT) {
-            const uint8_t* qrow = nullptr;
-            if (r < a.R) {
-                const int h = hk * a.G + r / a.obs_w;
-                const int pos = a.q_row0 + r % a.obs_w;
-                qrow = Qb + ((size_t)h * a.q_head_rows + pos) * rowb;
-            }
-            for (int u = 0; u < nu; ++u) {
-                uint4 x = make_uint4(0u, 0u, 0u, 0u);
-                if (qrow) x = __ldg(reinterpret_cast<const uint4*>(qrow) + u0 + u);
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int r = tid + i * kMmaNT;
+                if (r >= NP) break;
                 if (TF32) {
                     uint4 h, l;
-                    split_tf32(x, h, l);
+                    split_tf32(qx[i][u], h, l);
                     *reinterpret_cast<uint4*>(qhi + u * (NP * 16) + r * 16) = h;
                     *reinterpret_cast<uint4*>(qlo + u * (NP * 16) + r * 16) = l;
                 } else {
-                    *reinterpret_cast<uint4*>(qhi + u * (NP * 16) + r * 16) = x;
+                    *reinterpret_cast<uint4*>(qhi + u * (NP * 16) + r * 16) = qx[i][u];
                 }
             }
         }
+        if (s + 1 < L.slices) fetch(s + 1);
         fence_proxy_async();  // generic-proxy stores -> visible to the tensor core
         __syncthreads();
         if (tid == 0) {
@@ -300,37 +319,41 @@ __global__ void __launch_bounds__(kMmaNT) evict_mma_kernel(const EvictArgs a) {
     if (warp == 0) tmem_dealloc(tbase, tcols);
     if (!ok) return;
 
-    if (MODE == 0) {
-        // the last CTA of this (item, head) folds the tile statistics (rocket.cpp:108-113)
-        if (tid == 0) {
-            __threadfence();
-            const unsigned prev = atomicAdd(&a.counters[(size_t)b * a.head_count + hc], 1u);
-            s_last = (prev == (unsigned)a.ntiles - 1u);
-        }
-        __syncthreads();
-        if (!s_last) return;
-        __threadfence();
-        for (int r = tid; r < a.R; r += kMmaNT) {
-            const float2* ts = a.tstats + (row_base + r) * a.ntiles;
-            float M = -FLT_MAX;
-            for (int t = 0; t < a.ntiles; ++t) M = fmaxf(M, __ldcg(&ts[t].x));
-            float S = 0.0f;
-            for (int t = 0; t < a.ntiles; ++t) {
-                const float2 v = __ldcg(ts + t);
-                S += v.y * expf(v.x - M);
-            }
-            a.rstats[row_base + r] = make_float2(M, 1.0f / (S + 1e-9f));
-        }
-        if (tid == 0) a.counters[(size_t)b * a.head_count + hc] = 0u;
+}
+
+// Row max M_r and 1 / (sum_r + 1e-9) from the tile statistics
+// (rocket.cpp:108-113), one warp per (item, head, row): max over the tiles,
+// then sum_t s_t * exp(m_t - M_r).
+constexpr int kFoldRows = 8;  // rows (warps) per CTA
+__global__ void __launch_bounds__(kFoldRows * 32) evict_fold_kernel(const EvictArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int r = blockIdx.x * kFoldRows + (threadIdx.x >> 5), hc = blockIdx.y, b = blockIdx.z;
+    if (r >= a.R) return;  // warp-uniform
+    const size_t row = ((size_t)b * a.head_count + hc) * a.R + r;
+    const float2* ts = a.tstats + row * a.ntiles;
+    float M = -FLT_MAX;
+    for (int t = lane; t < a.ntiles; t += 32) M = fmaxf(M, ts[t].x);
+#pragma unroll
+    for (int x = 16; x > 0; x >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, x));
+    float S = 0.0f;
+    for (int t = lane; t < a.ntiles; t += 32) {
+        const float2 v = ts[t];
+        S += v.y * expf(v.x - M);
     }
+#pragma unroll
+    for (int x = 16; x > 0; x >>= 1) S += __shfl_xor_sync(0xffffffffu, S, x);
+    if (lane == 0) a.rstats[row] = make_float2(M, 1.0f / (S + 1e-9f));
 }
 
 template <typename T>
 int launch_t(const EvictArgs& a, int batch, cudaStream_t st) {
     const MmaLayout L0 = mma_layout(a.R, a.D, (int)sizeof(T), 0);
     const MmaLayout L1 = mma_layout(a.R, a.D, (int)sizeof(T), 1);
-    // at most two CTAs per SM when a CTA takes 256 tensor-memory columns
-    const size_t floor = L0.NP > 128 ? 116 * 1024 : 0;
+    // Resident CTAs share the SM's 512 tensor-memory columns: size the shared
+    // memory so at most 512 / tcols of them fit (228 KB per SM, 1 KB reserved per CTA).
+    const int tcols = L0.NP <= 32 ? 32 : L0.NP <= 64 ? 64 : L0.NP <= 128 ? 128 : 256;
+    const int maxc = 512 / tcols;
+    const size_t floor = (size_t)(228 * 1024) / (size_t)(maxc + 1) - 1024 + 256;
     const size_t s0 = (size_t)L0.total > floor ? (size_t)L0.total : floor;
     const size_t s1 = (size_t)L1.total > floor ? (size_t)L1.total : floor;
     auto f0 = evict_mma_kernel<T, 0>;
@@ -338,10 +361,10 @@ int launch_t(const EvictArgs& a, int batch, cudaStream_t st) {
     if (cudaFuncSetAttribute(f0, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s0) != cudaSuccess ||
         cudaFuncSetAttribute(f1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s1) != cudaSuccess)
         return RKV_ERR_CUDA;
-    if (cudaMemsetAsync(a.counters, 0, (size_t)batch * a.head_count * sizeof(unsigned), st) != cudaSuccess)
-        return RKV_ERR_CUDA;
     dim3 grid(a.ntiles, a.head_count, batch);
     f0<<<grid, kMmaNT, s0, st>>>(a);
+    if (cudaGetLastError() != cudaSuccess) return RKV_ERR_CUDA;
+    evict_fold_kernel<<<dim3((a.R + kFoldRows - 1) / kFoldRows, a.head_count, batch), kFoldRows * 32, 0, st>>>(a);
     if (cudaGetLastError() != cudaSuccess) return RKV_ERR_CUDA;
     f1<<<grid, kMmaNT, s1, st>>>(a);
     return cudaGetLastError() == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
