@@ -206,6 +206,15 @@ int rkv_hsa_decode_noalloc(const void* Q, const void* K, const void* V, int dtyp
  * `stream`, returns RKV_OK or the recorded status, and clears it. */
 int rkv_workspace_status(void* workspace, void* stream);
 
+/* Diagnostic (no reference counterpart): launches one warp that waits on a
+ * barrier nothing completes, through the same bounded wait the kernels use,
+ * so the failure path can be checked without a GPU fault: the wait gives up
+ * after about two seconds of device time and records RKV_ERR_DEVICE_TIMEOUT
+ * in the workspace error word (clear on entry), which rkv_workspace_status
+ * then returns; the CUDA context stays usable.  workspace: device memory,
+ * 16-byte aligned, at least 16 bytes.  Asynchronous on `stream`. */
+int rkv_selftest_wait_timeout(void* workspace, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

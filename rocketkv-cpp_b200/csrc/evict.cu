@@ -283,6 +283,18 @@ __global__ void evict_keep_all_kernel(int* kept, int kept_stride, int* n_kept, i
     if (blockIdx.x == 0 && threadIdx.x == 0) n_kept[b] = len_k;
 }
 
+// One warp waits on a barrier that nothing arrives at; the bounded wait runs
+// out and records RKV_ERR_DEVICE_TIMEOUT (the diagnostic of the failure path).
+__global__ void wait_selftest_kernel(int* err) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    mbar_wait_bounded(&bar, 0, err);
+}
+
 int floor_log2(int x) {
     int j = 0;
     while ((2 << j) <= x) ++j;
@@ -369,6 +381,12 @@ int launch_evict_pool(const PoolArgs& in, int batch, cudaStream_t st) {
 
 int launch_evict_select(const SelectArgs& a, int batch, cudaStream_t st) {
     evict_select_kernel<<<batch, kSelNT, 0, st>>>(a);
+    return cudaGetLastError() == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
+}
+
+int launch_wait_selftest(int* err, cudaStream_t st) {
+    if (cudaMemsetAsync(err, 0, sizeof(int), st) != cudaSuccess) return RKV_ERR_CUDA;
+    wait_selftest_kernel<<<1, 32, 0, st>>>(err);
     return cudaGetLastError() == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
 }
 

@@ -56,5 +56,7 @@ int launch_evict_mma(const EvictArgs& a, int batch, cudaStream_t st);
 int launch_evict_pool(const PoolArgs& a, int batch, cudaStream_t st);
 int launch_evict_select(const SelectArgs& a, int batch, cudaStream_t st);
 int launch_evict_keep_all(int* kept, int kept_stride, int* n_kept, int len_k, int batch, cudaStream_t st);
+// the bounded-wait diagnostic (rkv_selftest_wait_timeout)
+int launch_wait_selftest(int* err, cudaStream_t st);
 
 }  // namespace rkv

@@ -498,4 +498,9 @@ int rkv_workspace_status(void* workspace, void* stream) {
     return e;
 }
 
+int rkv_selftest_wait_timeout(void* workspace, void* stream) {
+    if (!workspace || !aligned16(workspace)) return RKV_ERR_INVALID_ARG;
+    return launch_wait_selftest(static_cast<int*>(workspace), static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -36,6 +36,7 @@ EXPORTS = [
     "rkv_evict_select_pooled", "rkv_prefill_eviction_host", "rkv_hsa_sel_capacity",
     "rkv_hsa_workspace_size", "rkv_hsa_decode", "rkv_hybrid_sparse_decode_host",
     "rkv_hsa_decode_host_ex", "rkv_workspace_status", "rkv_hsa_decode_noalloc",
+    "rkv_selftest_wait_timeout",
 ]
 
 
@@ -127,6 +128,7 @@ def lib() -> ctypes.CDLL:
         "rkv_hybrid_sparse_decode_host": ([_VP, _VP, _VP, _I, _CFGP, _VP], _I),
         "rkv_hsa_decode_host_ex": ([_VP, _VP, _VP, _I, _I, _I, _I, _LL, _LL, _CFGP, _VP, _VP, _I, _VP], _I),
         "rkv_workspace_status": ([_VP, _VP], _I),
+        "rkv_selftest_wait_timeout": ([_VP, _VP], _I),
         "rkv_hsa_decode_noalloc": ([_VP, _VP, _VP, _I, _I, _I, _I, _LL, _LL, _CFGP, _I, _I, _VP, _VP, _I, _VP,
                                     _VP], _I),
     }

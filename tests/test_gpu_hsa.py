@@ -159,3 +159,19 @@ def test_stage2_headline_batch_properties(cuda):
         q = Q[b].float().cpu().numpy()
         Kb, Vb = K[b].float().cpu().numpy(), V[b].float().cpu().numpy()
         check_against_oracle(q, Kb, Vb, L, cfg, d.O[b].cpu().numpy(), sel[b], nsel[b], w=w)
+
+
+def test_bounded_wait_runs_out_and_reports(cuda):
+    """Failure path without a GPU fault: a kernel waits on a barrier nothing
+    completes; the bounded wait gives up (about two seconds), the status is
+    RKV_ERR_DEVICE_TIMEOUT, and the context still runs a decode correctly."""
+    import torch
+    ws = torch.zeros(64, dtype=torch.uint8, device=cuda)
+    assert rkv.lib().rkv_selftest_wait_timeout(rkv._ptr(ws), 0) == 0
+    assert rkv.lib().rkv_workspace_status(rkv._ptr(ws), 0) == rkv.RKV_ERR_DEVICE_TIMEOUT
+    assert rkv.lib().rkv_workspace_status(rkv._ptr(ws), 0) == 0  # reading the status clears it
+    p = dict(cases.STAGE2)["s2_mha_d64"]
+    q, K, V = cases.stage2_build(p)
+    cfg = cases.stage2_config(p)
+    Og, sel, nsel = run_gpu(q[None], K[None], V[None], p["L"], cfg, cuda, bf16=p["bf16"])
+    check_against_oracle(q, K, V, p["L"], cfg, Og[0], sel[0], nsel[0], bf16=p["bf16"])
