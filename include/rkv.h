@@ -176,7 +176,10 @@ int rkv_hybrid_sparse_decode_host(const float* Q, const float* K, const float* V
 
 /* Host-buffer stage 2, general form (any dtype, batch, recent window): the
  * inputs are host buffers laid out as for rkv_hsa_decode; copies in, runs,
- * copies O (and sel/n_sel when non-NULL) back.  Synchronous. */
+ * copies O (and sel/n_sel when non-NULL) back.  Synchronous.  When V is
+ * pinned host memory mapped into the device's address space (cudaHostAlloc,
+ * or cudaHostRegister with mapping), V is not copied: the attention reads the
+ * selected rows in place, so only those cross the bus. */
 int rkv_hsa_decode_host_ex(const void* Q, const void* K, const void* V, int dtype,
                            int len_k, int recent_window, int batch,
                            long long q_item_stride, long long kv_item_stride,

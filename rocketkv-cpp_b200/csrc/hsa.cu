@@ -75,6 +75,16 @@ __device__ __forceinline__ void vec_to_f<uint16_t>(const uint4& v, float* out) {
     }
 }
 
+// A plain (coherent) 16-byte global load: V may be pinned host memory that
+// the host path maps into the device's address space.
+__device__ __forceinline__ uint4 ld_global_v4(const uint4* p) {
+    uint4 v;
+    asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -914,7 +924,7 @@ __global__ void __launch_bounds__(kNT, 3) hsa_attn_kernel(const HsaArgs a) {
 #pragma unroll
         for (int u = 0; u < UC; ++u) {
             const int j = j0 + u * NGC;
-            if (j < n) vw[u] = __ldg(reinterpret_cast<const uint4*>(Vu + (size_t)sel[j] * RB) + vi);
+            if (j < n) vw[u] = ld_global_v4(reinterpret_cast<const uint4*>(Vu + (size_t)sel[j] * RB) + vi);
         }
 #pragma unroll
         for (int u = 0; u < UC; ++u) {

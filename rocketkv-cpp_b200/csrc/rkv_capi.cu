@@ -447,8 +447,19 @@ int rkv_hsa_decode_host_ex(const void* Q, const void* K, const void* V, int dtyp
     const size_t kvbytes = (size_t)kv_item_stride * (batch - 1) + row_bytes(dtype, cfg->dim_head) * (size_t)HK * len_k;
     const size_t obytes = (size_t)batch * cfg->num_heads * cfg->dim_head * 4;
     const int sstride = s.sel_cap > 0 ? s.sel_cap : 1;
+    // V in pinned host memory that the device can address (cudaHostAlloc, or
+    // cudaHostRegister with mapping) is read in place by the attention kernel:
+    // only the selected rows cross the bus.  Otherwise V is copied like K.
+    const void* v_mapped = nullptr;
+    cudaPointerAttributes pa;
+    if (cudaPointerGetAttributes(&pa, V) == cudaSuccess) {
+        if (pa.type == cudaMemoryTypeHost && pa.devicePointer && aligned16(pa.devicePointer)) v_mapped = pa.devicePointer;
+    } else {
+        cudaGetLastError();
+    }
     Carve cv;
-    const size_t o_q = cv.take(qbytes), o_k = cv.take(kvbytes), o_v = cv.take(kvbytes), o_o = cv.take(obytes);
+    const size_t o_q = cv.take(qbytes), o_k = cv.take(kvbytes), o_v = cv.take(v_mapped ? 0 : kvbytes),
+                 o_o = cv.take(obytes);
     const size_t o_sel = cv.take((size_t)batch * HK * sstride * 4), o_n = cv.take((size_t)batch * HK * 4);
     const size_t o_ws = cv.take(s.ws_bytes);
     DevCtx* ctx;
@@ -458,10 +469,11 @@ int rkv_hsa_decode_host_ex(const void* Q, const void* K, const void* V, int dtyp
     cudaStream_t st = ctx->stream;
     if (cudaMemcpyAsync(base + o_q, Q, qbytes, cudaMemcpyHostToDevice, st) != cudaSuccess ||
         cudaMemcpyAsync(base + o_k, K, kvbytes, cudaMemcpyHostToDevice, st) != cudaSuccess ||
-        cudaMemcpyAsync(base + o_v, V, kvbytes, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        (!v_mapped && cudaMemcpyAsync(base + o_v, V, kvbytes, cudaMemcpyHostToDevice, st) != cudaSuccess) ||
         cudaMemsetAsync(base + o_o, 0, obytes, st) != cudaSuccess)
         return RKV_ERR_CUDA;
-    rc = rkv_hsa_decode(base + o_q, base + o_k, base + o_v, dtype, len_k, recent_window, batch, q_item_stride,
+    const void* vd = v_mapped ? v_mapped : static_cast<const void*>(base + o_v);
+    rc = rkv_hsa_decode(base + o_q, base + o_k, vd, dtype, len_k, recent_window, batch, q_item_stride,
                         kv_item_stride, cfg, 0, HK, reinterpret_cast<float*>(base + o_o),
                         reinterpret_cast<int*>(base + o_sel), sstride, reinterpret_cast<int*>(base + o_n),
                         base + o_ws, s.ws_bytes, st);

@@ -99,6 +99,20 @@ def test_stage2_host_ex_bf16_with_selection(cuda):
     check_against_oracle(q, K, V, p["L"], cfg, Og[0], sel[0], nsel[0], w=32)
 
 
+def test_stage2_host_ex_pinned_v_read_in_place(cuda):
+    """Host path with V in pinned host memory: the attention reads the selected
+    V rows in place (no copy of V); same selection and O as the oracle."""
+    import torch
+    p = dict(cases.STAGE2)["s2_headline"]
+    q, K, V = cases.stage2_build(p)
+    cfg = cases.stage2_config(p)
+    Vp = torch.from_numpy(rkvgen.bf16_bits(V)[None].view(np.int16)).pin_memory()
+    Og, sel, nsel = rkv.hsa_decode_host(rkvgen.bf16_bits(q)[None], rkvgen.bf16_bits(K)[None],
+                                        Vp.numpy().view(np.uint16), rkv.BF16, p["L"], to_rkv(cfg),
+                                        recent_window=32, with_sel=True)
+    check_against_oracle(q, K, V, p["L"], cfg, Og[0], sel[0], nsel[0], w=32)
+
+
 @pytest.mark.parametrize("L,k,C,r", [(1, 1, 1, 1), (5, 0, 2, 8), (33, 32, 2, 8), (64, 1, 64, 128), (130, 17, 65, 3)])
 def test_stage2_edges(L, k, C, r, cuda):
     cfg = O.Config(num_heads=6, num_heads_kv=2, dim_head=128, topk_decode=k, chunk_size=C, r_dim=r)
