@@ -42,25 +42,29 @@ void rkvo_compute_params(int token_budget, int sequence_length, int max_new_toke
 }
 
 /* ------------------------------------------------------------------------ */
-/* exp for the stage-2 selection path.                                        */
+/* exp for the stage-2 selection path, x <= 0 (the softmax argument l - max).  */
 /* Method: Cody & Waite argument reduction x = n*ln2 + r, |r| <= ln2/2, with  */
-/* ln2 split into a 12-bit-short head and a tail, then the degree-7 Taylor    */
-/* polynomial of e^r (coefficients 1/k!) in Horner form with fused            */
-/* multiply-adds, then an exact scaling by 2^n.  Every step is a correctly    */
-/* rounded IEEE operation, so the CUDA copy of this routine returns the same  */
-/* bits.  Accuracy is checked against double-precision exp in the tests.     */
+/* n rounded by one fused multiply-add against 1.5*2^23, ln2 split into a     */
+/* 12-bit-short head and a tail, then the degree-7 Taylor polynomial of e^r   */
+/* (coefficients 1/k!) in Horner form with fused multiply-adds, then an exact */
+/* two-step scaling by 2^n.  Every step is a correctly rounded IEEE operation,*/
+/* so the CUDA copy of this routine returns the same bits.  Accuracy is       */
+/* checked against double-precision exp in the tests.                         */
 /* ------------------------------------------------------------------------ */
 static float f_from_bits(uint32_t b) { float f; memcpy(&f, &b, 4); return f; }
 
 float rkvo_expf(float x) {
     if (x != x) return x;
-    if (x > 88.72283935546875f) return INFINITY;
-    if (x < -103.97208404541015625f) return 0.0f;
+    if (x > 0.0f) return expf(x);  /* outside the selection's domain (x = l - max <= 0) */
     const float log2e = f_from_bits(0x3fb8aa3bu);   /* 1/ln2 rounded to float   */
     const float ln2_hi = f_from_bits(0x3f317000u);  /* ln2, low 12 bits cleared */
     const float ln2_lo = f_from_bits(0x3805fdf4u);  /* ln2 - ln2_hi, rounded    */
-    float n = rintf(x * log2e);
-    float r = fmaf(-n, ln2_hi, x);
+    const float magic = f_from_bits(0x4b400000u);   /* 1.5 * 2^23               */
+    const float xc = x < -104.0f ? -104.0f : x;
+    /* n = round-to-nearest-even(x * log2e): one fused multiply-add against 1.5*2^23 */
+    const float t = fmaf(xc, log2e, magic);
+    const float n = t - magic;
+    float r = fmaf(-n, ln2_hi, xc);
     r = fmaf(-n, ln2_lo, r);
     float p = f_from_bits(0x39500d01u);             /* 1/7! */
     p = fmaf(p, r, f_from_bits(0x3ab60b61u));       /* 1/6! */
@@ -70,11 +74,12 @@ float rkvo_expf(float x) {
     p = fmaf(p, r, 0.5f);                           /* 1/2! */
     p = fmaf(p, r, 1.0f);
     p = fmaf(p, r, 1.0f);
-    int ni = (int)n;
-    if (ni > 127) return (p * f_from_bits(0x7f000000u)) * 2.0f;
-    if (ni >= -126) return p * f_from_bits((uint32_t)(ni + 127) << 23);
-    /* subnormal result: exact scaling into the normal range, then one rounding */
-    return (p * f_from_bits((uint32_t)(ni + 64 + 127) << 23)) * f_from_bits(0x1f800000u); /* 2^-64 */
+    uint32_t tb;
+    memcpy(&tb, &t, 4);
+    const int ni = (int)tb - 0x4b400000;            /* n as an integer, -151 .. 0 */
+    /* exact two-step scaling: p * 2^(n+64) is exact, * 2^-64 rounds once (subnormals too) */
+    const float res = (p * f_from_bits((uint32_t)(ni + 64 + 127) << 23)) * f_from_bits(0x1f800000u);
+    return x < -103.97208404541015625f ? 0.0f : res;
 }
 
 /* ------------------------------------------------------------------------ */

@@ -556,7 +556,7 @@ __global__ void __launch_bounds__(kSelThreads, 8) hsa_select_kernel(const HsaArg
     __shared__ float part[MAXG][kSelThreads];
     __shared__ float red_[MAXG][kSelThreads / 32];
     __shared__ float hmax[MAXG], hinv[MAXG];
-    __shared__ int hist[256], scan_tmp[33];
+    __shared__ int hist[256], scan_tmp[66];
     __shared__ int s_kk;
     __shared__ uint32_t s_prefix;
 
@@ -702,26 +702,22 @@ __global__ void __launch_bounds__(kSelThreads, 8) hsa_select_kernel(const HsaArg
         }
         const uint32_t thr = s_prefix;
         const int need = s_kk;
-        // stable compaction: thread t owns the contiguous page range [c_beg, c_end)
+        // stable compaction: thread t owns the contiguous page range [c_beg, c_end);
+        // threshold ties are taken in token order until `need` is met, so the
+        // output position is (weight above the threshold before the range) +
+        // min(tie weight before the range, need): one scan of both weights
         const int per = (nch + kSelThreads - 1) / kSelThreads;
         const int c_beg = min(nch, tid * per), c_end = min(nch, c_beg + per);
-        int eqw = 0;
-        for (int c = c_beg; c < c_end; ++c)
-            if (keys[c] == thr) eqw += min(C, Lc - c * C);
-        int tot;
-        int eq_rank = block_exclusive_scan(eqw, scan_tmp, &tot);
-        int takes = 0;
-        for (int c = c_beg, eb = eq_rank; c < c_end; ++c) {
+        int gtw = 0, eqw = 0;
+        for (int c = c_beg; c < c_end; ++c) {
             const uint32_t k = keys[c];
             const int wt = min(C, Lc - c * C);
-            if (k > thr) {
-                takes += wt;
-            } else if (k == thr) {
-                takes += max(0, min(wt, need - eb));
-                eb += wt;
-            }
+            if (k > thr) gtw += wt;
+            else if (k == thr) eqw += wt;
         }
-        int pos = block_exclusive_scan(takes, scan_tmp, &tot);
+        int eq_rank, tot_gt, tot_eq;
+        const int gt_before = block_exclusive_scan2(gtw, eqw, scan_tmp, &eq_rank, &tot_gt, &tot_eq);
+        int pos = gt_before + min(eq_rank, need);
         for (int c = c_beg; c < c_end; ++c) {
             const uint32_t k = keys[c];
             const int wt = min(C, Lc - c * C);

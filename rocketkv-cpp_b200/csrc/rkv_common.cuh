@@ -45,20 +45,24 @@ __host__ __device__ inline size_t row_bytes(int dtype, int dim) {
 }
 
 // ---------------------------------------------------------------------------
-// Deterministic exp for the stage-2 selection path (identical IEEE operation
-// sequence to the oracle's rkvo_expf): Cody & Waite reduction with ln2 split
-// into a short head and a tail, degree-7 Taylor polynomial (1/k!) by Horner
-// with fused multiply-adds, exact scaling by 2^n.
+// Deterministic exp for the stage-2 selection path, for x <= 0 (the softmax
+// argument l - max) and NaN; the same IEEE operation sequence as the oracle's
+// rkvo_expf.  Cody & Waite reduction x = n ln2 + r with n = round(x log2 e)
+// taken by one fused multiply-add against 1.5 * 2^23 (round to nearest even,
+// no double rounding), ln2 split into a short head and a tail, the degree-7
+// Taylor polynomial (1/k!) by Horner with fused multiply-adds, then the exact
+// two-step scaling p * 2^(n+64) * 2^-64 (one rounding, subnormals included).
+// Branch-free.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float det_expf(float x) {
-    if (x != x) return x;
-    if (x > 88.72283935546875f) return __int_as_float(0x7f800000);
-    if (x < -103.97208404541015625f) return 0.0f;
     const float log2e = __int_as_float(0x3fb8aa3b);
     const float ln2_hi = __int_as_float(0x3f317000);
     const float ln2_lo = __int_as_float(0x3805fdf4);
-    const float n = rintf(__fmul_rn(x, log2e));
-    float r = __fmaf_rn(-n, ln2_hi, x);
+    const float magic = __int_as_float(0x4b400000);  // 1.5 * 2^23
+    const float xc = fmaxf(x, -104.0f);
+    const float t = __fmaf_rn(xc, log2e, magic);
+    const float n = __fsub_rn(t, magic);
+    float r = __fmaf_rn(-n, ln2_hi, xc);
     r = __fmaf_rn(-n, ln2_lo, r);
     float p = __int_as_float(0x39500d01);
     p = __fmaf_rn(p, r, __int_as_float(0x3ab60b61));
@@ -68,10 +72,10 @@ __device__ __forceinline__ float det_expf(float x) {
     p = __fmaf_rn(p, r, 0.5f);
     p = __fmaf_rn(p, r, 1.0f);
     p = __fmaf_rn(p, r, 1.0f);
-    const int ni = static_cast<int>(n);
-    if (ni > 127) return __fmul_rn(__fmul_rn(p, __int_as_float(0x7f000000)), 2.0f);
-    if (ni >= -126) return __fmul_rn(p, __int_as_float((ni + 127) << 23));
-    return __fmul_rn(__fmul_rn(p, __int_as_float((ni + 64 + 127) << 23)), __int_as_float(0x1f800000));
+    const int ni = __float_as_int(t) - 0x4b400000;  // n as an integer, -151 .. 0
+    const float res = __fmul_rn(__fmul_rn(p, __int_as_float((ni + 64 + 127) << 23)), __int_as_float(0x1f800000));
+    const float out = x < -103.97208404541015625f ? 0.0f : res;
+    return x != x ? x : out;
 }
 
 // Order-preserving map float -> uint32 (larger float, larger key).
@@ -142,9 +146,9 @@ __device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t pa
 }
 
 // Bounded wait for phase `parity` of `bar`.  Returns false (and records
-// RKV_ERR_DEVICE_TIMEOUT in *err) if the clock budget runs out.
-// Backs off with a short sleep between polls so waiting warps leave the
-// issue slots to the warps that have work.
+// RKV_ERR_DEVICE_TIMEOUT in *err) if the clock budget runs out.  Waiting
+// threads are suspended by try_wait's time hint, so they leave the issue
+// slots to the warps that have work.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
@@ -189,6 +193,53 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* tmp, int* total)
     *total = tmp[32];
     __syncthreads();  // tmp reusable after return
     return before;
+}
+
+// Block-wide exclusive scan of two ints per thread at once (same contract as
+// block_exclusive_scan; `tmp` holds 66 ints).  Returns the prefix of `a` and
+// writes the prefix of `b` to *pb; the totals to *ta, *tb.
+__device__ __forceinline__ int block_exclusive_scan2(int a, int b, int* tmp, int* pb, int* ta, int* tb) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    int x = a, y = b;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, x, o), v = __shfl_up_sync(0xffffffffu, y, o);
+        if (lane >= o) {
+            x += u;
+            y += v;
+        }
+    }
+    if (lane == 31) {
+        tmp[warp] = x;
+        tmp[33 + warp] = y;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        int u = lane < nwarps ? tmp[lane] : 0, v = lane < nwarps ? tmp[33 + lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int uu = __shfl_up_sync(0xffffffffu, u, o), vv = __shfl_up_sync(0xffffffffu, v, o);
+            if (lane >= o) {
+                u += uu;
+                v += vv;
+            }
+        }
+        if (lane < nwarps) {
+            tmp[lane] = u;
+            tmp[33 + lane] = v;
+        }
+        if (lane == nwarps - 1) {
+            tmp[32] = u;
+            tmp[65] = v;
+        }
+    }
+    __syncthreads();
+    const int before_a = (warp > 0 ? tmp[warp - 1] : 0) + x - a;
+    *pb = (warp > 0 ? tmp[33 + warp - 1] : 0) + y - b;
+    *ta = tmp[32];
+    *tb = tmp[65];
+    __syncthreads();  // tmp reusable after return
+    return before_a;
 }
 
 }  // namespace rkv
