@@ -53,11 +53,21 @@ typedef enum rkv_dtype {
 typedef enum rkv_evict_engine {
     RKV_EVICT_AUTO = 0,   /* the fastest engine built for the inputs          */
     RKV_EVICT_SIMT = 1,   /* fp32 CUDA-core scoring                            */
-    RKV_EVICT_TENSOR = 2  /* tcgen05 tensor-core scoring: fp32 K/Q as three
-                             TF32 products per step, bf16 directly; needs
-                             16-byte aligned rows and a row size that is a
-                             multiple of 32 bytes (else RKV_ERR_UNSUPPORTED);
-                             AUTO takes it whenever it applies               */
+    RKV_EVICT_TENSOR = 2, /* tcgen05 tensor-core scoring: fp32 and q8_0 K/Q
+                             (q8_0 dequantised exactly to fp32 in shared
+                             memory) as three TF32 products per step, bf16
+                             directly.  The persistent kernel (one CTA per
+                             SM, TMA-staged K, window queries resident) takes
+                             G * window <= 128 with fp32/bf16 rows 16-byte
+                             aligned and a multiple of 32 bytes, or q8_0 at
+                             dim_head 128; other fp32/bf16 shapes with such
+                             rows run the per-tile kernel; anything else is
+                             RKV_ERR_UNSUPPORTED.  AUTO takes it whenever it
+                             applies                                         */
+    RKV_EVICT_TENSOR_TILES = 3 /* the per-tile tcgen05 kernel only (one CTA
+                             per 128-key tile; fp32 and bf16), kept as the
+                             fallback of RKV_EVICT_TENSOR and for
+                             comparison                                      */
 } rkv_evict_engine;
 
 /* Field-for-field image of RocketConfig (rocket.h:18-34). */

@@ -321,9 +321,12 @@ EvictShape evict_shape(const rkv_config& c, int len_q, int len_k, int batch, int
     s.off_counters = off; off = align_up(off + B * HC * sizeof(unsigned), kWorkspaceAlign);
     s.off_rstats = off;   off = align_up(off + B * HC * R * sizeof(float2), kWorkspaceAlign);
     s.off_tstats = off;   off = align_up(off + B * HC * R * s.ntiles * sizeof(float2), kWorkspaceAlign);
-    s.off_logits = off;   off = align_up(off + B * HC * R * nk * sizeof(float), kWorkspaceAlign);
+    s.nkp = (int)((nk + 3) & ~(size_t)3);
+    s.off_logits = off;   off = align_up(off + B * HC * R * (size_t)s.nkp * sizeof(float), kWorkspaceAlign);
     s.off_keys = off;     off = align_up(off + B * nk * sizeof(uint32_t), kWorkspaceAlign);
     s.off_pooled = off;   off = align_up(off + B * (size_t)c.num_heads_kv * nk * sizeof(float), kWorkspaceAlign);
+    s.off_hs = off;       off = align_up(off + B * HC * nk * sizeof(float), kWorkspaceAlign);
+    s.off_qmax = off;     off = align_up(off + B * HC * R * s.ntiles * 4 * sizeof(float), kWorkspaceAlign);
     s.ws_bytes = off;
     return s;
 }

@@ -16,11 +16,16 @@ struct EvictArgs {
     int k_head_rows;  // rows per KV head in K (len_k, or nk when compacted)
     int head_begin, head_count;
     float inv_sqrt_d;
-    float* logits;      // [batch][head_count][R][nk]; the tensor-core engine keeps head scores [batch][head_count][nk] here
+    float* logits;      // [batch][head_count][R][nk]; the per-tile tensor-core engine keeps head scores [batch][head_count][nk]
+                        // here; the persistent one keeps exp(l - quarter max) [batch][head_count][R][nkp] here
+    int nkp;            // nk rounded up to 4 (16-byte rows of the persistent engine's exp values)
+    float* hs;          // [batch][head_count][nk] head scores of the persistent tensor-core engine
+    float* qmax;        // [batch][head_count][R][ntiles][4] per-(row, tile, 32-key quarter) logit max
     float2* tstats;     // [batch][head_count][R][ntiles]  (tile max, tile sum)
     float2* rstats;     // [batch][head_count][R]          (row max, 1/(sum+1e-9))
     unsigned* counters; // [batch][head_count]
     int* err;           // workspace error word (bounded in-kernel waits)
+    unsigned* gbar;     // workspace word after it: the grid barrier of the one-launch tensor-core scorer
 };
 
 struct PoolArgs {
@@ -44,7 +49,8 @@ struct SelectArgs {
 struct EvictShape {
     int G, obs_w, nk, R, ntiles, target_keep;
     bool keep_all;
-    size_t off_counters, off_rstats, off_tstats, off_logits, off_keys, off_pooled, ws_bytes;
+    int nkp;
+    size_t off_counters, off_rstats, off_tstats, off_logits, off_keys, off_pooled, off_hs, off_qmax, ws_bytes;
 };
 
 EvictShape evict_shape(const rkv_config& c, int len_q, int len_k, int batch, int head_count);
@@ -53,6 +59,11 @@ int launch_evict_scores(const EvictArgs& a, int batch, cudaStream_t st);
 // tcgen05 scoring (evict_mma.cu): statistics, then head scores for the pool kernel (hs_direct)
 bool evict_mma_supported(const EvictArgs& a);
 int launch_evict_mma(const EvictArgs& a, int batch, cudaStream_t st);
+// row max and 1 / (sum + 1e-9) from the per-tile statistics (both tensor-core scorers)
+int launch_evict_fold(const EvictArgs& a, int batch, cudaStream_t st);
+// persistent warp-specialised tcgen05 scoring (evict_tc.cu): fp32, bf16, q8_0 (D = 128), G * obs_w <= 128
+bool evict_tc_supported(const EvictArgs& a, int batch);
+int launch_evict_tc(const EvictArgs& a, int batch, cudaStream_t st);
 int launch_evict_pool(const PoolArgs& a, int batch, cudaStream_t st);
 int launch_evict_select(const SelectArgs& a, int batch, cudaStream_t st);
 int launch_evict_keep_all(int* kept, int kept_stride, int* n_kept, int len_k, int batch, cudaStream_t st);

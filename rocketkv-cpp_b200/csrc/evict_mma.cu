@@ -24,6 +24,7 @@
 //           hs[k] = sum_r exp(l[r][k] - M_r) * inv_r in row order, written
 //           for the pooling kernel (the logits are never stored).
 #include "evict.cuh"
+#include "tc_common.cuh"
 
 #include <float.h>
 
@@ -34,81 +35,6 @@ constexpr int kMT = 128;       // keys per tile: the MMA's M
 constexpr int kMmaNT = 128;    // threads: warp w reads tensor-memory lanes 32w .. 32w+31
 constexpr int kSliceB = 64;    // bytes of every row staged per slice (four 16-byte K units, two MMA K steps)
 constexpr int kTB = 129;       // row stride (floats) of the statistics transpose buffer
-
-// ---- tcgen05 / tensor memory (PTX ISA 8.7) --------------------------------
-// Shared-memory matrix descriptor: K-major, no swizzle.  lbo = bytes between
-// the two 16-byte K units one MMA reads, sbo = bytes between 8-row groups;
-// bits 46-47 = 1 (the sm_100 descriptor version).
-__device__ __forceinline__ uint64_t mma_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
-    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
-           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
-}
-
-// Instruction descriptor: fp32 accumulator, K-major A and B, M = 128.
-// fmt: 2 = TF32, 1 = BF16 (both operands).
-__host__ __device__ constexpr uint32_t mma_idesc(uint32_t fmt, uint32_t n) {
-    return (1u << 4) | (fmt << 7) | (fmt << 10) | ((n >> 3) << 17) | ((uint32_t)(kMT >> 4) << 24);
-}
-
-__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {  // one full warp
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
-                 "r"(ncols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {  // the allocating warp
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-template <bool TF32>
-__device__ __forceinline__ void mma_issue(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-    if (TF32)
-        asm volatile(
-            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-            "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
-            "l"(a), "l"(b), "r"(idesc), "r"(acc)
-            : "memory");
-    else
-        asm volatile(
-            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
-            "l"(a), "l"(b), "r"(idesc), "r"(acc)
-            : "memory");
-}
-// Arrives on `bar` once every MMA this thread issued before it has completed.
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                     smem_u32(bar))
-                 : "memory");
-}
-// 32 consecutive accumulator columns of this thread's lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-    uint32_t r[32];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
-        "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
-          "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
-          "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr)
-        : "memory");
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// hi: x with the low 13 mantissa bits cleared (the TF32 value); lo = x - hi (exact).
-__device__ __forceinline__ void split_tf32(const uint4& x, uint4& hi, uint4& lo) {
-    hi = make_uint4(x.x & 0xFFFFE000u, x.y & 0xFFFFE000u, x.z & 0xFFFFE000u, x.w & 0xFFFFE000u);
-    lo = make_uint4(__float_as_uint(__fsub_rn(__uint_as_float(x.x), __uint_as_float(hi.x))),
-                    __float_as_uint(__fsub_rn(__uint_as_float(x.y), __uint_as_float(hi.y))),
-                    __float_as_uint(__fsub_rn(__uint_as_float(x.z), __uint_as_float(hi.z))),
-                    __float_as_uint(__fsub_rn(__uint_as_float(x.w), __uint_as_float(hi.w))));
-}
 
 struct MmaLayout {  // shared-memory offsets, the same on host and device
     int NP, slices, upr, kb, qb, buf, bars, epi, total;
@@ -364,13 +290,17 @@ int launch_t(const EvictArgs& a, int batch, cudaStream_t st) {
     dim3 grid(a.ntiles, a.head_count, batch);
     f0<<<grid, kMmaNT, s0, st>>>(a);
     if (cudaGetLastError() != cudaSuccess) return RKV_ERR_CUDA;
-    evict_fold_kernel<<<dim3((a.R + kFoldRows - 1) / kFoldRows, a.head_count, batch), kFoldRows * 32, 0, st>>>(a);
-    if (cudaGetLastError() != cudaSuccess) return RKV_ERR_CUDA;
+    if (launch_evict_fold(a, batch, st) != RKV_OK) return RKV_ERR_CUDA;
     f1<<<grid, kMmaNT, s1, st>>>(a);
     return cudaGetLastError() == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
 }
 
 }  // namespace
+
+int launch_evict_fold(const EvictArgs& a, int batch, cudaStream_t st) {
+    evict_fold_kernel<<<dim3((a.R + kFoldRows - 1) / kFoldRows, a.head_count, batch), kFoldRows * 32, 0, st>>>(a);
+    return cudaGetLastError() == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
+}
 
 bool evict_mma_supported(const EvictArgs& a) {
     if (a.dtype != RKV_F32 && a.dtype != RKV_BF16) return false;

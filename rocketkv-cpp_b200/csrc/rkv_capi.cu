@@ -119,23 +119,39 @@ EvictArgs make_evict_args(const void* Q, const void* K, int dtype, int len_q, in
     a.head_count = head_count;
     a.inv_sqrt_d = 1.0f / sqrtf((float)c.dim_head);
     a.logits = reinterpret_cast<float*>(ws + s.off_logits);
+    a.nkp = s.nkp;
+    a.hs = reinterpret_cast<float*>(ws + s.off_hs);
+    a.qmax = reinterpret_cast<float*>(ws + s.off_qmax);
     a.tstats = reinterpret_cast<float2*>(ws + s.off_tstats);
     a.rstats = reinterpret_cast<float2*>(ws + s.off_rstats);
     a.counters = reinterpret_cast<unsigned*>(ws + s.off_counters);
     a.err = reinterpret_cast<int*>(ws);
+    a.gbar = reinterpret_cast<unsigned*>(ws + sizeof(int));
     return a;
 }
 
 int evict_run(const EvictArgs& a, const rkv_config& c, const EvictShape& s, int batch, uint8_t* ws,
               float* pooled_out, int* kept, int kept_stride, int* n_kept, int engine, cudaStream_t st) {
-    const bool tensor = engine != RKV_EVICT_SIMT && evict_mma_supported(a);
-    if (engine == RKV_EVICT_TENSOR && !tensor) return RKV_ERR_UNSUPPORTED;
-    if (cudaMemsetAsync(a.err, 0, sizeof(int), st) != cudaSuccess) return RKV_ERR_CUDA;
-    int rc = tensor ? launch_evict_mma(a, batch, st) : launch_evict_scores(a, batch, st);
-    if (rc) return rc;
+    if (cudaMemsetAsync(a.err, 0, sizeof(int) + sizeof(unsigned), st) != cudaSuccess) return RKV_ERR_CUDA;  // error word, grid barrier
+    // engine chain: persistent tensor-core kernel, per-tile tensor-core kernel, CUDA cores
+    bool tensor = false, persistent = false;
+    int rc = RKV_OK;
+    if ((engine == RKV_EVICT_AUTO || engine == RKV_EVICT_TENSOR) && evict_tc_supported(a, batch)) {
+        rc = launch_evict_tc(a, batch, st);
+        if (rc != RKV_OK && rc != RKV_ERR_UNSUPPORTED) return rc;
+        tensor = persistent = rc == RKV_OK;
+    }
+    if (!tensor && engine != RKV_EVICT_SIMT && evict_mma_supported(a)) {
+        if ((rc = launch_evict_mma(a, batch, st))) return rc;
+        tensor = true;
+    }
+    if (!tensor) {
+        if (engine == RKV_EVICT_TENSOR || engine == RKV_EVICT_TENSOR_TILES) return RKV_ERR_UNSUPPORTED;
+        if ((rc = launch_evict_scores(a, batch, st))) return rc;
+    }
     PoolArgs p{};
     p.hs_direct = tensor ? 1 : 0;
-    p.logits = a.logits;
+    p.logits = persistent ? a.hs : a.logits;
     p.rstats = a.rstats;
     p.R = s.R;
     p.nk = s.nk;
@@ -251,7 +267,7 @@ int rkv_evict(const void* Q, const void* K, int dtype, int len_q, int len_k, int
               long long q_item_stride, long long k_item_stride, const rkv_config* cfg, int* kept,
               int kept_stride, int* n_kept, void* workspace, size_t workspace_bytes, int engine,
               void* stream) {
-    if (engine < RKV_EVICT_AUTO || engine > RKV_EVICT_TENSOR) return RKV_ERR_INVALID_ARG;
+    if (engine < RKV_EVICT_AUTO || engine > RKV_EVICT_TENSOR_TILES) return RKV_ERR_INVALID_ARG;
     if (check_cfg(cfg)) return RKV_ERR_INVALID_ARG;
     const EvictShape s = evict_shape(*cfg, len_q, len_k, batch, cfg->num_heads_kv);
     int rc = evict_validate(Q, K, dtype, len_q, len_k, batch, cfg, s);
@@ -271,7 +287,7 @@ int rkv_evict_pool_heads(const void* Q, const void* K, int dtype, int len_q, int
                          long long q_item_stride, long long k_item_stride, const rkv_config* cfg,
                          int head_begin, int head_count, float* pooled, void* workspace,
                          size_t workspace_bytes, int engine, void* stream) {
-    if (engine < RKV_EVICT_AUTO || engine > RKV_EVICT_TENSOR) return RKV_ERR_INVALID_ARG;
+    if (engine < RKV_EVICT_AUTO || engine > RKV_EVICT_TENSOR_TILES) return RKV_ERR_INVALID_ARG;
     if (check_cfg(cfg)) return RKV_ERR_INVALID_ARG;
     if (head_begin < 0 || head_count < 0 || head_begin + head_count > cfg->num_heads_kv) return RKV_ERR_INVALID_ARG;
     EvictShape s = evict_shape(*cfg, len_q, len_k, batch, head_count);

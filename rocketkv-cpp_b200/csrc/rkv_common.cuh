@@ -78,6 +78,38 @@ __device__ __forceinline__ float det_expf(float x) {
     return x != x ? x : out;
 }
 
+// det_expf on two values at once with the packed fp32x2 operations of
+// sm_100: the same operation sequence per lane, so each lane's result equals
+// det_expf of it bit for bit (t - magic is exact; fma(-n, c, r) equals
+// fma(n, -c, r)).
+__device__ __forceinline__ float2 det_expf2(float2 x) {
+    const float log2e = __int_as_float(0x3fb8aa3b);
+    const float magic = __int_as_float(0x4b400000);
+    const float2 xc = make_float2(fmaxf(x.x, -104.0f), fmaxf(x.y, -104.0f));
+    const float2 t = __ffma2_rn(xc, make_float2(log2e, log2e), make_float2(magic, magic));
+    const float2 n = __fadd2_rn(t, make_float2(-magic, -magic));
+    const float nh = -__int_as_float(0x3f317000), nl = -__int_as_float(0x3805fdf4);
+    float2 r = __ffma2_rn(n, make_float2(nh, nh), xc);
+    r = __ffma2_rn(n, make_float2(nl, nl), r);
+    float2 p = make_float2(__int_as_float(0x39500d01), __int_as_float(0x39500d01));
+    p = __ffma2_rn(p, r, make_float2(__int_as_float(0x3ab60b61), __int_as_float(0x3ab60b61)));
+    p = __ffma2_rn(p, r, make_float2(__int_as_float(0x3c088889), __int_as_float(0x3c088889)));
+    p = __ffma2_rn(p, r, make_float2(__int_as_float(0x3d2aaaab), __int_as_float(0x3d2aaaab)));
+    p = __ffma2_rn(p, r, make_float2(__int_as_float(0x3e2aaaab), __int_as_float(0x3e2aaaab)));
+    p = __ffma2_rn(p, r, make_float2(0.5f, 0.5f));
+    p = __ffma2_rn(p, r, make_float2(1.0f, 1.0f));
+    p = __ffma2_rn(p, r, make_float2(1.0f, 1.0f));
+    const int nx = __float_as_int(t.x) - 0x4b400000, ny = __float_as_int(t.y) - 0x4b400000;
+    const float2 sc = make_float2(__int_as_float((nx + 64 + 127) << 23), __int_as_float((ny + 64 + 127) << 23));
+    const float m64 = __int_as_float(0x1f800000);
+    const float2 res = __fmul2_rn(__fmul2_rn(p, sc), make_float2(m64, m64));
+    const float lim = -103.97208404541015625f;
+    float2 out;
+    out.x = x.x != x.x ? x.x : (x.x < lim ? 0.0f : res.x);
+    out.y = x.y != x.y ? x.y : (x.y < lim ? 0.0f : res.y);
+    return out;
+}
+
 // Order-preserving map float -> uint32 (larger float, larger key).
 __device__ __forceinline__ uint32_t float_key(float f) {
     const uint32_t b = __float_as_uint(f);

@@ -27,7 +27,7 @@ RKV_ERR_DEVICE_TIMEOUT = 5
 RKV_ERR_NO_DEVICE = 6
 
 F32, BF16, Q8_0 = 0, 1, 2
-ENGINE_AUTO, ENGINE_SIMT, ENGINE_TENSOR = 0, 1, 2
+ENGINE_AUTO, ENGINE_SIMT, ENGINE_TENSOR, ENGINE_TENSOR_TILES = 0, 1, 2, 3
 
 # Every symbol include/rkv.h declares.
 EXPORTS = [

@@ -44,11 +44,12 @@ def test_stage1_cases(name, cuda):
     assert len(got) == len(ref) and len({float(total[i]) for i in diff}) <= 1
 
 
-@pytest.mark.parametrize("name", ["s1_basic", "s1_bf16", "s1_shortq", "s1_mha_ks1", "s1_evenks"])
-def test_stage1_tensor_engine_matches_cuda_cores(name, cuda):
-    """tcgen05 scoring (fp32 as three TF32 products, bf16 direct) against the
-    fp32 CUDA-core engine on the same inputs: pooled rows within 1e-4
-    relative, kept indices identical."""
+@pytest.mark.parametrize("name", ["s1_basic", "s1_bf16", "s1_shortq", "s1_mha_ks1", "s1_evenks", "s1_q8", "s1_needle"])
+def test_stage1_tensor_engines_match_cuda_cores(name, cuda):
+    """The tcgen05 scorers (the persistent kernel, and for fp32/bf16 the
+    per-tile kernel; fp32 and q8_0 as three TF32 products per step, bf16
+    direct) against the fp32 CUDA-core engine on the same inputs: pooled rows
+    within 1e-4 relative, kept indices identical."""
     import torch
     p = dict(cases.STAGE1)[name]
     Q, K, (kind, Qd, Kd) = cases.stage1_build(p)
@@ -57,18 +58,20 @@ def test_stage1_tensor_engine_matches_cuda_cores(name, cuda):
     Kt = dev(Kd, kind, cuda).unsqueeze(0).contiguous()
     ev = rkv.Evictor(cfg, p["len_q"], p["len_k"], 1, KIND[kind], cuda)
     nk = p["len_k"] - min(p["window"], p["len_q"])
+    engines = [rkv.ENGINE_TENSOR, rkv.ENGINE_SIMT] + ([rkv.ENGINE_TENSOR_TILES] if kind != "q8_0" else [])
     pooled = {}
-    for eng in (rkv.ENGINE_TENSOR, rkv.ENGINE_SIMT):
+    for eng in engines:
         out = torch.empty((1, p["HK"], nk), dtype=torch.float32, device=cuda)
         ev.pool_heads(Qt, Kt, 0, p["HK"], out, engine=eng)
         torch.cuda.synchronize()
         pooled[eng] = out[0].cpu().numpy()
-    np.testing.assert_allclose(pooled[rkv.ENGINE_TENSOR], pooled[rkv.ENGINE_SIMT], rtol=1e-4, atol=1e-7)
     kept = {}
-    for eng in (rkv.ENGINE_TENSOR, rkv.ENGINE_SIMT):
+    for eng in engines:
         k, n = ev(Qt, Kt, engine=eng)
         kept[eng] = k[0, : int(n[0])].cpu().numpy().copy()
-    np.testing.assert_array_equal(kept[rkv.ENGINE_TENSOR], kept[rkv.ENGINE_SIMT])
+    for eng in engines:
+        np.testing.assert_allclose(pooled[eng], pooled[rkv.ENGINE_SIMT], rtol=1e-4, atol=1e-7, err_msg=str(eng))
+        np.testing.assert_array_equal(kept[eng], kept[rkv.ENGINE_SIMT], err_msg=str(eng))
     assert rkv.lib().rkv_workspace_status(rkv._ptr(ev.ws), 0) == 0
 
 
