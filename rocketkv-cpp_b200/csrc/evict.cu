@@ -276,6 +276,167 @@ __global__ void __launch_bounds__(kSelNT) evict_select_kernel(SelectArgs a) {
     if (tid == 0) a.n_kept[b] = a.target_keep + a.obs_w;
 }
 
+// The same selection with every key in registers (up to kSelPer consecutive
+// keys per thread, nk <= 16384): the head-order sum, a radix select in
+// digits of up to 8 bits that starts below the bits every key shares (the
+// common prefix of the block's min and max key: the pooled sums share their
+// sign and top exponent bits, which would put every key of a first 8-bit
+// digit into one or two bins), one warp scanning the bins, and one dual
+// block scan for the stable compaction (position of a kept key = keys above
+// the threshold before it + min(threshold keys before it, the number of
+// threshold keys kept)).
+constexpr int kSelPer = 16;
+__global__ void __launch_bounds__(kSelNT) evict_select_reg_kernel(SelectArgs a) {
+    __shared__ int hist[256];
+    __shared__ int scan_tmp[66];
+    __shared__ uint32_t s_prefix, s_lo[32], s_hi[32];
+    __shared__ int s_kk;
+    const int tid = threadIdx.x, b = blockIdx.x, lane = tid & 31, warp = tid >> 5;
+    int* kept = a.kept + (size_t)b * a.kept_stride;
+    int C = (a.nk + kSelNT - 1) / kSelNT;
+    const bool vec = (a.nk & 3) == 0;
+    if (vec) C = (C + 3) & ~3;  // whole 16-byte groups per thread
+    const int i0 = tid * C;
+    // total = sum of the HK pooled rows in head order (rocket.cpp:143-146)
+    float v[kSelPer];
+#pragma unroll
+    for (int j = 0; j < kSelPer; ++j) v[j] = 0.0f;
+    if (vec) {
+        for (int h0 = 0; h0 < a.HK; h0 += 2) {  // two heads' loads in flight at once
+            float4 x[2][kSelPer / 4];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const float4* row = reinterpret_cast<const float4*>(a.pooled + ((size_t)b * a.HK + h0 + u) * a.nk + i0);
+#pragma unroll
+                for (int g = 0; g < kSelPer / 4; ++g)
+                    x[u][g] = (h0 + u < a.HK && 4 * g < C && i0 + 4 * g < a.nk) ? __ldg(row + g) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                if (h0 + u >= a.HK) break;
+#pragma unroll
+                for (int g = 0; g < kSelPer / 4; ++g) {
+                    v[4 * g] = __fadd_rn(v[4 * g], x[u][g].x);
+                    v[4 * g + 1] = __fadd_rn(v[4 * g + 1], x[u][g].y);
+                    v[4 * g + 2] = __fadd_rn(v[4 * g + 2], x[u][g].z);
+                    v[4 * g + 3] = __fadd_rn(v[4 * g + 3], x[u][g].w);
+                }
+            }
+        }
+    } else {
+        for (int h = 0; h < a.HK; ++h) {
+            const float* row = a.pooled + ((size_t)b * a.HK + h) * a.nk + i0;
+            float x[kSelPer];
+#pragma unroll
+            for (int j = 0; j < kSelPer; ++j) x[j] = (j < C && i0 + j < a.nk) ? __ldg(row + j) : 0.0f;
+#pragma unroll
+            for (int j = 0; j < kSelPer; ++j) v[j] = __fadd_rn(v[j], x[j]);
+        }
+    }
+    uint32_t key[kSelPer];
+    uint32_t valid = 0u, kmin = 0xffffffffu, kmax = 0u;
+#pragma unroll
+    for (int j = 0; j < kSelPer; ++j) {
+        key[j] = float_key(v[j]);
+        if (j < C && i0 + j < a.nk) {
+            valid |= 1u << j;
+            kmin = min(kmin, key[j]);
+            kmax = max(kmax, key[j]);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+        kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+    }
+    if (lane == 0) {
+        s_lo[warp] = kmin;
+        s_hi[warp] = kmax;
+    }
+    __syncthreads();
+    kmin = s_lo[lane];
+    kmax = s_hi[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+        kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+    }
+    // bits below the common prefix of every key
+    const uint32_t diff = kmin ^ kmax;
+    int rem = diff ? 32 - __clz(diff) : 0;
+    uint32_t mask = rem == 32 ? 0u : ~((1u << rem) - 1u);
+    if (tid == 0) {
+        s_prefix = kmax & mask;
+        s_kk = a.target_keep;
+    }
+    __syncthreads();
+    // radix select of the target_keep-th largest key, digits of up to 8 bits from the top
+    while (rem > 0 && a.target_keep > 0) {
+        const int w = rem < 8 ? rem : 8, shift = rem - w, nb = 1 << w;
+        if (tid < 256) hist[tid] = 0;
+        __syncthreads();
+        const uint32_t prefix = s_prefix;
+#pragma unroll
+        for (int j = 0; j < kSelPer; ++j)
+            if (((valid >> j) & 1u) && (key[j] & mask) == prefix) atomicAdd(&hist[(key[j] >> shift) & (uint32_t)(nb - 1)], 1);
+        __syncthreads();
+        if (warp == 0) {  // the digit where the count from the top reaches kk; lane L: digits nb-1-8L ..
+            int c[8], sum = 0;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                const int idx = 8 * lane + t;
+                c[t] = idx < nb ? hist[nb - 1 - idx] : 0;
+                sum += c[t];
+            }
+            int incl = sum;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            int before = incl - sum;
+            const int kk = s_kk;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                if (c[t] > 0 && before < kk && before + c[t] >= kk) {
+                    s_kk = kk - before;
+                    s_prefix = prefix | ((uint32_t)(nb - 1 - (8 * lane + t)) << shift);
+                }
+                before += c[t];
+            }
+        }
+        mask |= (uint32_t)(nb - 1) << shift;
+        rem = shift;
+        __syncthreads();
+    }
+    const uint32_t T = a.target_keep > 0 ? s_prefix : 0xffffffffu;
+    const int need = a.target_keep > 0 ? s_kk : 0;  // threshold-key members kept, lowest index first
+    int gt = 0, eq = 0;
+#pragma unroll
+    for (int j = 0; j < kSelPer; ++j)
+        if ((valid >> j) & 1u) {
+            gt += key[j] > T ? 1 : 0;
+            eq += key[j] == T ? 1 : 0;
+        }
+    int gt_before, eq_tot, gt_tot;
+    const int eq_before = block_exclusive_scan2(eq, gt, scan_tmp, &gt_before, &eq_tot, &gt_tot);
+    if (a.target_keep > 0) {
+        int pos = gt_before + min(eq_before, need), e = eq_before;
+#pragma unroll
+        for (int j = 0; j < kSelPer; ++j) {
+            if (!((valid >> j) & 1u)) continue;
+            if (key[j] > T) {
+                kept[pos++] = i0 + j;
+            } else if (key[j] == T) {
+                if (e < need) kept[pos++] = i0 + j;
+                ++e;
+            }
+        }
+    }
+    for (int t = tid; t < a.obs_w; t += kSelNT) kept[a.target_keep + t] = a.nk + t;
+    if (tid == 0) a.n_kept[b] = a.target_keep + a.obs_w;
+}
+
 __global__ void evict_keep_all_kernel(int* kept, int kept_stride, int* n_kept, int len_k) {
     const int b = blockIdx.y;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < len_k; i += gridDim.x * blockDim.x)
@@ -383,7 +544,10 @@ int launch_evict_pool(const PoolArgs& in, int batch, cudaStream_t st) {
 }
 
 int launch_evict_select(const SelectArgs& a, int batch, cudaStream_t st) {
-    evict_select_kernel<<<batch, kSelNT, 0, st>>>(a);
+    if (a.nk <= kSelNT * kSelPer)
+        evict_select_reg_kernel<<<batch, kSelNT, 0, st>>>(a);
+    else
+        evict_select_kernel<<<batch, kSelNT, 0, st>>>(a);
     return cudaGetLastError() == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
 }
 
