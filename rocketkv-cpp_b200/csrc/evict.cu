@@ -213,64 +213,114 @@ __global__ void __launch_bounds__(kNT) evict_pool_kernel(PoolArgs a) {
 
 __global__ void __launch_bounds__(kSelNT) evict_select_kernel(SelectArgs a) {
     __shared__ int hist[256];
-    __shared__ int scan_tmp[33];
-    __shared__ uint32_t s_prefix;
+    __shared__ int scan_tmp[66];
+    __shared__ uint32_t s_prefix, s_lo[32], s_hi[32];
     __shared__ int s_kk;
-    const int tid = threadIdx.x, b = blockIdx.x;
+    const int tid = threadIdx.x, b = blockIdx.x, lane = tid & 31, warp = tid >> 5;
     uint32_t* keys = a.keys + (size_t)b * a.nk;
     int* kept = a.kept + (size_t)b * a.kept_stride;
 
-    // total = sum of the HK pooled rows in head order (rocket.cpp:143-146)
+    // total = sum of the HK pooled rows in head order (rocket.cpp:143-146), as order-preserving keys
+    uint32_t kmin = 0xffffffffu, kmax = 0u;
     for (int i = tid; i < a.nk; i += kSelNT) {
         float v = 0.0f;
         for (int h = 0; h < a.HK; ++h) v = __fadd_rn(v, a.pooled[((size_t)b * a.HK + h) * a.nk + i]);
-        keys[i] = float_key(v);
+        const uint32_t k = float_key(v);
+        keys[i] = k;
+        kmin = min(kmin, k);
+        kmax = max(kmax, k);
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+        kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+    }
+    if (lane == 0) {
+        s_lo[warp] = kmin;
+        s_hi[warp] = kmax;
+    }
+    __syncthreads();
+    kmin = s_lo[lane];
+    kmax = s_hi[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+        kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+    }
+    // radix select of the target_keep-th largest key in digits of up to 8 bits, starting below the
+    // bits every key shares (as in evict_select_reg_kernel)
+    const uint32_t diff = kmin ^ kmax;
+    int rem = diff ? 32 - __clz(diff) : 0;
+    uint32_t mask = rem == 32 ? 0u : ~((1u << rem) - 1u);
     if (tid == 0) {
-        s_prefix = 0u;
+        s_prefix = kmax & mask;
         s_kk = a.target_keep;
     }
     __syncthreads();
-
-    // 4 x 8-bit radix select of the target_keep-th largest key.
-    uint32_t mask = 0u;
-    for (int shift = 24; shift >= 0 && a.target_keep > 0; shift -= 8) {
-        for (int i = tid; i < 256; i += kSelNT) hist[i] = 0;
+    while (rem > 0 && a.target_keep > 0) {
+        const int w = rem < 8 ? rem : 8, shift = rem - w, nb = 1 << w;
+        if (tid < 256) hist[tid] = 0;
         __syncthreads();
         const uint32_t prefix = s_prefix;
-        const int kk = s_kk;
         for (int i = tid; i < a.nk; i += kSelNT) {
             const uint32_t k = keys[i];
-            if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1);
+            if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & (uint32_t)(nb - 1)], 1);
         }
         __syncthreads();
-        // counts from the top digit down; the digit where the running count reaches kk
-        const int v = tid < 256 ? hist[255 - tid] : 0;
-        int tot;
-        const int before = block_exclusive_scan(v, scan_tmp, &tot);
-        if (tid < 256 && before < kk && before + v >= kk) {
-            s_kk = kk - before;
-            s_prefix = prefix | ((uint32_t)(255 - tid) << shift);
+        if (warp == 0) {
+            int c[8], sum = 0;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                const int idx = 8 * lane + t;
+                c[t] = idx < nb ? hist[nb - 1 - idx] : 0;
+                sum += c[t];
+            }
+            int incl = sum;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            int before = incl - sum;
+            const int kk = s_kk;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                if (c[t] > 0 && before < kk && before + c[t] >= kk) {
+                    s_kk = kk - before;
+                    s_prefix = prefix | ((uint32_t)(nb - 1 - (8 * lane + t)) << shift);
+                }
+                before += c[t];
+            }
         }
-        mask |= 255u << shift;
+        mask |= (uint32_t)(nb - 1) << shift;
+        rem = shift;
         __syncthreads();
     }
     const uint32_t T = a.target_keep > 0 ? s_prefix : 0xffffffffu;
     const int need = a.target_keep > 0 ? s_kk : 0;  // threshold-key members kept, lowest index first
 
-    int eq_base = 0, keep_base = 0;
-    for (int i0 = 0; i0 < a.nk && a.target_keep > 0; i0 += kSelNT) {
-        const int i = i0 + tid;
-        const uint32_t k = i < a.nk ? keys[i] : 0u;
-        const int eq = (i < a.nk && k == T) ? 1 : 0;
-        int eq_tot;
-        const int eq_rank = eq_base + block_exclusive_scan(eq, scan_tmp, &eq_tot);
-        const int keep = (i < a.nk && (k > T || (eq && eq_rank < need))) ? 1 : 0;
-        int keep_tot;
-        const int pos = keep_base + block_exclusive_scan(keep, scan_tmp, &keep_tot);
-        if (keep) kept[pos] = i;
-        eq_base += eq_tot;
-        keep_base += keep_tot;
+    // stable compaction: each thread a contiguous chunk, one dual block scan
+    const int C = (a.nk + kSelNT - 1) / kSelNT;
+    const int i0 = tid * C, i1 = min(i0 + C, a.nk);
+    int gt = 0, eq = 0;
+    for (int i = i0; i < i1; ++i) {
+        const uint32_t k = keys[i];
+        gt += k > T ? 1 : 0;
+        eq += k == T ? 1 : 0;
+    }
+    int gt_before, eq_tot, gt_tot;
+    const int eq_before = block_exclusive_scan2(eq, gt, scan_tmp, &gt_before, &eq_tot, &gt_tot);
+    if (a.target_keep > 0) {
+        int pos = gt_before + min(eq_before, need), e = eq_before;
+        for (int i = i0; i < i1; ++i) {
+            const uint32_t k = keys[i];
+            if (k > T) {
+                kept[pos++] = i;
+            } else if (k == T) {
+                if (e < need) kept[pos++] = i;
+                ++e;
+            }
+        }
     }
     for (int t = tid; t < a.obs_w; t += kSelNT) kept[a.target_keep + t] = a.nk + t;
     if (tid == 0) a.n_kept[b] = a.target_keep + a.obs_w;
@@ -437,6 +487,183 @@ __global__ void __launch_bounds__(kSelNT) evict_select_reg_kernel(SelectArgs a) 
     if (tid == 0) a.n_kept[b] = a.target_keep + a.obs_w;
 }
 
+// The selection of long prefixes over several CTAs per item (one cooperative
+// launch, every CTA resident): each CTA holds a contiguous chunk of up to
+// kCoopNT * kSelPer keys in registers; the key range (min, max), the radix
+// histograms and the per-CTA counts are merged in the workspace, and every
+// CTA of an item takes the same digit decision from the merged histogram
+// after a bounded grid barrier.  Workspace words (zeroed before the launch):
+// [0] the barrier counter, then per item ~min and max, 4 x 256 histogram
+// bins, and per CTA the (above, equal) threshold counts.
+constexpr int kCoopNT = 512;
+struct SelCoop {
+    unsigned* bar;
+    unsigned* mm;  // [item][2]: ~min, max (atomicMax of both)
+    int* hist;     // [item][4][256]
+    int* cnt;      // [item][P][2]
+    int P, chunk;
+};
+
+__global__ void __launch_bounds__(kCoopNT) evict_select_coop_kernel(SelectArgs a, SelCoop c) {
+    __shared__ int hist[256];
+    __shared__ int scan_tmp[66];
+    __shared__ uint32_t s_lo[16], s_hi[16], s_prefix;
+    __shared__ int s_kk, s_ok, s_pre[2];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int b = blockIdx.x / c.P, p = blockIdx.x % c.P;
+    const int base = p * c.chunk, end = min(base + c.chunk, a.nk);
+    const int C = (c.chunk + kCoopNT - 1) / kCoopNT;  // <= kSelPer
+    const int i0 = base + tid * C;
+    unsigned nbar = 0;
+    auto gsync = [&]() -> bool {  // grid barrier; false once any CTA's wait has run out
+        __syncthreads();
+        if (tid == 0) s_ok = grid_sync_bounded(c.bar, (++nbar) * gridDim.x, a.err) ? 1 : 0;
+        else ++nbar;
+        __syncthreads();
+        return s_ok != 0;
+    };
+    // total = sum of the HK pooled rows in head order (rocket.cpp:143-146)
+    float v[kSelPer];
+#pragma unroll
+    for (int j = 0; j < kSelPer; ++j) v[j] = 0.0f;
+    for (int h = 0; h < a.HK; ++h) {
+        const float* row = a.pooled + ((size_t)b * a.HK + h) * a.nk + i0;
+        float x[kSelPer];
+#pragma unroll
+        for (int j = 0; j < kSelPer; ++j) x[j] = (j < C && i0 + j < end) ? __ldg(row + j) : 0.0f;
+#pragma unroll
+        for (int j = 0; j < kSelPer; ++j) v[j] = __fadd_rn(v[j], x[j]);
+    }
+    uint32_t key[kSelPer], valid = 0u, kmin = 0xffffffffu, kmax = 0u;
+#pragma unroll
+    for (int j = 0; j < kSelPer; ++j) {
+        key[j] = float_key(v[j]);
+        if (j < C && i0 + j < end) {
+            valid |= 1u << j;
+            kmin = min(kmin, key[j]);
+            kmax = max(kmax, key[j]);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+        kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+    }
+    if (lane == 0) {
+        s_lo[warp] = kmin;
+        s_hi[warp] = kmax;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        for (int w = 1; w < kCoopNT / 32; ++w) {
+            kmin = min(kmin, s_lo[w]);
+            kmax = max(kmax, s_hi[w]);
+        }
+        atomicMax(&c.mm[2 * b], ~kmin);
+        atomicMax(&c.mm[2 * b + 1], kmax);
+    }
+    if (!gsync()) return;
+    kmin = ~__ldcg(&c.mm[2 * b]);
+    kmax = __ldcg(&c.mm[2 * b + 1]);
+    const uint32_t diff = kmin ^ kmax;
+    int rem = diff ? 32 - __clz(diff) : 0;
+    uint32_t mask = rem == 32 ? 0u : ~((1u << rem) - 1u);
+    uint32_t prefix = kmax & mask;
+    int kk = a.target_keep;
+    // every CTA of the grid takes the same four barrier rounds, whatever its item needs
+    for (int ps = 0; ps < 4; ++ps) {
+        const bool active = rem > 0 && a.target_keep > 0;  // uniform over the item's CTAs
+        const int w = rem < 8 ? rem : 8, shift = active ? rem - w : 0, nb = 1 << w;
+        int* gh = c.hist + ((size_t)b * 4 + ps) * 256;
+        if (active) {
+            if (tid < 256) hist[tid] = 0;
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < kSelPer; ++j)
+                if (((valid >> j) & 1u) && (key[j] & mask) == prefix)
+                    atomicAdd(&hist[(key[j] >> shift) & (uint32_t)(nb - 1)], 1);
+            __syncthreads();
+            if (tid < nb && hist[tid]) atomicAdd(&gh[tid], hist[tid]);
+        }
+        if (!gsync()) return;
+        if (!active) continue;
+        if (warp == 0) {  // the same decision in every CTA of the item, from the merged histogram
+            int cc[8], sum = 0;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                const int idx = 8 * lane + t;
+                cc[t] = idx < nb ? __ldcg(&gh[nb - 1 - idx]) : 0;
+                sum += cc[t];
+            }
+            int incl = sum;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            int before = incl - sum;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                if (cc[t] > 0 && before < kk && before + cc[t] >= kk) {
+                    s_kk = kk - before;
+                    s_prefix = prefix | ((uint32_t)(nb - 1 - (8 * lane + t)) << shift);
+                }
+                before += cc[t];
+            }
+        }
+        __syncthreads();
+        prefix = s_prefix;
+        kk = s_kk;
+        mask |= (uint32_t)(nb - 1) << shift;
+        rem = shift;
+    }
+    const uint32_t T = a.target_keep > 0 ? prefix : 0xffffffffu;
+    const int need = a.target_keep > 0 ? kk : 0;  // threshold-key members kept, lowest index first
+    int gt = 0, eq = 0;
+#pragma unroll
+    for (int j = 0; j < kSelPer; ++j)
+        if ((valid >> j) & 1u) {
+            gt += key[j] > T ? 1 : 0;
+            eq += key[j] == T ? 1 : 0;
+        }
+    int gt_before, eq_tot, gt_tot;
+    const int eq_before = block_exclusive_scan2(eq, gt, scan_tmp, &gt_before, &eq_tot, &gt_tot);
+    if (tid == 0) {
+        c.cnt[((size_t)b * c.P + p) * 2] = gt_tot;
+        c.cnt[((size_t)b * c.P + p) * 2 + 1] = eq_tot;
+    }
+    if (!gsync()) return;
+    if (tid == 0) {  // the counts of the item's CTAs before this one
+        int g0 = 0, e0 = 0;
+        for (int q = 0; q < p; ++q) {
+            g0 += __ldcg(&c.cnt[((size_t)b * c.P + q) * 2]);
+            e0 += __ldcg(&c.cnt[((size_t)b * c.P + q) * 2 + 1]);
+        }
+        s_pre[0] = g0;
+        s_pre[1] = e0;
+    }
+    __syncthreads();
+    int* kept = a.kept + (size_t)b * a.kept_stride;
+    if (a.target_keep > 0) {
+        const int eb = s_pre[1] + eq_before;
+        int pos = s_pre[0] + gt_before + min(eb, need), e = eb;
+#pragma unroll
+        for (int j = 0; j < kSelPer; ++j) {
+            if (!((valid >> j) & 1u)) continue;
+            if (key[j] > T) {
+                kept[pos++] = i0 + j;
+            } else if (key[j] == T) {
+                if (e < need) kept[pos++] = i0 + j;
+                ++e;
+            }
+        }
+    }
+    if (p == 0) {
+        for (int t = tid; t < a.obs_w; t += kCoopNT) kept[a.target_keep + t] = a.nk + t;
+        if (tid == 0) a.n_kept[b] = a.target_keep + a.obs_w;
+    }
+}
+
 __global__ void evict_keep_all_kernel(int* kept, int kept_stride, int* n_kept, int len_k) {
     const int b = blockIdx.y;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < len_k; i += gridDim.x * blockDim.x)
@@ -544,10 +771,30 @@ int launch_evict_pool(const PoolArgs& in, int batch, cudaStream_t st) {
 }
 
 int launch_evict_select(const SelectArgs& a, int batch, cudaStream_t st) {
-    if (a.nk <= kSelNT * kSelPer)
+    if (a.nk <= kSelNT * kSelPer) {
         evict_select_reg_kernel<<<batch, kSelNT, 0, st>>>(a);
-    else
-        evict_select_kernel<<<batch, kSelNT, 0, st>>>(a);
+        return cudaGetLastError() == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
+    }
+    // long prefixes: several CTAs per item in one cooperative launch, bookkeeping in the keys region
+    SelCoop c{};
+    c.chunk = kCoopNT * kSelPer;
+    c.P = (a.nk + c.chunk - 1) / c.chunk;
+    const size_t words = 1 + 2 * (size_t)batch + 1024 * (size_t)batch + 2 * (size_t)c.P * batch;
+    if (a.err && words <= (size_t)batch * a.nk) {
+        c.bar = a.keys;
+        c.mm = a.keys + 1;
+        c.hist = reinterpret_cast<int*>(a.keys + 1 + 2 * (size_t)batch);
+        c.cnt = c.hist + 1024 * (size_t)batch;
+        if (cudaMemsetAsync(a.keys, 0, words * sizeof(uint32_t), st) != cudaSuccess) return RKV_ERR_CUDA;
+        SelectArgs aa = a;
+        void* args[] = {&aa, &c};
+        const cudaError_t e = cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(evict_select_coop_kernel),
+                                                          dim3(batch * c.P), dim3(kCoopNT), args, 0, st);
+        if (e == cudaSuccess) return RKV_OK;
+        (void)cudaGetLastError();
+        if (e != cudaErrorCooperativeLaunchTooLarge && e != cudaErrorNotSupported) return RKV_ERR_CUDA;
+    }
+    evict_select_kernel<<<batch, kSelNT, 0, st>>>(a);  // one CTA per item
     return cudaGetLastError() == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
 }
 

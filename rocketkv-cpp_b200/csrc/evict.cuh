@@ -44,6 +44,7 @@ struct SelectArgs {
     int* kept;
     int kept_stride;
     int* n_kept;
+    int* err;             // workspace error word (the bounded grid barrier of the multi-CTA selection)
 };
 
 struct EvictShape {

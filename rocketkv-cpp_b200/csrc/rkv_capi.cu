@@ -167,6 +167,7 @@ int evict_run(const EvictArgs& a, const rkv_config& c, const EvictShape& s, int 
     sa.obs_w = s.obs_w;
     sa.target_keep = s.target_keep;
     sa.keys = reinterpret_cast<uint32_t*>(ws + s.off_keys);
+    sa.err = a.err;
     sa.kept = kept;
     sa.kept_stride = kept_stride;
     sa.n_kept = n_kept;
@@ -322,6 +323,8 @@ int rkv_evict_select_pooled(const float* pooled, int len_q, int len_k, int batch
     sa.obs_w = s.obs_w;
     sa.target_keep = s.target_keep;
     sa.keys = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + s.off_keys);
+    sa.err = static_cast<int*>(workspace);
+    if (cudaMemsetAsync(sa.err, 0, sizeof(int), st) != cudaSuccess) return RKV_ERR_CUDA;
     sa.kept = kept;
     sa.kept_stride = kept_stride;
     sa.n_kept = n_kept;

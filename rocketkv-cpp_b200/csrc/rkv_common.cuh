@@ -195,6 +195,29 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     return true;
 }
 
+// Grid-wide barrier for cooperative launches (every CTA resident): arrive on
+// the counter, then wait until it reaches `target` (k * gridDim.x for the
+// k-th barrier of a launch; the counter starts at zero).  One thread per CTA
+// calls it between __syncthreads.  Bounded: a timeout records
+// RKV_ERR_DEVICE_TIMEOUT in *err and returns false.
+__device__ __forceinline__ bool grid_sync_bounded(unsigned* cnt, unsigned target, int* err) {
+    __threadfence();
+    atomicAdd(cnt, 1u);
+    const long long t0 = clock64();
+    for (;;) {
+        unsigned v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(cnt) : "memory");
+        if (v >= target) break;
+        if (clock64() - t0 > kWaitCycles) {
+            atomicExch(err, (int)RKV_ERR_DEVICE_TIMEOUT);
+            return false;
+        }
+        __nanosleep(100);
+    }
+    __threadfence();
+    return true;
+}
+
 // ---------------------------------------------------------------------------
 // Block-wide exclusive scan of one int per thread (blockDim.x threads,
 // blockDim.x a multiple of 32, at most 1024).  `tmp` holds 33 ints.

@@ -75,6 +75,32 @@ def test_stage1_tensor_engines_match_cuda_cores(name, cuda):
     assert rkv.lib().rkv_workspace_status(rkv._ptr(ev.ws), 0) == 0
 
 
+@pytest.mark.parametrize("kind", ["f32", "bf16"])
+def test_stage1_long_prefix_select(kind, cuda):
+    """nk > 16384 takes the selection that keeps its keys in global memory
+    (and the tensor scorer with many tiles per head): kept indices equal the
+    oracle's and every engine's."""
+    import torch
+    cfg = O.Config(num_heads=6, num_heads_kv=2, dim_head=64, prompt_budget=3000)
+    len_k = 20000
+    Q, K = rkvgen.stage1_inputs(91, 6, 2, 64, 32, len_k)
+    if kind == "bf16":
+        Q, K = rkvgen.bf16_round(Q), rkvgen.bf16_round(K)
+        Qd, Kd = rkvgen.bf16_bits(Q), rkvgen.bf16_bits(K)
+    else:
+        Qd, Kd = Q, K
+    want, total = O.prefill_eviction(Q, K, 32, len_k, cfg, want_total=True)
+    Qt = dev(Qd, kind, cuda).unsqueeze(0).contiguous()
+    Kt = dev(Kd, kind, cuda).unsqueeze(0).contiguous()
+    ev = rkv.Evictor(to_rkv(cfg), 32, len_k, 1, KIND[kind], cuda)
+    for eng in (rkv.ENGINE_AUTO, rkv.ENGINE_TENSOR_TILES, rkv.ENGINE_SIMT):
+        k, n = ev(Qt, Kt, engine=eng)
+        torch.cuda.synchronize()
+        got = k[0, : int(n[0])].cpu().numpy()
+        assert len(got) == 3000
+        assert np.array_equal(got, want), (eng, boundary_report(total, got, want))
+
+
 def test_stage1_config0_full_size(cuda):
     """K [8, 8192, 128] fp32, Q [24, 32, 128] window, budget 1024, ks 63."""
     cfg = O.Config(num_heads=24, num_heads_kv=8, dim_head=128, prompt_budget=1024)
