@@ -326,6 +326,52 @@ def time_evict(device, steps, warmup):
     return statistics.mean(times), statistics.median(e2e) * 1e3, 3  # tcgen05 scoring (both passes), pool, select
 
 
+def time_compaction(device, steps, warmup, layers=28):
+    """KV-cache compaction after stage 1 at the headline geometry: 28 layers
+    of bf16 K and V [8, 8192, 128] reduced to the 3685 kept tokens (the prompt
+    budget compute_rocket_params gives for budget 1024; sorted random indices
+    per layer), out of place and in place; ms per layer and GB/s of rows read
+    and written, L2 flushed before each call."""
+    import torch
+    import rocketkv_b200 as rkv
+    p, _, _ = decode_params()
+    keep = p.prompt_budget
+    gen = torch.Generator(device=device)
+    gen.manual_seed(99)
+    K = torch.randn((layers, HK, PROMPT, D), generator=gen, device=device).bfloat16()
+    V = torch.randn((layers, HK, PROMPT, D), generator=gen, device=device).bfloat16()
+    kept = torch.stack([torch.sort(torch.randperm(PROMPT, generator=gen, device=device)[:keep])[0]
+                        for _ in range(layers)]).to(torch.int32).contiguous()
+    n = torch.full((layers,), keep, dtype=torch.int32, device=device)
+    Ko = torch.empty((layers, HK, keep, D), dtype=torch.bfloat16, device=device)
+    Vo = torch.empty_like(Ko)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    st = torch.cuda.current_stream()
+    moved = 2 * 2 * layers * HK * keep * D * 2  # K and V rows, read and written
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        ts = []
+        for _ in range(steps):
+            flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            fn()
+            e1.record(st)
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return statistics.mean(ts)
+
+    out_ms = timed(lambda: rkv.compact_kv(K, V, kept, n, D, K_out=Ko, V_out=Vo))
+    assert torch.equal(Ko[3, 5, 100], K[3, 5, int(kept[3, 100])])
+    in_ms = timed(lambda: rkv.compact_kv(K, V, kept, n, D))  # repeated in place: the same work every call
+    return {"ms_per_layer_out_of_place": round(out_ms / layers, 5), "ms_per_layer_in_place": round(in_ms / layers, 5),
+            "gbs_out_of_place": round(moved / (out_ms / 1e3) / 1e9, 1),
+            "gbs_in_place": round(moved / (in_ms / 1e3) / 1e9, 1), "bytes_moved_per_call": moved,
+            "workload": f"bf16 K,V [{layers}][8,8192,128] -> {keep} kept tokens per layer (rkv_compact_kv)"}
+
+
 def q8_rows(shape, gen, device):
     """Seeded q8_0 rows on the device: per 32-value block an fp16 scale
     |N(0, 0.02)| and 32 int8 values uniform in [-127, 127] (ggml block_q8_0
@@ -464,6 +510,11 @@ def main():
     for k in q8["ms_per_layer"]:
         q8["ms_per_layer"][k] = round(allreduce_max(q8["ms_per_layer"][k], world), 4)
     eviction["q8_0_28_layers"] = q8
+    comp = time_compaction(device, 5, args.warmup)
+    for k in ("ms_per_layer_out_of_place", "ms_per_layer_in_place"):
+        comp[k] = round(allreduce_max(comp[k], world), 5)
+    comp["frac_of_hbm_out_of_place"] = round(comp["gbs_out_of_place"] / peak, 4)
+    eviction["kv_compaction"] = comp
 
     e2e = None
     if not args.no_e2e:

@@ -214,6 +214,28 @@ int rkv_hsa_decode_noalloc(const void* Q, const void* K, const void* V, int dtyp
                            int head_count, float* O, int* sel, int sel_stride, int* n_sel,
                            void* stream);
 
+/* ---- KV-cache compaction ---------------------------------------------------
+ * Applies stage 1's kept indices to the KV cache on the device: for every
+ * item (layer or sequence) and KV head, row kept[i] of K (and of V) becomes
+ * row i, for i < min(n_kept[item], out_len).  Replaces the reference
+ * runner's removal of the evicted ranges from the model's KV cache
+ * (runner.cpp:246-269, llama_memory_seq_rm per run of evicted positions).
+ * K, V: [batch][num_heads_kv][len_k] rows of `dtype` (fp32, bf16 or q8_0
+ * rows of head_dim values) at kv_item_stride bytes per item; V may be NULL
+ * (then V_out must be NULL too).  kept, n_kept: device int arrays
+ * [batch][kept_stride] and [batch], as rkv_evict writes them (ascending
+ * indices; an index outside [0, len_k) is skipped).  Outputs: K_out, V_out
+ * [batch][num_heads_kv][out_len] rows at out_item_stride bytes per item,
+ * rows from n_kept on left as they are.  In place when K_out == K (and
+ * V_out == V): then out_len must equal len_k and the strides must match, and
+ * the kept lists must be ascending; K and V must not overlap.  Out of place
+ * the output must not overlap the input.  Asynchronous on `stream`;
+ * allocates nothing. */
+int rkv_compact_kv(const void* K, const void* V, int dtype, int head_dim, int num_heads_kv,
+                   int len_k, int batch, long long kv_item_stride, const int* kept,
+                   const int* n_kept, int kept_stride, void* K_out, void* V_out, int out_len,
+                   long long out_item_stride, void* stream);
+
 /* ---- errors raised inside kernels ----------------------------------------
  * Kernels record a failed bounded wait in the workspace.  This synchronises
  * `stream`, returns RKV_OK or the recorded status, and clears it. */

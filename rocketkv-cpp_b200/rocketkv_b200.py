@@ -36,7 +36,7 @@ EXPORTS = [
     "rkv_evict_select_pooled", "rkv_prefill_eviction_host", "rkv_hsa_sel_capacity",
     "rkv_hsa_workspace_size", "rkv_hsa_decode", "rkv_hybrid_sparse_decode_host",
     "rkv_hsa_decode_host_ex", "rkv_workspace_status", "rkv_hsa_decode_noalloc",
-    "rkv_selftest_wait_timeout",
+    "rkv_selftest_wait_timeout", "rkv_compact_kv",
 ]
 
 
@@ -131,6 +131,7 @@ def lib() -> ctypes.CDLL:
         "rkv_selftest_wait_timeout": ([_VP, _VP], _I),
         "rkv_hsa_decode_noalloc": ([_VP, _VP, _VP, _I, _I, _I, _I, _LL, _LL, _CFGP, _I, _I, _VP, _VP, _I, _VP,
                                     _VP], _I),
+        "rkv_compact_kv": ([_VP, _VP, _I, _I, _I, _I, _I, _LL, _VP, _VP, _I, _VP, _VP, _I, _LL, _VP], _I),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -311,6 +312,28 @@ class Evictor:
                                              _ptr(self.n_kept), _ptr(self.ws), self.ws_bytes,
                                              _stream(stream)), "rkv_evict_select_pooled")
         return self.kept, self.n_kept
+
+
+def compact_kv(K, V, kept, n_kept, dim_head: int, K_out=None, V_out=None, stream=None):
+    """Applies kept token indices to a KV cache on the device (rkv_compact_kv).
+
+    K, V: [B, HK, len_k, D*] (float32, bfloat16, or uint8 q8_0 rows of
+    dim_head values); V may be None.  kept [B, >=n] int32 ascending, n_kept
+    [B] int32 (an Evictor's outputs).  Without K_out / V_out the cache is
+    compacted in place (row i of every head becomes row kept[i]); with them,
+    K_out / V_out [B, HK, out_len, D*] receive the kept rows.  Returns the
+    tensors written."""
+    assert K.is_contiguous() and (V is None or V.is_contiguous())
+    dtype = _dtype_of(K)
+    B, HK, len_k = K.shape[0], K.shape[1], K.shape[2]
+    if K_out is None:
+        K_out, V_out = K, V
+    assert K_out.is_contiguous() and (V_out is None or V_out.is_contiguous())
+    _check(lib().rkv_compact_kv(_ptr(K), _ptr(V) if V is not None else None, dtype, dim_head, HK, len_k, B,
+                                K[0].nbytes if B else 0, _ptr(kept), _ptr(n_kept), kept.shape[1], _ptr(K_out),
+                                _ptr(V_out) if V_out is not None else None, K_out.shape[2],
+                                K_out[0].nbytes if B else 0, _stream(stream)), "rkv_compact_kv")
+    return K_out, V_out
 
 
 class HsaDecoder:
