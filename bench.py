@@ -11,7 +11,9 @@ decodes one token for all 64 sequences through the 28 layers: one launch of
 the stage-2 kernel over 64 * 28 * 8 = 14336 (item, KV head) units.  Inputs:
 seeded N(0,1) bf16, 1% of K rows scaled x8; 27 GB per rank, far larger than
 L2.  With N ranks each rank decodes its own 64 sequences (weak scaling, no
-collective on the data path).
+collective on the data path).  The headline steps read the caches' page
+summaries (built once per cache before the timed steps); the stateless steps,
+which scan every K row, are reported beside them.
 
 Eviction: the single-layer fp32 configuration, K [8, 8192, 128], window
 queries Q [24, 32, 128], window 32, kernel 63, budget 1024; and the 28-layer
@@ -61,6 +63,17 @@ def unit_bytes(cache: int, k: int, w: int) -> int:
     G = H // HK
     Lc = cache - w
     return G * D * 2 + Lc * D * 2 + k * D * 2 + 2 * w * D * 2 + G * D * 4 + (k + w) * 4
+
+
+def unit_bytes_summary(cache: int, k: int, w: int, r: int, C: int) -> int:
+    """The same unit read through the page summaries: the r selected
+    dimensions' sign-chosen page extrema replace the scan over every K row
+    (pages = ceil((cache - w) / C), 2 bytes each); the selected K rows are
+    read by the attention."""
+    G = H // HK
+    Lc = cache - w
+    pages = (Lc + C - 1) // C
+    return G * D * 2 + r * pages * 2 + 2 * k * D * 2 + 2 * w * D * 2 + G * D * 4 + (k + w) * 4
 
 
 EVICT_BYTES = 8 * 8160 * 128 * 4 + 24 * 32 * 128 * 4 + 1024 * 4  # 33,820,672
@@ -275,17 +288,17 @@ def make_decode_inputs(device, seed, cache):
     return Qs, K, V
 
 
-def time_decode(dec, Qs, K, V, steps, warmup, world, gpu_index):
+def time_decode(dec, Qs, K, V, steps, warmup, world, gpu_index, summary=None):
     import torch
     st = torch.cuda.current_stream()
     for i in range(warmup):
-        dec(Qs[i % len(Qs)], K, V, want_sel=True)
+        dec(Qs[i % len(Qs)], K, V, want_sel=True, summary=summary)
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(gpu_index) as cs:
         e0.record(st)
         for i in range(steps):
-            dec(Qs[i % len(Qs)], K, V, want_sel=True)
+            dec(Qs[i % len(Qs)], K, V, want_sel=True, summary=summary)
         e1.record(st)
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
@@ -481,7 +494,19 @@ def main():
     Qs, K, V = make_decode_inputs(device, 1234 + rank, cache)
     items = SEQS * LAYERS
     dec = rkv.HsaDecoder(cfg, cache, items, device, recent_window=WINDOW)
-    ms, clocks = time_decode(dec, Qs, K, V, args.steps, args.warmup, world, gpu_index)
+    # stateless: every step scans every K row of the compressed cache
+    ms_sl, clocks_sl = time_decode(dec, Qs, K, V, args.steps, args.warmup, world, gpu_index)
+    assert dec.status() == 0, "in-kernel wait timed out"
+    ms_sl = allreduce_max(ms_sl, world)
+    # persistent page summaries: built once per cache (after eviction), read by every step
+    st = torch.cuda.current_stream()
+    b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    b0.record(st)
+    S = dec.build_summary(K)
+    b1.record(st)
+    torch.cuda.synchronize()
+    build_ms = allreduce_max(b0.elapsed_time(b1), world)
+    ms, clocks = time_decode(dec, Qs, K, V, args.steps, args.warmup, world, gpu_index, summary=S)
     assert dec.status() == 0, "in-kernel wait timed out"
     ms_max = allreduce_max(ms, world)
     step_ms = ms_max / args.steps
@@ -490,12 +515,31 @@ def main():
     peak, peak_kind = peaks()
     units = items * HK
     ub = unit_bytes(cache, p.k, WINDOW)
-    achieved = units * ub / (ms / args.steps / 1e3) / 1e9
-    tr = traffic_per_unit("rkv_hsa_decode")
+    ubs = unit_bytes_summary(cache, p.k, WINDOW, p.r, p.chunk_size)
+    achieved = units * ubs / (ms / args.steps / 1e3) / 1e9
+    tr = traffic_per_unit("rkv_hsa_decode_summary")
     roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
             "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
-            "traffic": (round(tr * units) if tr else None), "algorithmic_bytes_per_launch": units * ub,
-            "kernel": "rkv_hsa_decode (hsa_scan_kernel + hsa_select_kernel + hsa_attn_kernel)"}
+            "traffic": (round(tr * units) if tr else None), "algorithmic_bytes_per_launch": units * ubs,
+            "stateless_equivalent_gbs": round(units * ub / (ms / args.steps / 1e3) / 1e9, 1),
+            "stateless_algorithmic_bytes_per_launch": units * ub,
+            "kernel": "rkv_hsa_decode_summary (hsa_sumscan_kernel + hsa_select_kernel + hsa_attn_kernel)"}
+    ach_sl = units * ub / (ms_sl / args.steps / 1e3) / 1e9
+    tr_sl = traffic_per_unit("rkv_hsa_decode")
+    stateless = {"value": round(world * args.steps / (ms_sl / 1e3), 3), "unit": "steps/s",
+                 "ms_per_step": round(ms_sl / args.steps, 4),
+                 "roofline": {"bound": "hbm", "achieved": round(ach_sl, 1), "peak": peak, "unit": "GB/s",
+                              "frac": round(ach_sl / peak, 4), "traffic": (round(tr_sl * units) if tr_sl else None),
+                              "algorithmic_bytes_per_launch": units * ub,
+                              "kernel": "rkv_hsa_decode (hsa_scan_kernel + hsa_select_kernel + hsa_attn_kernel)"},
+                 "clocks": clocks_sl}
+    summary_info = {"build_ms_per_step_cache": round(build_ms, 3), "bytes": int(S.numel()),
+                    "what": "per (item, KV head, dimension, page of 2 tokens): max of K and of -K over the page, "
+                            "bf16, built once per cache by rkv_hsa_build_summary (outside the timed steps; "
+                            "the compressed cache does not change during decode, new tokens join the recent "
+                            "window); each step reads the r = 71 selected dimensions' sign-chosen extrema "
+                            "instead of every K row",
+                    "break_even_steps": round(build_ms / max(ms_sl / args.steps - step_ms, 1e-9), 2)}
 
     ev_ms, ev_e2e_ms, ev_kernels = time_evict(device, max(args.steps, 5), args.warmup)
     ev_ms = allreduce_max(ev_ms, world)
@@ -544,7 +588,8 @@ def main():
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: seeded N(0,1) bf16 K/V/Q, 1% of K rows x8 (no public dataset on this path)",
             "config": workload_config(cache), "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": args.steps, "clocks": clocks, "eviction": eviction,
+            "gpu_launches": 3 * args.steps, "clocks": clocks, "decode_path": "persistent page summaries",
+            "page_summaries": summary_info, "stateless_decode": stateless, "eviction": eviction,
         }
         print(json.dumps(line))
     if world > 1:

@@ -196,6 +196,35 @@ int rkv_hsa_decode_host_ex(const void* Q, const void* K, const void* V, int dtyp
                            const rkv_config* cfg, float* O, int* sel, int sel_stride,
                            int* n_sel);
 
+/* ---- stage 2 with persistent page summaries --------------------------------
+ * The page scoring of stage 2 (rocket.cpp:252-289) needs, per page of C
+ * tokens of the compressed cache and per selected dimension, the max (or, for
+ * a negative query sign, the min) of K over the page.  A cache that does not
+ * change between decode steps (the compressed part; new tokens go to the
+ * recent window) can keep these extrema as state, so that each step reads
+ * only the selected dimensions' sign-chosen extrema instead of every K row:
+ * 27.7 % of the K bytes at the headline geometry (C 2, r 71 of 128).  The
+ * selected tokens and O are the same as rkv_hsa_decode's, bit for bit.
+ *
+ * rkv_hsa_summary_size: bytes of the summaries of `batch` items (every KV
+ * head) for (cfg, dtype, len_k, recent_window).
+ * rkv_hsa_build_summary: writes them from K (the layout rkv_hsa_decode takes;
+ * all num_heads_kv heads of each item); summary: device memory, 16-byte
+ * aligned, items back to back.  Asynchronous on `stream`.  Rebuild after the
+ * compressed part of K changes.
+ * rkv_hsa_decode_summary: rkv_hsa_decode with the page scoring read from the
+ * summaries built for the same cfg, dtype, len_k and recent_window (the K
+ * rows are still read for the selected tokens and the window). */
+int rkv_hsa_summary_size(const rkv_config* cfg, int dtype, int len_k, int recent_window, int batch,
+                         size_t* bytes);
+int rkv_hsa_build_summary(const void* K, int dtype, int len_k, int recent_window, int batch,
+                          long long kv_item_stride, const rkv_config* cfg, void* summary, void* stream);
+int rkv_hsa_decode_summary(const void* Q, const void* K, const void* V, const void* summary, int dtype,
+                           int len_k, int recent_window, int batch, long long q_item_stride,
+                           long long kv_item_stride, const rkv_config* cfg, int head_begin, int head_count,
+                           float* O, int* sel, int sel_stride, int* n_sel, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
 /* No-allocation stage 2.  This entry point has no counterpart in the
  * reference; it exists for callers that cannot allocate device memory (an
  * inference server or plugin host whose allocator owns the device heap, or a

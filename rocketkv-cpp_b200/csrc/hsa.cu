@@ -955,6 +955,357 @@ __global__ void __launch_bounds__(kNT, 3) hsa_attn_kernel(const HsaArgs a) {
     }
 }
 
+// ===========================================================================
+// Page summaries (persistent cache state; SURVEY-style "page min/max" option)
+// ===========================================================================
+// For every (item, KV head), dimension d and page p (rows p C .. min(p C + C,
+// Lc) - 1 of the compressed cache), the summary holds the NaN-ignoring max of
+// x and of -x over the page's rows, in the K element type, laid out
+// [2][D][npp] with the pages of a dimension contiguous.  These are exactly the
+// values hsa_scan_kernel forms in its sign-flipped domain (max.bf16x2 / fmaxf
+// over the rows, the first row first), so a scan that reads them for the
+// selected dimensions -- max x where sum_h q >= 0, max -x elsewhere -- repeats
+// the same float operations and selects the same tokens.
+
+constexpr int kSumBuildNT = 256;
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kSumBuildNT) hsa_summary_build_kernel(const uint8_t* K, long long kv_stride,
+                                                                         int len_k, int C, int Lc, int nchunks,
+                                                                         int npp, int TP, uint8_t* summary,
+                                                                         long long sum_stride) {
+    constexpr int ES = (int)sizeof(T), RB = D * ES, W = RB / 4;  // 32-bit words per row
+    constexpr uint32_t FLIP = ES == 2 ? 0x80008000u : 0x80000000u;
+    extern __shared__ __align__(16) uint8_t smraw[];
+    T* tile = reinterpret_cast<T*>(smraw);  // [2][D][TP]
+    const int pt = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+    const int p0 = pt * TP;
+    const uint8_t* Kh = K + (size_t)b * kv_stride + (size_t)hk * len_k * RB;
+    for (int x = threadIdx.x; x < TP * W; x += kSumBuildNT) {
+        const int p = x / W, wd = x % W, page = p0 + p;
+        uint32_t m = 0u, n = 0u;
+        if (page < nchunks) {
+            const int r0 = page * C, r1 = min(r0 + C, Lc);
+            const uint32_t v0 = *reinterpret_cast<const uint32_t*>(Kh + (size_t)r0 * RB + 4 * wd);
+            m = v0;
+            n = v0 ^ FLIP;
+            for (int r = r0 + 1; r < r1; ++r) {
+                const uint32_t v = *reinterpret_cast<const uint32_t*>(Kh + (size_t)r * RB + 4 * wd);
+                m = Chunk<T>::wmax(m, v);
+                n = Chunk<T>::wmax(n, v ^ FLIP);
+            }
+        }
+        if (ES == 2) {
+            tile[(0 * D + 2 * wd) * TP + p] = (T)(m & 0xffffu);
+            tile[(0 * D + 2 * wd + 1) * TP + p] = (T)(m >> 16);
+            tile[(1 * D + 2 * wd) * TP + p] = (T)(n & 0xffffu);
+            tile[(1 * D + 2 * wd + 1) * TP + p] = (T)(n >> 16);
+        } else {
+            reinterpret_cast<uint32_t*>(tile)[(0 * D + wd) * TP + p] = m;
+            reinterpret_cast<uint32_t*>(tile)[(1 * D + wd) * TP + p] = n;
+        }
+    }
+    __syncthreads();
+    // rows of TP pages out, 16 bytes at a time (npp and TP are multiples of 8 pages)
+    const int np = min(TP, npp - p0);
+    const int vpr = np * ES / 16;
+    uint8_t* Sb = summary + (size_t)b * sum_stride + (size_t)hk * 2 * D * npp * ES;
+    for (int x = threadIdx.x; x < 2 * D * vpr; x += kSumBuildNT) {
+        const int row = x / vpr, v = x % vpr;
+        *reinterpret_cast<uint4*>(Sb + ((size_t)row * npp + p0) * ES + 16 * v) =
+            *reinterpret_cast<const uint4*>(smraw + ((size_t)row * TP) * ES + 16 * v);
+    }
+}
+
+// Phases 0 and 1 from the page summaries.  Per tile of TP pages one bulk copy
+// per selected dimension brings its sign-chosen run of extrema into shared
+// memory (mbarrier completion, bounded wait; several CTAs per SM overlap their
+// tiles).  A quad of four lanes scores four pages, lane j taking the chunks
+// j, j + 4, ... as in hsa_scan_kernel, each page pair in the two lanes of
+// paired fp32 FMAs.  Per page and head the sum is the scan's: per 16-byte
+// chunk an even and an odd fused multiply-add chain over the selected
+// dimensions (the unselected ones add exact zeros there), chunk value
+// even + odd; the lane's chunks added pairwise; the lanes as
+// (l0 + l2) + (l1 + l3) by two shuffles.  Each chunk keeps lists of its
+// selected even and odd dimensions (tile row and s q per head); the lanes of
+// a warp run the longest list of their slot, the shorter ones padded with an
+// all-zero tile row and q = 0, so that control flow is the same on every
+// lane and the padding adds exact zeros (0 x 0).  The representatives are clamped at -FLT_MAX, which
+// is the scan's result on every page (the clamp only changes a representative
+// that makes a page's sum non-finite, where the scan recomputes clamped).
+constexpr int kSumScanNT = 128;
+
+template <typename T, int D, int MAXG>
+__global__ void __launch_bounds__(kSumScanNT) hsa_sumscan_kernel(const HsaArgs a) {
+    constexpr int ES = (int)sizeof(T);
+    constexpr int CD = 16 / ES, NCH = D / CD, NSL = NCH / 4;
+    constexpr int TOP = NSL >= 16 ? 4 : NSL >= 8 ? 3 : NSL >= 4 ? 2 : 1;  // log2(NSL)
+    constexpr int LEV = TOP + 1;                                            // pairwise-tree stack depth per lane
+    static_assert((1 << TOP) == NSL, "slots per lane: a power of two up to 16");
+    constexpr int DPT = (D + kSumScanNT - 1) / kSumScanNT;  // dimensions per thread in phase 0
+    extern __shared__ __align__(128) uint8_t sbuf[];         // [nr][TP] extrema
+    __shared__ __align__(16) float qf[MAXG * D];
+    constexpr int QW = (MAXG + 1 + 3) / 4 * 4;  // floats per list entry: the tile row, then s q per head
+    constexpr int HALF = CD / 2;                // even (odd) dimensions per chunk
+    constexpr int CST = 2 * HALF * QW + 4;      // floats per chunk of lists (padded: quad lanes in other banks)
+    __shared__ __align__(16) float ent[NCH * CST];
+    __shared__ int maxe[NSL], maxo[NSL];
+    __shared__ float sabs[D], qsum[D];
+    __shared__ int Rl[D];
+    __shared__ unsigned char dsel[D], dneg[D];
+    __shared__ uint32_t selw[D / 32];
+    __shared__ float sumall[MAXG], cscale[MAXG];
+    __shared__ int scan_tmp[33];
+    __shared__ uint64_t full;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int split = blockIdx.x, hc = blockIdx.y, b = blockIdx.z, hk = a.head_begin + hc;
+    const int G = a.G, TP = a.stage_rows;  // pages per tile
+    const int p_beg = split * a.pages_per_split;
+    const int p_end = min(a.nchunks, p_beg + a.pages_per_split);
+    if (p_beg >= p_end) return;  // uniform
+    const uint8_t* Qg = a.Q + (size_t)b * a.q_stride + (size_t)hk * G * D * sizeof(T);
+    float* wl = a.wlogits + ((size_t)b * a.head_count + hc) * (size_t)G * a.nch_pad;
+    if (tid == 0) {
+        mbar_init(&full, 1);
+        fence_mbar_init();
+    }
+    for (int e = tid; e < G * D; e += kSumScanNT) qf[e] = to_f<T>(reinterpret_cast<const T*>(Qg)[e]);
+    __syncthreads();
+    // ---- phase 0: group query statistics (rocket.cpp:197-250), as hsa_scan_kernel ----
+    for (int d = tid; d < D; d += kSumScanNT) {
+        float sa = 0.0f, sv = 0.0f;
+        for (int h = 0; h < G; ++h) {
+            const float q = qf[h * D + d];
+            sa = __fadd_rn(sa, fabsf(q));
+            sv = __fadd_rn(sv, q);
+        }
+        sabs[d] = sa;
+        qsum[d] = sv;
+    }
+    if (lane == 0 && warp < G) {
+        for (int h = warp; h < G; h += kSumScanNT / 32) {
+            const float4* q4 = reinterpret_cast<const float4*>(qf + h * D);
+            float s = 0.0f;
+#pragma unroll 8
+            for (int v = 0; v < D / 4; ++v) {
+                const float4 x = q4[v];
+                s = __fadd_rn(s, fabsf(x.x));
+                s = __fadd_rn(s, fabsf(x.y));
+                s = __fadd_rn(s, fabsf(x.z));
+                s = __fadd_rn(s, fabsf(x.w));
+            }
+            sumall[h] = s;
+        }
+    }
+    __syncthreads();
+    // top r by (sum |q| desc, dimension asc); thread t owns dimensions t DPT .. t DPT + DPT - 1
+    int myflags = 0, nmine = 0;
+#pragma unroll
+    for (int u = 0; u < DPT; ++u) {
+        const int d = tid * DPT + u;
+        if (d < D) {
+            int rank = 0;
+            const float me = sabs[d];
+#pragma unroll 8
+            for (int e = 0; e < D; ++e) {
+                const float o = sabs[e];
+                rank += (o > me || (o == me && e < d)) ? 1 : 0;
+            }
+            const int f = (a.r >= D || rank < a.r) ? 1 : 0;
+            myflags |= f << u;
+            nmine += f;
+            dsel[d] = (unsigned char)f;
+            dneg[d] = !(qsum[d] >= 0.0f) ? 1 : 0;  // rocket.cpp:263: sign >= 0 takes the max
+        }
+    }
+    int nr;
+    int pos = block_exclusive_scan(nmine, scan_tmp, &nr);
+#pragma unroll
+    for (int u = 0; u < DPT; ++u)
+        if ((myflags >> u) & 1) Rl[pos++] = tid * DPT + u;  // the selected dimensions, ascending
+    __syncthreads();
+    if (tid < G) {
+        float sk;
+        if (a.r >= D) {
+            sk = sumall[tid];
+        } else {
+            sk = 0.0f;
+            for (int i = 0; i < nr; ++i) sk = __fadd_rn(sk, fabsf(qf[tid * D + Rl[i]]));
+        }
+        cscale[tid] = __fsqrt_rn(__fmul_rn((float)D, __fdiv_rn(sk, __fadd_rn(sumall[tid], 1e-9f))));
+    }
+    if (tid < D / 32) {
+        uint32_t m = 0;
+        for (int e = 0; e < 32; ++e) m |= (uint32_t)dsel[tid * 32 + e] << e;
+        selw[tid] = m;
+    }
+    __syncthreads();
+    if (tid < NCH) {  // chunk tid: its selected even / odd dimensions, ascending, then padding entries
+        const int c = tid;
+        int k = 0;
+        for (int d = 0; d < c * CD; ++d) k += dsel[d];  // tile row of the chunk's first selected dimension
+        int n[2] = {0, 0};
+        for (int e = 0; e < CD; ++e) {
+            const int d = c * CD + e, par = e & 1;
+            if (!dsel[d]) continue;
+            float* en = ent + c * CST + (par * HALF + n[par]) * QW;
+            en[0] = __int_as_float(k++);
+            for (int h = 0; h < QW - 1; ++h) {
+                const float q = h < G ? qf[h * D + d] : 0.0f;
+                en[1 + h] = dneg[d] ? -q : q;
+            }
+            ++n[par];
+        }
+        for (int par = 0; par < 2; ++par)
+            for (int u = n[par]; u < HALF; ++u) {
+                float* en = ent + c * CST + (par * HALF + u) * QW;
+                en[0] = __int_as_float(nr);  // the zero row
+                for (int h = 0; h < QW - 1; ++h) en[1 + h] = 0.0f;
+            }
+        reinterpret_cast<int*>(ent + c * CST)[2 * HALF * QW] = n[0];
+        reinterpret_cast<int*>(ent + c * CST)[2 * HALF * QW + 1] = n[1];
+    }
+    __syncthreads();
+    if (tid < NSL) {  // the longest lists of slot tid over the four lanes
+        int me = 0, mo = 0;
+        for (int jj = 0; jj < 4; ++jj) {
+            const int* cn = reinterpret_cast<const int*>(ent + (jj + 4 * tid) * CST) + 2 * HALF * QW;
+            me = max(me, cn[0]);
+            mo = max(mo, cn[1]);
+        }
+        maxe[tid] = me;
+        maxo[tid] = mo;
+    }
+    __syncthreads();
+
+    // ---- phase 1: page logits from the summaries ----
+    const uint8_t* Sb = a.summary + (size_t)b * a.sum_stride + (size_t)hk * 2 * D * a.npp * ES;
+    const int ntile = (p_end - p_beg + TP - 1) / TP;
+    const int j = tid & 3, qd = tid >> 2;  // lane of the quad, quad
+    float my_scale[(MAXG + 3) / 4];
+#pragma unroll
+    for (int u = 0; u < (MAXG + 3) / 4; ++u) my_scale[u] = (j + 4 * u < G) ? cscale[j + 4 * u] : 1.0f;
+    const size_t row_b = (size_t)TP * ES + 16;  // bytes per dimension row of the tile (padded: other banks)
+    for (int x = tid; x < (int)(row_b / 16); x += kSumScanNT)  // row nr: zeros, the padding entries' row
+        reinterpret_cast<uint4*>(sbuf + (size_t)nr * row_b)[x] = make_uint4(0u, 0u, 0u, 0u);
+    __syncthreads();
+    for (int t = 0; t < ntile; ++t) {
+        const int tp0 = p_beg + t * TP;
+        if (warp == 0) {  // the tile's copies, spread over the lanes of warp 0
+            const int np = min(TP, a.npp - tp0);  // whole 8-page groups: bytes a multiple of 16
+            fence_proxy_async();
+            if (lane == 0) mbar_arrive_expect_tx(&full, (uint32_t)((size_t)nr * np * ES));
+            __syncwarp();
+            for (int k = lane; k < nr; k += 32) {
+                const int d = Rl[k];
+                bulk_load(sbuf + (size_t)k * row_b, Sb + ((size_t)(dneg[d] * D + d) * a.npp + tp0) * ES,
+                          (uint32_t)(np * ES), &full);
+            }
+        }
+        const bool w = mbar_wait_bounded(&full, (uint32_t)(t & 1), a.err);
+        if (!__syncthreads_and(w)) {
+            if (tid == 0) mbar_wait_bounded(&full, (uint32_t)(t & 1), a.err);  // the copies land before the exit
+            return;
+        }
+        // the same trip count for every lane (the quad shuffles below take the whole warp): quads past
+        // the unit's end score stale columns of the tile buffer and write nothing
+        for (int g0 = 4 * qd; g0 < TP; g0 += 4 * (kSumScanNT / 4)) {  // four pages per quad
+            const int p0 = tp0 + g0;
+            const uint8_t* col = sbuf + (size_t)g0 * ES;
+            float2 sv[NSL][MAXG][2];  // [slot][head][page pair]
+#pragma unroll
+            for (int i = 0; i < NSL; ++i) {
+                const float* ec = ent + (j + 4 * i) * CST;
+                float2 acc[2][MAXG][2];  // [parity][head][page pair]
+#pragma unroll
+                for (int par = 0; par < 2; ++par)
+#pragma unroll
+                    for (int h = 0; h < MAXG; ++h) acc[par][h][0] = acc[par][h][1] = make_float2(0.0f, 0.0f);
+#pragma unroll
+                for (int par = 0; par < 2; ++par) {
+                    const int nu = par ? maxo[i] : maxe[i];  // the same on every lane of the warp
+                    for (int u = 0; u < nu; ++u) {
+                        const float4* en = reinterpret_cast<const float4*>(ec + (par * HALF + u) * QW);
+                        const float4 e0 = en[0];
+                        const int k = __float_as_int(e0.x);
+                        float2 P0, P1;  // pages 0-1, 2-3
+                        if (ES == 2) {
+                            const uint2 w4 = *reinterpret_cast<const uint2*>(col + (size_t)k * row_b);
+                            P0 = make_float2(__uint_as_float(w4.x << 16), __uint_as_float(w4.x & 0xffff0000u));
+                            P1 = make_float2(__uint_as_float(w4.y << 16), __uint_as_float(w4.y & 0xffff0000u));
+                        } else {
+                            const float4 f4 = *reinterpret_cast<const float4*>(col + (size_t)k * row_b);
+                            P0 = make_float2(f4.x, f4.y);
+                            P1 = make_float2(f4.z, f4.w);
+                        }
+                        P0 = make_float2(fmaxf(P0.x, -FLT_MAX), fmaxf(P0.y, -FLT_MAX));
+                        P1 = make_float2(fmaxf(P1.x, -FLT_MAX), fmaxf(P1.y, -FLT_MAX));
+                        float qh[QW];
+                        qh[0] = e0.y;
+                        qh[1] = e0.z;
+                        qh[2] = e0.w;
+#pragma unroll
+                        for (int uu = 1; uu < QW / 4; ++uu) {
+                            const float4 ex = en[uu];
+                            qh[4 * uu - 1] = ex.x;
+                            qh[4 * uu] = ex.y;
+                            qh[4 * uu + 1] = ex.z;
+                            qh[4 * uu + 2] = ex.w;
+                        }
+#pragma unroll
+                        for (int h = 0; h < MAXG; ++h) {
+                            const float2 q2 = make_float2(qh[h], qh[h]);
+                            ffma2(acc[par][h][0], q2, P0);
+                            ffma2(acc[par][h][1], q2, P1);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int h = 0; h < MAXG; ++h) {
+                    sv[i][h][0] = __fadd2_rn(acc[0][h][0], acc[1][h][0]);
+                    sv[i][h][1] = __fadd2_rn(acc[0][h][1], acc[1][h][1]);
+                }
+            }
+#pragma unroll
+            for (int w2 = 1; w2 < NSL; w2 *= 2)
+#pragma unroll
+                for (int i = 0; i < NSL; i += 2 * w2)
+#pragma unroll
+                    for (int h = 0; h < MAXG; ++h) {
+                        sv[i][h][0] = __fadd2_rn(sv[i][h][0], sv[i + w2][h][0]);
+                        sv[i][h][1] = __fadd2_rn(sv[i][h][1], sv[i + w2][h][1]);
+                    }
+            // (l0 + l2) + (l1 + l3) over the quad, as quad_sum
+            float v[MAXG][4];
+#pragma unroll
+            for (int h = 0; h < MAXG; ++h) {
+                v[h][0] = sv[0][h][0].x;
+                v[h][1] = sv[0][h][0].y;
+                v[h][2] = sv[0][h][1].x;
+                v[h][3] = sv[0][h][1].y;
+#pragma unroll
+                for (int pg = 0; pg < 4; ++pg) {
+                    v[h][pg] = __fadd_rn(v[h][pg], __shfl_xor_sync(0xffffffffu, v[h][pg], 2));
+                    v[h][pg] = __fadd_rn(v[h][pg], __shfl_xor_sync(0xffffffffu, v[h][pg], 1));
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < (MAXG + 3) / 4; ++u) {
+                const int h = j + 4 * u;
+#pragma unroll
+                for (int hh = 0; hh < MAXG; ++hh) {
+                    if (hh != h || h >= G) continue;
+#pragma unroll
+                    for (int pg = 0; pg < 4; ++pg)
+                        if (p0 + pg < p_end) wl[(size_t)h * a.nch_pad + p0 + pg] = __fdiv_rn(v[hh][pg], my_scale[u]);
+                }
+            }
+        }
+        __syncthreads();  // the buffer is refilled for the next tile
+    }
+}
+
 int num_sms() {
     int dev = 0, n = 0;
     if (cudaGetDevice(&dev) != cudaSuccess ||
@@ -965,7 +1316,26 @@ int num_sms() {
 
 template <typename T, int D, int MAXG>
 int launch_t(HsaArgs a, int batch, cudaStream_t st) {
-    if (a.nchunks > 0) {
+    if (a.nchunks > 0 && a.summary) {
+        // page logits from the summaries; enough CTAs to cover the GPU
+        const long long units = (long long)batch * a.head_count;
+        const long long want = 4LL * num_sms();
+        int splits = units >= want ? 1 : (int)((want + units - 1) / units);
+        const int max_splits = (a.nchunks + 2 * kSumScanNT - 1) / (2 * kSumScanNT);
+        if (splits > max_splits) splits = max_splits;
+        if (splits < 1) splits = 1;
+        // tile of TP = 2 x threads pages: one buffer of r runs (several CTAs per SM overlap)
+        const int tp = 2 * kSumScanNT;
+        a.stage_rows = tp;
+        a.pages_per_split = ((a.nchunks + splits - 1) / splits + tp - 1) / tp * tp;  // whole tiles
+        a.splits = (a.nchunks + a.pages_per_split - 1) / a.pages_per_split;
+        const size_t smem = (size_t)((a.r < D ? a.r : D) + 1) * (tp * sizeof(T) + 16);  // + the zero row
+        auto fs = hsa_sumscan_kernel<T, D, MAXG>;
+        if (cudaFuncSetAttribute(fs, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return RKV_ERR_CUDA;
+        fs<<<dim3(a.splits, a.head_count, batch), kSumScanNT, smem, st>>>(a);
+        if (cudaGetLastError() != cudaSuccess) return RKV_ERR_CUDA;
+    } else if (a.nchunks > 0) {
         auto fs = hsa_scan_kernel<T, D, MAXG>;
         cudaFuncAttributes fa;
         if (cudaFuncGetAttributes(&fa, fs) != cudaSuccess) return RKV_ERR_CUDA;
@@ -1099,6 +1469,48 @@ HsaShape hsa_shape(const rkv_config& c, int len_k, int recent_window, int batch,
                    kWorkspaceAlign);
     s.ws_bytes = off;
     return s;
+}
+
+HsaSummaryShape hsa_summary_shape(const rkv_config& c, int dtype, int len_k, int recent_window) {
+    const HsaShape h = hsa_shape(c, len_k, recent_window, 1, c.num_heads_kv);
+    HsaSummaryShape s{};
+    s.C = h.C;
+    s.Lc = h.Lc;
+    s.nchunks = h.Lc > 0 ? (h.Lc + h.C - 1) / h.C : 0;  // every page, whether or not a call scores them
+    s.npp = (s.nchunks + 7) / 8 * 8;
+    s.item_bytes = (long long)c.num_heads_kv * 2 * c.dim_head * s.npp * (dtype == RKV_F32 ? 4 : 2);
+    return s;
+}
+
+template <typename T, int D>
+static int build_t(const uint8_t* K, int HK, int len_k, long long kv_stride, const HsaSummaryShape& s,
+                   uint8_t* summary, int batch, cudaStream_t st) {
+    const int rowb = D * (int)sizeof(T);
+    int TP = 16384 / rowb;
+    if (TP > 64) TP = 64;
+    if (TP < 8) TP = 8;
+    const size_t smem = (size_t)2 * D * TP * sizeof(T);
+    auto f = hsa_summary_build_kernel<T, D>;
+    if (smem > 48 * 1024 && cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return RKV_ERR_CUDA;
+    dim3 grid((s.npp + TP - 1) / TP, HK, batch);
+    f<<<grid, kSumBuildNT, smem, st>>>(K, kv_stride, len_k, s.C, s.Lc, s.nchunks, s.npp, TP, summary, s.item_bytes);
+    return cudaGetLastError() == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
+}
+
+int launch_hsa_summary_build(const uint8_t* K, int dtype, int D, int HK, int len_k, long long kv_stride,
+                             const HsaSummaryShape& s, uint8_t* summary, int batch, cudaStream_t st) {
+    if (batch <= 0 || s.nchunks <= 0) return RKV_OK;
+    const bool f32 = dtype == RKV_F32;
+    switch (D) {
+        case 64: return f32 ? build_t<float, 64>(K, HK, len_k, kv_stride, s, summary, batch, st)
+                            : build_t<uint16_t, 64>(K, HK, len_k, kv_stride, s, summary, batch, st);
+        case 128: return f32 ? build_t<float, 128>(K, HK, len_k, kv_stride, s, summary, batch, st)
+                             : build_t<uint16_t, 128>(K, HK, len_k, kv_stride, s, summary, batch, st);
+        case 256: return f32 ? build_t<float, 256>(K, HK, len_k, kv_stride, s, summary, batch, st)
+                             : build_t<uint16_t, 256>(K, HK, len_k, kv_stride, s, summary, batch, st);
+        default: return RKV_ERR_UNSUPPORTED;
+    }
 }
 
 int hsa_check_supported(const rkv_config& c, int dtype) {

@@ -38,7 +38,21 @@ struct HsaArgs {
     int nstage;           // scan ring stages
     int tail_r0_bytes;    // attention-kernel shared memory for the merge buffer
     int nch_pad;          // row stride of the page logits (nchunks rounded up to 4)
+    // page summaries (nullable): per (item, KV head) [2][D][npp] values of the K type, the
+    // NaN-ignoring max over a page's rows of x and of -x; the scan then reads these instead of K
+    const uint8_t* summary;
+    long long sum_stride;  // bytes between items
+    int npp;               // pages per summary row (nchunks rounded up to 8)
 };
+
+// Page-summary geometry for (cfg, len_k, recent_window): pages per row and bytes per item.
+struct HsaSummaryShape {
+    int C, Lc, nchunks, npp;
+    long long item_bytes;
+};
+HsaSummaryShape hsa_summary_shape(const rkv_config& c, int dtype, int len_k, int recent_window);
+int launch_hsa_summary_build(const uint8_t* K, int dtype, int D, int HK, int len_k, long long kv_stride,
+                             const HsaSummaryShape& s, uint8_t* summary, int batch, cudaStream_t st);
 
 struct HsaShape {
     int G, C, r, w, Lc, final_k, nchunks, nch_pad, sel_cap;

@@ -179,6 +179,12 @@ int max_kept_of(const EvictShape& s, int len_k) {
     return s.target_keep + s.obs_w;
 }
 
+// stage 2 on device buffers; summary: page summaries (rkv_hsa_build_summary) or null
+int hsa_decode_impl(const void* Q, const void* K, const void* V, const void* summary, int dtype, int len_k,
+                    int recent_window, int batch, long long q_item_stride, long long kv_item_stride,
+                    const rkv_config* cfg, int head_begin, int head_count, float* O, int* sel, int sel_stride,
+                    int* n_sel, void* workspace, size_t workspace_bytes, void* stream);
+
 }  // namespace
 
 extern "C" {
@@ -402,6 +408,54 @@ int rkv_hsa_decode(const void* Q, const void* K, const void* V, int dtype, int l
                    int batch, long long q_item_stride, long long kv_item_stride, const rkv_config* cfg,
                    int head_begin, int head_count, float* O, int* sel, int sel_stride, int* n_sel,
                    void* workspace, size_t workspace_bytes, void* stream) {
+    return hsa_decode_impl(Q, K, V, nullptr, dtype, len_k, recent_window, batch, q_item_stride, kv_item_stride, cfg,
+                           head_begin, head_count, O, sel, sel_stride, n_sel, workspace, workspace_bytes, stream);
+}
+
+int rkv_hsa_summary_size(const rkv_config* cfg, int dtype, int len_k, int recent_window, int batch, size_t* bytes) {
+    if (check_cfg(cfg) || !bytes || batch < 0 || len_k < 0) return RKV_ERR_INVALID_ARG;
+    if (dtype != RKV_F32 && dtype != RKV_BF16) return dtype == RKV_Q8_0 ? RKV_ERR_UNSUPPORTED : RKV_ERR_INVALID_ARG;
+    const int rc = hsa_check_supported(*cfg, dtype);
+    if (rc) return rc;
+    *bytes = (size_t)batch * (size_t)hsa_summary_shape(*cfg, dtype, len_k, recent_window).item_bytes;
+    return RKV_OK;
+}
+
+int rkv_hsa_build_summary(const void* K, int dtype, int len_k, int recent_window, int batch,
+                          long long kv_item_stride, const rkv_config* cfg, void* summary, void* stream) {
+    if (check_cfg(cfg) || batch < 0 || len_k < 0) return RKV_ERR_INVALID_ARG;
+    if (dtype != RKV_F32 && dtype != RKV_BF16) return dtype == RKV_Q8_0 ? RKV_ERR_UNSUPPORTED : RKV_ERR_INVALID_ARG;
+    int rc = hsa_check_supported(*cfg, dtype);
+    if (rc) return rc;
+    if (batch == 0) return RKV_OK;
+    if (!K || !summary || !aligned16(summary) || (kv_item_stride & 3) || (reinterpret_cast<uintptr_t>(K) & 3))
+        return RKV_ERR_INVALID_ARG;
+    const HsaSummaryShape sh = hsa_summary_shape(*cfg, dtype, len_k, recent_window);
+    const long long rowb = (long long)cfg->dim_head * (dtype == RKV_F32 ? 4 : 2);
+    if (batch > 1 && kv_item_stride < (long long)cfg->num_heads_kv * len_k * rowb) return RKV_ERR_INVALID_ARG;
+    return launch_hsa_summary_build(static_cast<const uint8_t*>(K), dtype, cfg->dim_head, cfg->num_heads_kv, len_k,
+                                    kv_item_stride, sh, static_cast<uint8_t*>(summary), batch,
+                                    static_cast<cudaStream_t>(stream));
+}
+
+int rkv_hsa_decode_summary(const void* Q, const void* K, const void* V, const void* summary, int dtype,
+                           int len_k, int recent_window, int batch, long long q_item_stride,
+                           long long kv_item_stride, const rkv_config* cfg, int head_begin, int head_count,
+                           float* O, int* sel, int sel_stride, int* n_sel, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+    if (!summary || !aligned16(summary)) return RKV_ERR_INVALID_ARG;
+    return hsa_decode_impl(Q, K, V, summary, dtype, len_k, recent_window, batch, q_item_stride, kv_item_stride, cfg,
+                           head_begin, head_count, O, sel, sel_stride, n_sel, workspace, workspace_bytes, stream);
+}
+
+}  // extern "C"
+
+namespace {
+
+int hsa_decode_impl(const void* Q, const void* K, const void* V, const void* summary, int dtype, int len_k,
+                    int recent_window, int batch, long long q_item_stride, long long kv_item_stride,
+                    const rkv_config* cfg, int head_begin, int head_count, float* O, int* sel, int sel_stride,
+                    int* n_sel, void* workspace, size_t workspace_bytes, void* stream) {
     if (check_cfg(cfg) || batch < 0 || len_k < 0) return RKV_ERR_INVALID_ARG;
     if (head_begin < 0 || head_count < 0 || head_begin + head_count > cfg->num_heads_kv) return RKV_ERR_INVALID_ARG;
     if (dtype != RKV_F32 && dtype != RKV_BF16) return dtype == RKV_Q8_0 ? RKV_ERR_UNSUPPORTED : RKV_ERR_INVALID_ARG;
@@ -450,8 +504,18 @@ int rkv_hsa_decode(const void* Q, const void* K, const void* V, int dtype, int l
     a.wscore = reinterpret_cast<float*>(ws + s.off_scores);
     a.score_stride = s.sel_cap > 0 ? s.sel_cap : 1;
     a.err = reinterpret_cast<int*>(ws);
+    if (summary) {
+        const HsaSummaryShape sh = hsa_summary_shape(*cfg, dtype, len_k, recent_window);
+        a.summary = static_cast<const uint8_t*>(summary);
+        a.sum_stride = sh.item_bytes;
+        a.npp = sh.npp;
+    }
     return launch_hsa(a, dtype, batch, st);
 }
+
+}  // namespace
+
+extern "C" {
 
 int rkv_hsa_decode_host_ex(const void* Q, const void* K, const void* V, int dtype, int len_k, int recent_window,
                            int batch, long long q_item_stride, long long kv_item_stride, const rkv_config* cfg,

@@ -36,7 +36,8 @@ EXPORTS = [
     "rkv_evict_select_pooled", "rkv_prefill_eviction_host", "rkv_hsa_sel_capacity",
     "rkv_hsa_workspace_size", "rkv_hsa_decode", "rkv_hybrid_sparse_decode_host",
     "rkv_hsa_decode_host_ex", "rkv_workspace_status", "rkv_hsa_decode_noalloc",
-    "rkv_selftest_wait_timeout", "rkv_compact_kv",
+    "rkv_selftest_wait_timeout", "rkv_compact_kv", "rkv_hsa_summary_size", "rkv_hsa_build_summary",
+    "rkv_hsa_decode_summary",
 ]
 
 
@@ -132,6 +133,10 @@ def lib() -> ctypes.CDLL:
         "rkv_hsa_decode_noalloc": ([_VP, _VP, _VP, _I, _I, _I, _I, _LL, _LL, _CFGP, _I, _I, _VP, _VP, _I, _VP,
                                     _VP], _I),
         "rkv_compact_kv": ([_VP, _VP, _I, _I, _I, _I, _I, _LL, _VP, _VP, _I, _VP, _VP, _I, _LL, _VP], _I),
+        "rkv_hsa_summary_size": ([_CFGP, _I, _I, _I, _I, ctypes.POINTER(_SZ)], _I),
+        "rkv_hsa_build_summary": ([_VP, _I, _I, _I, _I, _LL, _CFGP, _VP, _VP], _I),
+        "rkv_hsa_decode_summary": ([_VP, _VP, _VP, _VP, _I, _I, _I, _I, _LL, _LL, _CFGP, _I, _I, _VP, _VP, _I,
+                                    _VP, _VP, _SZ, _VP], _I),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -354,16 +359,31 @@ class HsaDecoder:
         self.sel = torch.zeros((batch, self.head_count, self.sel_cap), dtype=torch.int32, device=device)
         self.n_sel = torch.zeros((batch, self.head_count), dtype=torch.int32, device=device)
 
-    def __call__(self, Q, K, V, stream=None, want_sel: bool = True):
+    def build_summary(self, K, stream=None):
+        """Page summaries of K (every KV head) for this decoder's geometry:
+        later calls with summary=... read them instead of scanning every K row."""
+        import torch
+        dt = _dtype_of(K)
+        n = ctypes.c_size_t(0)
+        _check(lib().rkv_hsa_summary_size(ctypes.byref(self.c), dt, self.len_k, self.w, self.batch, ctypes.byref(n)),
+               "rkv_hsa_summary_size")
+        S = torch.empty(max(n.value, 16), dtype=torch.uint8, device=K.device)
+        _check(lib().rkv_hsa_build_summary(_ptr(K), dt, self.len_k, self.w, self.batch, K[0].nbytes if self.batch else 0,
+                                           ctypes.byref(self.c), _ptr(S), _stream(stream)), "rkv_hsa_build_summary")
+        return S
+
+    def __call__(self, Q, K, V, stream=None, want_sel: bool = True, summary=None):
         assert Q.is_contiguous() and K.is_contiguous() and V.is_contiguous()
         assert K.shape == V.shape and Q.shape[0] == K.shape[0] == self.batch
         dt = _dtype_of(K)
-        _check(lib().rkv_hsa_decode(_ptr(Q), _ptr(K), _ptr(V), dt, self.len_k, self.w, self.batch,
-                                    Q[0].nbytes, K[0].nbytes, ctypes.byref(self.c), self.head_begin,
-                                    self.head_count, _ptr(self.O),
-                                    _ptr(self.sel) if want_sel else 0, self.sel_cap,
-                                    _ptr(self.n_sel) if want_sel else 0, _ptr(self.ws),
-                                    self.ws_bytes, _stream(stream)), "rkv_hsa_decode")
+        common = (dt, self.len_k, self.w, self.batch, Q[0].nbytes, K[0].nbytes, ctypes.byref(self.c), self.head_begin,
+                  self.head_count, _ptr(self.O), _ptr(self.sel) if want_sel else 0, self.sel_cap,
+                  _ptr(self.n_sel) if want_sel else 0, _ptr(self.ws), self.ws_bytes, _stream(stream))
+        if summary is None:
+            _check(lib().rkv_hsa_decode(_ptr(Q), _ptr(K), _ptr(V), *common), "rkv_hsa_decode")
+        else:
+            _check(lib().rkv_hsa_decode_summary(_ptr(Q), _ptr(K), _ptr(V), _ptr(summary), *common),
+                   "rkv_hsa_decode_summary")
         return self.O
 
     def status(self, stream=None) -> int:
