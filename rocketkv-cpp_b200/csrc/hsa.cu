@@ -1019,44 +1019,51 @@ __global__ void __launch_bounds__(kSumBuildNT) hsa_summary_build_kernel(const ui
 
 // Phases 0 and 1 from the page summaries.  Per tile of TP pages one bulk copy
 // per selected dimension brings its sign-chosen run of extrema into shared
-// memory (mbarrier completion, bounded wait; several CTAs per SM overlap their
-// tiles).  A quad of four lanes scores four pages, lane j taking the chunks
-// j, j + 4, ... as in hsa_scan_kernel, each page pair in the two lanes of
-// paired fp32 FMAs.  Per page and head the sum is the scan's: per 16-byte
+// memory (mbarrier completion, bounded wait; three CTAs per SM overlap their
+// tiles).  Each lane scores PPL consecutive pages over every selected
+// dimension, so the list entries it reads (tile row and s q per head) are the
+// same on every lane of the warp: one broadcast load per entry, no padding,
+// no shuffles.  Per page and head the sum is hsa_scan_kernel's: per 16-byte
 // chunk an even and an odd fused multiply-add chain over the selected
-// dimensions (the unselected ones add exact zeros there), chunk value
-// even + odd; the lane's chunks added pairwise; the lanes as
-// (l0 + l2) + (l1 + l3) by two shuffles.  Each chunk keeps lists of its
-// selected even and odd dimensions (tile row and s q per head); the lanes of
-// a warp run the longest list of their slot, the shorter ones padded with an
-// all-zero tile row and q = 0, so that control flow is the same on every
-// lane and the padding adds exact zeros (0 x 0).  The representatives are clamped at -FLT_MAX, which
-// is the scan's result on every page (the clamp only changes a representative
-// that makes a page's sum non-finite, where the scan recomputes clamped).
+// dimensions (the unselected ones add exact zeros there, and a chain that
+// starts at +0 never reaches -0, so skipping them changes nothing), chunk
+// value even + odd; the chunks j, j + 4, j + 8, ... of quad lane j added
+// pairwise as a balanced tree (kept here as a binary-counter stack), and the
+// four lane totals as (l0 + l2) + (l1 + l3); then the IEEE division by the
+// head's scale.  The representatives are clamped at -FLT_MAX, which is the
+// scan's result on every page (the clamp only changes a representative that
+// makes a page's sum non-finite, where the scan recomputes clamped).
 constexpr int kSumScanNT = 128;
+constexpr int kSumTileBudget = 72704;  // tile bytes per CTA: three CTAs per SM with their static part
+
+__host__ __device__ constexpr int sumscan_ppl(int maxg) { return maxg <= 4 ? 4 : 2; }
+// phase-0 scratch at the start of the dynamic buffer (dead before the first tile lands)
+__host__ __device__ constexpr int sumscan_scratch(int maxg, int d) { return (maxg * d + 3 * d + maxg) * 4 + 2 * d; }
 
 template <typename T, int D, int MAXG>
-__global__ void __launch_bounds__(kSumScanNT) hsa_sumscan_kernel(const HsaArgs a) {
+__global__ void __launch_bounds__(kSumScanNT, 3) hsa_sumscan_kernel(const HsaArgs a) {
     constexpr int ES = (int)sizeof(T);
     constexpr int CD = 16 / ES, NCH = D / CD, NSL = NCH / 4;
     constexpr int TOP = NSL >= 16 ? 4 : NSL >= 8 ? 3 : NSL >= 4 ? 2 : 1;  // log2(NSL)
-    constexpr int LEV = TOP + 1;                                            // pairwise-tree stack depth per lane
-    static_assert((1 << TOP) == NSL, "slots per lane: a power of two up to 16");
+    static_assert((1 << TOP) == NSL, "slots per quad lane: a power of two from 2 to 16");
+    constexpr int PPL = sumscan_ppl(MAXG), PV = PPL / 2;  // pages per lane, page pairs per lane
+    constexpr int QW = (MAXG + 1 + 3) / 4 * 4;             // floats per list entry
     constexpr int DPT = (D + kSumScanNT - 1) / kSumScanNT;  // dimensions per thread in phase 0
-    extern __shared__ __align__(128) uint8_t sbuf[];         // [nr][TP] extrema
-    __shared__ __align__(16) float qf[MAXG * D];
-    constexpr int QW = (MAXG + 1 + 3) / 4 * 4;  // floats per list entry: the tile row, then s q per head
-    constexpr int HALF = CD / 2;                // even (odd) dimensions per chunk
-    constexpr int CST = 2 * HALF * QW + 4;      // floats per chunk of lists (padded: quad lanes in other banks)
-    __shared__ __align__(16) float ent[NCH * CST];
-    __shared__ int maxe[NSL], maxo[NSL];
-    __shared__ float sabs[D], qsum[D];
-    __shared__ int Rl[D];
-    __shared__ unsigned char dsel[D], dneg[D];
+    extern __shared__ __align__(128) uint8_t sbuf[];        // [nr][TP] extrema (phase-0 scratch first)
+    __shared__ __align__(16) float ent[D * QW];             // the lists, in processing order
+    __shared__ unsigned short srow[D];                      // summary row of tile row k: s D + d
+    __shared__ unsigned char cnt[2 * NCH];                  // list lengths, [chunk][parity]
     __shared__ uint32_t selw[D / 32];
-    __shared__ float sumall[MAXG], cscale[MAXG];
+    __shared__ float cscale[MAXG];
     __shared__ int scan_tmp[33];
     __shared__ uint64_t full;
+    float* qf = reinterpret_cast<float*>(sbuf);  // [G][D]
+    float* sabs = qf + MAXG * D;
+    float* qsum = sabs + D;
+    int* Rl = reinterpret_cast<int*>(qsum + D);
+    float* sumall = reinterpret_cast<float*>(Rl + D);
+    unsigned char* dsel = reinterpret_cast<unsigned char*>(sumall + MAXG);
+    unsigned char* dneg = dsel + D;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int split = blockIdx.x, hc = blockIdx.y, b = blockIdx.z, hk = a.head_begin + hc;
@@ -1140,165 +1147,178 @@ __global__ void __launch_bounds__(kSumScanNT) hsa_sumscan_kernel(const HsaArgs a
         for (int e = 0; e < 32; ++e) m |= (uint32_t)dsel[tid * 32 + e] << e;
         selw[tid] = m;
     }
+    for (int k = tid; k < nr; k += kSumScanNT) srow[k] = (unsigned short)(dneg[Rl[k]] * D + Rl[k]);
+    for (int x = tid; x < 2 * NCH; x += kSumScanNT) {  // list lengths: selected dimensions of a chunk and parity
+        const int c = x >> 1, par = x & 1;
+        int n = 0;
+        for (int e = par; e < CD; e += 2) n += dsel[c * CD + e];
+        cnt[x] = (unsigned char)n;
+    }
     __syncthreads();
-    if (tid < NCH) {  // chunk tid: its selected even / odd dimensions, ascending, then padding entries
-        const int c = tid;
-        int k = 0;
-        for (int d = 0; d < c * CD; ++d) k += dsel[d];  // tile row of the chunk's first selected dimension
-        int n[2] = {0, 0};
-        for (int e = 0; e < CD; ++e) {
-            const int d = c * CD + e, par = e & 1;
+    if (tid < NCH) {  // chunk tid: its entries at its place in the processing order
+        const int c = tid, jc = c & 3, ic = c >> 2;
+        const int jrank = jc == 0 ? 0 : jc == 2 ? 1 : jc == 1 ? 2 : 3;  // quad lanes taken as 0, 2, 1, 3
+        int e = 0;
+        for (int c2 = 0; c2 < NCH; ++c2) {
+            const int j2 = c2 & 3, r2 = j2 == 0 ? 0 : j2 == 2 ? 1 : j2 == 1 ? 2 : 3;
+            if (r2 < jrank || (r2 == jrank && (c2 >> 2) < ic)) e += cnt[2 * c2] + cnt[2 * c2 + 1];
+        }
+        int k = 0;  // tile row of the chunk's first selected dimension
+        for (int w = 0; w < (c * CD) / 32; ++w) k += __popc(selw[w]);
+        if ((c * CD) % 32) k += __popc(selw[(c * CD) / 32] & ((1u << ((c * CD) % 32)) - 1u));
+        int ke = k, e_odd = e + cnt[2 * c];
+        for (int x = 0; x < CD; ++x) {
+            const int d = c * CD + x;
             if (!dsel[d]) continue;
-            float* en = ent + c * CST + (par * HALF + n[par]) * QW;
-            en[0] = __int_as_float(k++);
+            float* en = ent + ((x & 1) ? e_odd++ : e++) * QW;
+            en[0] = __int_as_float(ke++ * TP * ES);  // byte offset of the tile row
             for (int h = 0; h < QW - 1; ++h) {
                 const float q = h < G ? qf[h * D + d] : 0.0f;
                 en[1 + h] = dneg[d] ? -q : q;
             }
-            ++n[par];
         }
-        for (int par = 0; par < 2; ++par)
-            for (int u = n[par]; u < HALF; ++u) {
-                float* en = ent + c * CST + (par * HALF + u) * QW;
-                en[0] = __int_as_float(nr);  // the zero row
-                for (int h = 0; h < QW - 1; ++h) en[1 + h] = 0.0f;
-            }
-        reinterpret_cast<int*>(ent + c * CST)[2 * HALF * QW] = n[0];
-        reinterpret_cast<int*>(ent + c * CST)[2 * HALF * QW + 1] = n[1];
     }
-    __syncthreads();
-    if (tid < NSL) {  // the longest lists of slot tid over the four lanes
-        int me = 0, mo = 0;
-        for (int jj = 0; jj < 4; ++jj) {
-            const int* cn = reinterpret_cast<const int*>(ent + (jj + 4 * tid) * CST) + 2 * HALF * QW;
-            me = max(me, cn[0]);
-            mo = max(mo, cn[1]);
-        }
-        maxe[tid] = me;
-        maxo[tid] = mo;
-    }
+    fence_proxy_async();  // the scratch's generic writes ordered before the tiles' async copies
     __syncthreads();
 
     // ---- phase 1: page logits from the summaries ----
     const uint8_t* Sb = a.summary + (size_t)b * a.sum_stride + (size_t)hk * 2 * D * a.npp * ES;
     const int ntile = (p_end - p_beg + TP - 1) / TP;
-    const int j = tid & 3, qd = tid >> 2;  // lane of the quad, quad
-    float my_scale[(MAXG + 3) / 4];
+    const int wp0 = warp * 32 * PPL, lp = wp0 + lane * PPL;  // the warp's and the lane's first page in a tile
+    float rscale[MAXG];
 #pragma unroll
-    for (int u = 0; u < (MAXG + 3) / 4; ++u) my_scale[u] = (j + 4 * u < G) ? cscale[j + 4 * u] : 1.0f;
-    const size_t row_b = (size_t)TP * ES + 16;  // bytes per dimension row of the tile (padded: other banks)
-    for (int x = tid; x < (int)(row_b / 16); x += kSumScanNT)  // row nr: zeros, the padding entries' row
-        reinterpret_cast<uint4*>(sbuf + (size_t)nr * row_b)[x] = make_uint4(0u, 0u, 0u, 0u);
-    __syncthreads();
+    for (int h = 0; h < MAXG; ++h) rscale[h] = h < G ? cscale[h] : 1.0f;
     for (int t = 0; t < ntile; ++t) {
         const int tp0 = p_beg + t * TP;
         if (warp == 0) {  // the tile's copies, spread over the lanes of warp 0
             const int np = min(TP, a.npp - tp0);  // whole 8-page groups: bytes a multiple of 16
-            fence_proxy_async();
             if (lane == 0) mbar_arrive_expect_tx(&full, (uint32_t)((size_t)nr * np * ES));
             __syncwarp();
-            for (int k = lane; k < nr; k += 32) {
-                const int d = Rl[k];
-                bulk_load(sbuf + (size_t)k * row_b, Sb + ((size_t)(dneg[d] * D + d) * a.npp + tp0) * ES,
-                          (uint32_t)(np * ES), &full);
-            }
+            for (int k = lane; k < nr; k += 32)
+                bulk_load(sbuf + (size_t)k * TP * ES, Sb + ((size_t)srow[k] * a.npp + tp0) * ES, (uint32_t)(np * ES),
+                          &full);
         }
         const bool w = mbar_wait_bounded(&full, (uint32_t)(t & 1), a.err);
         if (!__syncthreads_and(w)) {
             if (tid == 0) mbar_wait_bounded(&full, (uint32_t)(t & 1), a.err);  // the copies land before the exit
             return;
         }
-        // the same trip count for every lane (the quad shuffles below take the whole warp): quads past
-        // the unit's end score stale columns of the tile buffer and write nothing
-        for (int g0 = 4 * qd; g0 < TP; g0 += 4 * (kSumScanNT / 4)) {  // four pages per quad
-            const int p0 = tp0 + g0;
-            const uint8_t* col = sbuf + (size_t)g0 * ES;
-            float2 sv[NSL][MAXG][2];  // [slot][head][page pair]
+        if (wp0 < TP && tp0 + wp0 < p_end) {  // warp-uniform: warps past the tile or the unit's end skip
+            const uint8_t* col = sbuf + (size_t)lp * ES;
+            const float4* ep = reinterpret_cast<const float4*>(ent);
+            float2 A[MAXG][PV], B[MAXG][PV];
 #pragma unroll
-            for (int i = 0; i < NSL; ++i) {
-                const float* ec = ent + (j + 4 * i) * CST;
-                float2 acc[2][MAXG][2];  // [parity][head][page pair]
+            for (int jj = 0; jj < 4; ++jj) {  // quad lanes 0, 2, 1, 3
+                const int j = jj == 0 ? 0 : jj == 1 ? 2 : jj == 2 ? 1 : 3;
+                float2 stk[TOP][MAXG][PV];
+                float2 cur[MAXG][PV];
 #pragma unroll
-                for (int par = 0; par < 2; ++par)
+                for (int i = 0; i < NSL; ++i) {
+                    const int c = j + 4 * i;
+                    float2 acc[2][MAXG][PV];
 #pragma unroll
-                    for (int h = 0; h < MAXG; ++h) acc[par][h][0] = acc[par][h][1] = make_float2(0.0f, 0.0f);
+                    for (int par = 0; par < 2; ++par) {
 #pragma unroll
-                for (int par = 0; par < 2; ++par) {
-                    const int nu = par ? maxo[i] : maxe[i];  // the same on every lane of the warp
-                    for (int u = 0; u < nu; ++u) {
-                        const float4* en = reinterpret_cast<const float4*>(ec + (par * HALF + u) * QW);
-                        const float4 e0 = en[0];
-                        const int k = __float_as_int(e0.x);
-                        float2 P0, P1;  // pages 0-1, 2-3
-                        if (ES == 2) {
-                            const uint2 w4 = *reinterpret_cast<const uint2*>(col + (size_t)k * row_b);
-                            P0 = make_float2(__uint_as_float(w4.x << 16), __uint_as_float(w4.x & 0xffff0000u));
-                            P1 = make_float2(__uint_as_float(w4.y << 16), __uint_as_float(w4.y & 0xffff0000u));
-                        } else {
-                            const float4 f4 = *reinterpret_cast<const float4*>(col + (size_t)k * row_b);
-                            P0 = make_float2(f4.x, f4.y);
-                            P1 = make_float2(f4.z, f4.w);
-                        }
-                        P0 = make_float2(fmaxf(P0.x, -FLT_MAX), fmaxf(P0.y, -FLT_MAX));
-                        P1 = make_float2(fmaxf(P1.x, -FLT_MAX), fmaxf(P1.y, -FLT_MAX));
-                        float qh[QW];
-                        qh[0] = e0.y;
-                        qh[1] = e0.z;
-                        qh[2] = e0.w;
+                        for (int h = 0; h < MAXG; ++h)
 #pragma unroll
-                        for (int uu = 1; uu < QW / 4; ++uu) {
-                            const float4 ex = en[uu];
-                            qh[4 * uu - 1] = ex.x;
-                            qh[4 * uu] = ex.y;
-                            qh[4 * uu + 1] = ex.z;
-                            qh[4 * uu + 2] = ex.w;
-                        }
+                            for (int v = 0; v < PV; ++v) acc[par][h][v] = make_float2(0.0f, 0.0f);
+                        const int n = cnt[2 * c + par];  // the same on every lane
+                        for (int u = 0; u < n; ++u, ep += QW / 4) {
+                            const float4 e0 = ep[0];
+                            const uint8_t* src = col + __float_as_int(e0.x);
+                            float2 P[PV];
+                            if (ES == 2) {
+                                if (PPL == 4) {
+                                    const uint2 w4 = *reinterpret_cast<const uint2*>(src);
+                                    P[0] = make_float2(__uint_as_float(w4.x << 16), __uint_as_float(w4.x & 0xffff0000u));
+                                    P[PV - 1] =
+                                        make_float2(__uint_as_float(w4.y << 16), __uint_as_float(w4.y & 0xffff0000u));
+                                } else {
+                                    const uint32_t w2 = *reinterpret_cast<const uint32_t*>(src);
+                                    P[0] = make_float2(__uint_as_float(w2 << 16), __uint_as_float(w2 & 0xffff0000u));
+                                }
+                            } else {
+                                if (PPL == 4) {
+                                    const float4 f4 = *reinterpret_cast<const float4*>(src);
+                                    P[0] = make_float2(f4.x, f4.y);
+                                    P[PV - 1] = make_float2(f4.z, f4.w);
+                                } else {
+                                    P[0] = *reinterpret_cast<const float2*>(src);
+                                }
+                            }
 #pragma unroll
-                        for (int h = 0; h < MAXG; ++h) {
-                            const float2 q2 = make_float2(qh[h], qh[h]);
-                            ffma2(acc[par][h][0], q2, P0);
-                            ffma2(acc[par][h][1], q2, P1);
+                            for (int v = 0; v < PV; ++v)
+                                P[v] = make_float2(fmaxf(P[v].x, -FLT_MAX), fmaxf(P[v].y, -FLT_MAX));
+                            float qh[QW];
+                            qh[0] = e0.y;
+                            qh[1] = e0.z;
+                            qh[2] = e0.w;
+#pragma unroll
+                            for (int uu = 1; uu < QW / 4; ++uu) {
+                                const float4 ex = ep[uu];
+                                qh[4 * uu - 1] = ex.x;
+                                qh[4 * uu] = ex.y;
+                                qh[4 * uu + 1] = ex.z;
+                                qh[4 * uu + 2] = ex.w;
+                            }
+#pragma unroll
+                            for (int h = 0; h < MAXG; ++h)
+#pragma unroll
+                                for (int v = 0; v < PV; ++v) ffma2(acc[par][h][v], make_float2(qh[h], qh[h]), P[v]);
                         }
                     }
+#pragma unroll
+                    for (int h = 0; h < MAXG; ++h)
+#pragma unroll
+                        for (int v = 0; v < PV; ++v) cur[h][v] = __fadd2_rn(acc[0][h][v], acc[1][h][v]);
+                    // balanced pairwise tree over the slots: merge while the low bits of i are ones
+#pragma unroll
+                    for (int l = 0; l < TOP; ++l)
+                        if (((i + 1) & ((2 << l) - 1)) == 0)
+#pragma unroll
+                            for (int h = 0; h < MAXG; ++h)
+#pragma unroll
+                                for (int v = 0; v < PV; ++v) cur[h][v] = __fadd2_rn(stk[l][h][v], cur[h][v]);
+                    // then keep it at the level of its trailing ones (the last slot leaves the total in cur)
+#pragma unroll
+                    for (int l = 0; l < TOP; ++l)
+                        if (((i + 1) & ((2 << l) - 1)) == (1 << l))
+#pragma unroll
+                            for (int h = 0; h < MAXG; ++h)
+#pragma unroll
+                                for (int v = 0; v < PV; ++v) stk[l][h][v] = cur[h][v];
                 }
 #pragma unroll
-                for (int h = 0; h < MAXG; ++h) {
-                    sv[i][h][0] = __fadd2_rn(acc[0][h][0], acc[1][h][0]);
-                    sv[i][h][1] = __fadd2_rn(acc[0][h][1], acc[1][h][1]);
-                }
+                for (int h = 0; h < MAXG; ++h)
+#pragma unroll
+                    for (int v = 0; v < PV; ++v) {
+                        if (jj == 0) A[h][v] = cur[h][v];
+                        if (jj == 1) A[h][v] = __fadd2_rn(A[h][v], cur[h][v]);
+                        if (jj == 2) B[h][v] = cur[h][v];
+                        if (jj == 3) B[h][v] = __fadd2_rn(B[h][v], cur[h][v]);
+                    }
             }
-#pragma unroll
-            for (int w2 = 1; w2 < NSL; w2 *= 2)
-#pragma unroll
-                for (int i = 0; i < NSL; i += 2 * w2)
-#pragma unroll
-                    for (int h = 0; h < MAXG; ++h) {
-                        sv[i][h][0] = __fadd2_rn(sv[i][h][0], sv[i + w2][h][0]);
-                        sv[i][h][1] = __fadd2_rn(sv[i][h][1], sv[i + w2][h][1]);
-                    }
-            // (l0 + l2) + (l1 + l3) over the quad, as quad_sum
-            float v[MAXG][4];
+            const int pa = tp0 + lp;
 #pragma unroll
             for (int h = 0; h < MAXG; ++h) {
-                v[h][0] = sv[0][h][0].x;
-                v[h][1] = sv[0][h][0].y;
-                v[h][2] = sv[0][h][1].x;
-                v[h][3] = sv[0][h][1].y;
+                if (h >= G) break;  // uniform
+                float o[PPL];
 #pragma unroll
-                for (int pg = 0; pg < 4; ++pg) {
-                    v[h][pg] = __fadd_rn(v[h][pg], __shfl_xor_sync(0xffffffffu, v[h][pg], 2));
-                    v[h][pg] = __fadd_rn(v[h][pg], __shfl_xor_sync(0xffffffffu, v[h][pg], 1));
+                for (int v = 0; v < PV; ++v) {
+                    const float2 s = __fadd2_rn(A[h][v], B[h][v]);
+                    o[2 * v] = __fdiv_rn(s.x, rscale[h]);
+                    o[2 * v + 1] = __fdiv_rn(s.y, rscale[h]);
                 }
-            }
+                float* dst = wl + (size_t)h * a.nch_pad + pa;
+                if (pa + PPL <= p_end) {
+                    if (PPL == 4)
+                        *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+                    else
+                        *reinterpret_cast<float2*>(dst) = make_float2(o[0], o[1]);
+                } else {
 #pragma unroll
-            for (int u = 0; u < (MAXG + 3) / 4; ++u) {
-                const int h = j + 4 * u;
-#pragma unroll
-                for (int hh = 0; hh < MAXG; ++hh) {
-                    if (hh != h || h >= G) continue;
-#pragma unroll
-                    for (int pg = 0; pg < 4; ++pg)
-                        if (p0 + pg < p_end) wl[(size_t)h * a.nch_pad + p0 + pg] = __fdiv_rn(v[hh][pg], my_scale[u]);
+                    for (int pg = 0; pg < PPL; ++pg)
+                        if (pa + pg < p_end) dst[pg] = o[pg];
                 }
             }
         }
@@ -1317,21 +1337,30 @@ int num_sms() {
 template <typename T, int D, int MAXG>
 int launch_t(HsaArgs a, int batch, cudaStream_t st) {
     if (a.nchunks > 0 && a.summary) {
-        // page logits from the summaries; enough CTAs to cover the GPU
+        // page logits from the summaries.  Tile: PPL pages per lane, whole warps, as many as the tile
+        // budget holds for the r selected runs (three CTAs per SM overlap their tiles)
+        constexpr int PPL = sumscan_ppl(MAXG), WP = 32 * PPL;
+        const int nr = a.r < D ? a.r : D;
+        const size_t run_b = (size_t)nr * sizeof(T);  // bytes per tile page
+        int tp = run_b > 0 ? (int)(kSumTileBudget / run_b) / WP * WP : kSumScanNT * PPL;
+        if (tp > kSumScanNT * PPL) tp = kSumScanNT * PPL;
+        if (tp < WP) tp = WP;
+        // enough CTAs to cover the GPU
         const long long units = (long long)batch * a.head_count;
-        const long long want = 4LL * num_sms();
+        const long long want = 3LL * num_sms();
         int splits = units >= want ? 1 : (int)((want + units - 1) / units);
-        const int max_splits = (a.nchunks + 2 * kSumScanNT - 1) / (2 * kSumScanNT);
+        const int max_splits = (a.nchunks + tp - 1) / tp;
         if (splits > max_splits) splits = max_splits;
         if (splits < 1) splits = 1;
-        // tile of TP = 2 x threads pages: one buffer of r runs (several CTAs per SM overlap)
-        const int tp = 2 * kSumScanNT;
         a.stage_rows = tp;
         a.pages_per_split = ((a.nchunks + splits - 1) / splits + tp - 1) / tp * tp;  // whole tiles
         a.splits = (a.nchunks + a.pages_per_split - 1) / a.pages_per_split;
-        const size_t smem = (size_t)((a.r < D ? a.r : D) + 1) * (tp * sizeof(T) + 16);  // + the zero row
+        const size_t tile = run_b * tp, scratch = (size_t)sumscan_scratch(MAXG, D);
+        const size_t smem = tile > scratch ? tile : scratch;
         auto fs = hsa_sumscan_kernel<T, D, MAXG>;
         if (cudaFuncSetAttribute(fs, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return RKV_ERR_CUDA;
+        if (cudaFuncSetAttribute(fs, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
             return RKV_ERR_CUDA;
         fs<<<dim3(a.splits, a.head_count, batch), kSumScanNT, smem, st>>>(a);
         if (cudaGetLastError() != cudaSuccess) return RKV_ERR_CUDA;
