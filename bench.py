@@ -117,10 +117,19 @@ class ClockSampler:
                  "-lms", "25"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
+        # the timed region starts once nvidia-smi samples: its start-up would otherwise stall the launches
+        self.first = []
+        if self.proc is not None:
+            import select
+            ready, _, _ = select.select([self.proc.stdout], [], [], 10.0)
+            if ready:
+                line = self.proc.stdout.readline()
+                if line.strip():
+                    self.first.append(line.strip())
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
+        self.lines = list(getattr(self, "first", []))
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -128,7 +137,7 @@ class ClockSampler:
             except Exception:
                 self.proc.kill()
                 out = ""
-            self.lines = [l for l in out.splitlines() if l.strip()]
+            self.lines += [l for l in out.splitlines() if l.strip()]
 
     def summary(self):
         sm, mx, reasons = [], None, set()

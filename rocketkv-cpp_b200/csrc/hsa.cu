@@ -1017,28 +1017,40 @@ __global__ void __launch_bounds__(kSumBuildNT) hsa_summary_build_kernel(const ui
     }
 }
 
-// Phases 0 and 1 from the page summaries.  Per tile of TP pages one bulk copy
-// per selected dimension brings its sign-chosen run of extrema into shared
-// memory (mbarrier completion, bounded wait; three CTAs per SM overlap their
-// tiles).  Each lane scores PPL consecutive pages over every selected
-// dimension, so the list entries it reads (tile row and s q per head) are the
-// same on every lane of the warp: one broadcast load per entry, no padding,
-// no shuffles.  Per page and head the sum is hsa_scan_kernel's: per 16-byte
-// chunk an even and an odd fused multiply-add chain over the selected
+// Phases 0 and 1 from the page summaries.  A tile is TP pages, a column of
+// 32 PPL pages per warp: lane l scores PPL consecutive pages over every
+// selected dimension, so the list entries it reads (the dimension's row in
+// the tile and s q per head) are the same on every lane of the warp: one
+// broadcast load per entry, no padding, no shuffles.  The rows of a tile,
+// one bulk copy per selected dimension, are kept in the order the lists take
+// them and loaded in two halves (the blocks of quad lanes 0, 2 and of 1, 3),
+// each on its own mbarrier with bounded waits: one half of the next tile is in
+// flight while the other half of this one is scored; several CTAs per SM
+// overlap as well.  Per page and head the sum is hsa_scan_kernel's: per
+// 16-byte chunk an even and an odd fused multiply-add chain over the selected
 // dimensions (the unselected ones add exact zeros there, and a chain that
 // starts at +0 never reaches -0, so skipping them changes nothing), chunk
-// value even + odd; the chunks j, j + 4, j + 8, ... of quad lane j added
-// pairwise as a balanced tree (kept here as a binary-counter stack), and the
-// four lane totals as (l0 + l2) + (l1 + l3); then the IEEE division by the
-// head's scale.  The representatives are clamped at -FLT_MAX, which is the
-// scan's result on every page (the clamp only changes a representative that
-// makes a page's sum non-finite, where the scan recomputes clamped).
+// value even + odd; the chunks j, j + 4, ... of quad lane j added pairwise as
+// a balanced tree (kept here as a binary-counter stack), and the four lane
+// totals as (l0 + l2) + (l1 + l3); then the IEEE division by the head's
+// scale.  The representatives are clamped at -FLT_MAX, which is the scan's
+// result on every page (the clamp only changes a representative that makes a
+// page's sum non-finite, where the scan recomputes clamped).
 constexpr int kSumScanNT = 128;
+constexpr int kSumScanWarps = kSumScanNT / 32;
 constexpr int kSumTileBudget = 72704;  // tile bytes per CTA: three CTAs per SM with their static part
 
-__host__ __device__ constexpr int sumscan_ppl(int maxg) { return maxg <= 4 ? 4 : 2; }
+__host__ __device__ constexpr int sumscan_ppl(int maxg, int es, int d) { return maxg <= 4 && es * d <= 512 ? 4 : 2; }
 // phase-0 scratch at the start of the dynamic buffer (dead before the first tile lands)
 __host__ __device__ constexpr int sumscan_scratch(int maxg, int d) { return (maxg * d + 3 * d + maxg) * 4 + 2 * d; }
+template <int B>
+struct VecBytes;
+template <>
+struct VecBytes<4> { using type = uint32_t; };
+template <>
+struct VecBytes<8> { using type = uint2; };
+template <>
+struct VecBytes<16> { using type = uint4; };
 
 template <typename T, int D, int MAXG>
 __global__ void __launch_bounds__(kSumScanNT, 3) hsa_sumscan_kernel(const HsaArgs a) {
@@ -1046,17 +1058,20 @@ __global__ void __launch_bounds__(kSumScanNT, 3) hsa_sumscan_kernel(const HsaArg
     constexpr int CD = 16 / ES, NCH = D / CD, NSL = NCH / 4;
     constexpr int TOP = NSL >= 16 ? 4 : NSL >= 8 ? 3 : NSL >= 4 ? 2 : 1;  // log2(NSL)
     static_assert((1 << TOP) == NSL, "slots per quad lane: a power of two from 2 to 16");
-    constexpr int PPL = sumscan_ppl(MAXG), PV = PPL / 2;  // pages per lane, page pairs per lane
+    constexpr int PPL = sumscan_ppl(MAXG, ES, D), PV = PPL / 2;  // pages per lane, page pairs per lane
+    constexpr int COLP = 32 * PPL;                         // pages per column: a warp's share of a tile
     constexpr int QW = (MAXG + 1 + 3) / 4 * 4;             // floats per list entry
     constexpr int DPT = (D + kSumScanNT - 1) / kSumScanNT;  // dimensions per thread in phase 0
-    extern __shared__ __align__(128) uint8_t sbuf[];        // [nr][TP] extrema (phase-0 scratch first)
-    __shared__ __align__(16) float ent[D * QW];             // the lists, in processing order
-    __shared__ unsigned short srow[D];                      // summary row of tile row k: s D + d
+    using RowV = typename VecBytes<ES * PPL>::type;         // a lane's extrema of one dimension
+    extern __shared__ __align__(128) uint8_t sbuf[];        // [nr][TP] extrema, list order (phase-0 scratch first)
+    __shared__ __align__(16) float ent[(D + 2) * QW];       // the lists, in processing order, + 2 blank
+    __shared__ unsigned short esrow[D];                     // summary row of entry e: s D + d
     __shared__ unsigned char cnt[2 * NCH];                  // list lengths, [chunk][parity]
+    __shared__ int ejs[5];                                  // first entry of each block
     __shared__ uint32_t selw[D / 32];
     __shared__ float cscale[MAXG];
     __shared__ int scan_tmp[33];
-    __shared__ uint64_t full;
+    __shared__ uint64_t full[2];
     float* qf = reinterpret_cast<float*>(sbuf);  // [G][D]
     float* sabs = qf + MAXG * D;
     float* qsum = sabs + D;
@@ -1067,16 +1082,12 @@ __global__ void __launch_bounds__(kSumScanNT, 3) hsa_sumscan_kernel(const HsaArg
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int split = blockIdx.x, hc = blockIdx.y, b = blockIdx.z, hk = a.head_begin + hc;
-    const int G = a.G, TP = a.stage_rows;  // pages per tile
+    const int G = a.G;
     const int p_beg = split * a.pages_per_split;
     const int p_end = min(a.nchunks, p_beg + a.pages_per_split);
     if (p_beg >= p_end) return;  // uniform
     const uint8_t* Qg = a.Q + (size_t)b * a.q_stride + (size_t)hk * G * D * sizeof(T);
     float* wl = a.wlogits + ((size_t)b * a.head_count + hc) * (size_t)G * a.nch_pad;
-    if (tid == 0) {
-        mbar_init(&full, 1);
-        fence_mbar_init();
-    }
     for (int e = tid; e < G * D; e += kSumScanNT) qf[e] = to_f<T>(reinterpret_cast<const T*>(Qg)[e]);
     __syncthreads();
     // ---- phase 0: group query statistics (rocket.cpp:197-250), as hsa_scan_kernel ----
@@ -1147,7 +1158,6 @@ __global__ void __launch_bounds__(kSumScanNT, 3) hsa_sumscan_kernel(const HsaArg
         for (int e = 0; e < 32; ++e) m |= (uint32_t)dsel[tid * 32 + e] << e;
         selw[tid] = m;
     }
-    for (int k = tid; k < nr; k += kSumScanNT) srow[k] = (unsigned short)(dneg[Rl[k]] * D + Rl[k]);
     for (int x = tid; x < 2 * NCH; x += kSumScanNT) {  // list lengths: selected dimensions of a chunk and parity
         const int c = x >> 1, par = x & 1;
         int n = 0;
@@ -1155,149 +1165,179 @@ __global__ void __launch_bounds__(kSumScanNT, 3) hsa_sumscan_kernel(const HsaArg
         cnt[x] = (unsigned char)n;
     }
     __syncthreads();
-    if (tid < NCH) {  // chunk tid: its entries at its place in the processing order
+    if (tid < 4) {  // block tid (quad lane 0, 2, 1, 3 for tid 0, 1, 2, 3): its first entry
+        int e = 0;
+        for (int c2 = 0; c2 < NCH; ++c2) {
+            const int j2 = c2 & 3, r2 = j2 == 0 ? 0 : j2 == 2 ? 1 : j2 == 1 ? 2 : 3;
+            if (r2 < tid) e += cnt[2 * c2] + cnt[2 * c2 + 1];
+        }
+        ejs[tid] = e;
+        if (tid == 0) ejs[4] = nr;
+    }
+    if (tid < NCH) {  // chunk tid: its entries at their place in the processing order
         const int c = tid, jc = c & 3, ic = c >> 2;
-        const int jrank = jc == 0 ? 0 : jc == 2 ? 1 : jc == 1 ? 2 : 3;  // quad lanes taken as 0, 2, 1, 3
+        const int jrank = jc == 0 ? 0 : jc == 2 ? 1 : jc == 1 ? 2 : 3;
         int e = 0;
         for (int c2 = 0; c2 < NCH; ++c2) {
             const int j2 = c2 & 3, r2 = j2 == 0 ? 0 : j2 == 2 ? 1 : j2 == 1 ? 2 : 3;
             if (r2 < jrank || (r2 == jrank && (c2 >> 2) < ic)) e += cnt[2 * c2] + cnt[2 * c2 + 1];
         }
-        int k = 0;  // tile row of the chunk's first selected dimension
-        for (int w = 0; w < (c * CD) / 32; ++w) k += __popc(selw[w]);
-        if ((c * CD) % 32) k += __popc(selw[(c * CD) / 32] & ((1u << ((c * CD) % 32)) - 1u));
-        int ke = k, e_odd = e + cnt[2 * c];
+        int e_odd = e + cnt[2 * c];
         for (int x = 0; x < CD; ++x) {
             const int d = c * CD + x;
             if (!dsel[d]) continue;
-            float* en = ent + ((x & 1) ? e_odd++ : e++) * QW;
-            en[0] = __int_as_float(ke++ * TP * ES);  // byte offset of the tile row
+            const int en_i = (x & 1) ? e_odd++ : e++;
+            float* en = ent + en_i * QW;
+            en[0] = __int_as_float(en_i * a.stage_rows * ES);  // byte offset of the row in the tile
             for (int h = 0; h < QW - 1; ++h) {
                 const float q = h < G ? qf[h * D + d] : 0.0f;
                 en[1 + h] = dneg[d] ? -q : q;
             }
+            esrow[en_i] = (unsigned short)(dneg[d] * D + d);
         }
     }
+    for (int x = tid; x < 2 * QW; x += kSumScanNT) ent[nr * QW + x] = 0.0f;  // blank entries for the prefetch
+    if (tid < 2) mbar_init(&full[tid], 1);
+    fence_mbar_init();
     fence_proxy_async();  // the scratch's generic writes ordered before the tiles' async copies
     __syncthreads();
 
     // ---- phase 1: page logits from the summaries ----
+    // Tiles of TP pages; the rows of a tile are loaded in two halves (blocks 0-1 and 2-3), each on its own
+    // mbarrier, so that one half of the next tile is in flight while the other half of this one is scored.
     const uint8_t* Sb = a.summary + (size_t)b * a.sum_stride + (size_t)hk * 2 * D * a.npp * ES;
+    const int TP = a.stage_rows;
     const int ntile = (p_end - p_beg + TP - 1) / TP;
-    const int wp0 = warp * 32 * PPL, lp = wp0 + lane * PPL;  // the warp's and the lane's first page in a tile
+    const int wp0 = warp * COLP, lp = wp0 + lane * PPL;  // the warp's and the lane's first page in a tile
+    const int eh = ejs[2];                                // entries of the first half
+    auto issue = [&](int t, int half) {                   // warp 0: the copies of one half of tile t
+        const int tp0 = p_beg + t * TP;
+        const int np = min(TP, a.npp - tp0);  // whole 8-page groups: bytes a multiple of 16
+        const int e0 = half ? eh : 0, e1 = half ? nr : eh;
+        if (lane == 0) mbar_arrive_expect_tx(&full[half], (uint32_t)((size_t)(e1 - e0) * np * ES));
+        __syncwarp();
+        for (int e = e0 + lane; e < e1; e += 32)
+            bulk_load(sbuf + (size_t)e * TP * ES, Sb + ((size_t)esrow[e] * a.npp + tp0) * ES, (uint32_t)(np * ES),
+                      &full[half]);
+    };
+    if (warp == 0) {
+        issue(0, 0);
+        issue(0, 1);
+    }
     float rscale[MAXG];
 #pragma unroll
     for (int h = 0; h < MAXG; ++h) rscale[h] = h < G ? cscale[h] : 1.0f;
     for (int t = 0; t < ntile; ++t) {
         const int tp0 = p_beg + t * TP;
-        if (warp == 0) {  // the tile's copies, spread over the lanes of warp 0
-            const int np = min(TP, a.npp - tp0);  // whole 8-page groups: bytes a multiple of 16
-            if (lane == 0) mbar_arrive_expect_tx(&full, (uint32_t)((size_t)nr * np * ES));
-            __syncwarp();
-            for (int k = lane; k < nr; k += 32)
-                bulk_load(sbuf + (size_t)k * TP * ES, Sb + ((size_t)srow[k] * a.npp + tp0) * ES, (uint32_t)(np * ES),
-                          &full);
-        }
-        const bool w = mbar_wait_bounded(&full, (uint32_t)(t & 1), a.err);
-        if (!__syncthreads_and(w)) {
-            if (tid == 0) mbar_wait_bounded(&full, (uint32_t)(t & 1), a.err);  // the copies land before the exit
-            return;
-        }
-        if (wp0 < TP && tp0 + wp0 < p_end) {  // warp-uniform: warps past the tile or the unit's end skip
-            const uint8_t* col = sbuf + (size_t)lp * ES;
-            const float4* ep = reinterpret_cast<const float4*>(ent);
-            float2 A[MAXG][PV], B[MAXG][PV];
+        const bool active = wp0 < TP && tp0 + wp0 < p_end;  // warp-uniform: warps past the tile or the unit skip
+        const uint8_t* col = sbuf + (size_t)lp * ES;
+        float2 A[MAXG][PV], B[MAXG][PV];
 #pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {  // quad lanes 0, 2, 1, 3
-                const int j = jj == 0 ? 0 : jj == 1 ? 2 : jj == 2 ? 1 : 3;
-                float2 stk[TOP][MAXG][PV];
-                float2 cur[MAXG][PV];
+        for (int half = 0; half < 2; ++half) {
+            const bool ok = mbar_wait_bounded(&full[half], (uint32_t)(t & 1), a.err);
+            if (!__syncthreads_and(ok)) {  // timed out: the copies in flight land before the exit
+                if (tid == 0) {
+                    mbar_wait_bounded(&full[half], (uint32_t)(t & 1), a.err);
+                    if (half == 0) mbar_wait_bounded(&full[1], (uint32_t)(t & 1), a.err);
+                    if (half == 1 && t + 1 < ntile) mbar_wait_bounded(&full[0], (uint32_t)((t + 1) & 1), a.err);
+                }
+                return;
+            }
+            if (active) {
+                const float4* ep = reinterpret_cast<const float4*>(ent + ejs[2 * half] * QW);
+                // the entry stream, prefetched: entry e and its extrema, entry e + 1 (reads past the half stay in
+                // the tile and are not used)
+                float4 Ec = ep[0];
+                RowV Dc = *reinterpret_cast<const RowV*>(col + __float_as_int(Ec.x));
+                float4 En = ep[QW / 4];
 #pragma unroll
-                for (int i = 0; i < NSL; ++i) {
-                    const int c = j + 4 * i;
-                    float2 acc[2][MAXG][PV];
+                for (int jh = 0; jh < 2; ++jh) {
+                    const int jj = 2 * half + jh;
+                    const int j = jj == 0 ? 0 : jj == 1 ? 2 : jj == 2 ? 1 : 3;  // quad lanes 0, 2, 1, 3
+                    float2 stk[TOP][MAXG][PV];
+                    float2 cur[MAXG][PV];
 #pragma unroll
-                    for (int par = 0; par < 2; ++par) {
+                    for (int i = 0; i < NSL; ++i) {
+                        const int c = j + 4 * i;
+                        float2 acc[2][MAXG][PV];
 #pragma unroll
-                        for (int h = 0; h < MAXG; ++h)
-#pragma unroll
-                            for (int v = 0; v < PV; ++v) acc[par][h][v] = make_float2(0.0f, 0.0f);
-                        const int n = cnt[2 * c + par];  // the same on every lane
-                        for (int u = 0; u < n; ++u, ep += QW / 4) {
-                            const float4 e0 = ep[0];
-                            const uint8_t* src = col + __float_as_int(e0.x);
-                            float2 P[PV];
-                            if (ES == 2) {
-                                if (PPL == 4) {
-                                    const uint2 w4 = *reinterpret_cast<const uint2*>(src);
-                                    P[0] = make_float2(__uint_as_float(w4.x << 16), __uint_as_float(w4.x & 0xffff0000u));
-                                    P[PV - 1] =
-                                        make_float2(__uint_as_float(w4.y << 16), __uint_as_float(w4.y & 0xffff0000u));
-                                } else {
-                                    const uint32_t w2 = *reinterpret_cast<const uint32_t*>(src);
-                                    P[0] = make_float2(__uint_as_float(w2 << 16), __uint_as_float(w2 & 0xffff0000u));
-                                }
-                            } else {
-                                if (PPL == 4) {
-                                    const float4 f4 = *reinterpret_cast<const float4*>(src);
-                                    P[0] = make_float2(f4.x, f4.y);
-                                    P[PV - 1] = make_float2(f4.z, f4.w);
-                                } else {
-                                    P[0] = *reinterpret_cast<const float2*>(src);
-                                }
-                            }
-#pragma unroll
-                            for (int v = 0; v < PV; ++v)
-                                P[v] = make_float2(fmaxf(P[v].x, -FLT_MAX), fmaxf(P[v].y, -FLT_MAX));
-                            float qh[QW];
-                            qh[0] = e0.y;
-                            qh[1] = e0.z;
-                            qh[2] = e0.w;
-#pragma unroll
-                            for (int uu = 1; uu < QW / 4; ++uu) {
-                                const float4 ex = ep[uu];
-                                qh[4 * uu - 1] = ex.x;
-                                qh[4 * uu] = ex.y;
-                                qh[4 * uu + 1] = ex.z;
-                                qh[4 * uu + 2] = ex.w;
-                            }
+                        for (int par = 0; par < 2; ++par) {
 #pragma unroll
                             for (int h = 0; h < MAXG; ++h)
 #pragma unroll
-                                for (int v = 0; v < PV; ++v) ffma2(acc[par][h][v], make_float2(qh[h], qh[h]), P[v]);
+                                for (int v = 0; v < PV; ++v) acc[par][h][v] = make_float2(0.0f, 0.0f);
+                            const int n = cnt[2 * c + par];  // the same on every lane
+                            for (int u = 0; u < n; ++u, ep += QW / 4) {
+                                const float4 En2 = ep[2 * (QW / 4)];                                         // e + 2
+                                const RowV Dn = *reinterpret_cast<const RowV*>(col + __float_as_int(En.x));  // e + 1
+                                const uint32_t* wv = reinterpret_cast<const uint32_t*>(&Dc);
+                                float2 P[PV];
+#pragma unroll
+                                for (int v = 0; v < PV; ++v) {
+                                    if (ES == 2)
+                                        P[v] = make_float2(__uint_as_float(wv[v] << 16),
+                                                           __uint_as_float(wv[v] & 0xffff0000u));
+                                    else
+                                        P[v] = make_float2(__uint_as_float(wv[2 * v]), __uint_as_float(wv[2 * v + 1]));
+                                    P[v] = make_float2(fmaxf(P[v].x, -FLT_MAX), fmaxf(P[v].y, -FLT_MAX));
+                                }
+                                float qh[QW];
+                                qh[0] = Ec.y;
+                                qh[1] = Ec.z;
+                                qh[2] = Ec.w;
+#pragma unroll
+                                for (int uu = 1; uu < QW / 4; ++uu) {
+                                    const float4 ex = ep[uu];
+                                    qh[4 * uu - 1] = ex.x;
+                                    qh[4 * uu] = ex.y;
+                                    qh[4 * uu + 1] = ex.z;
+                                    qh[4 * uu + 2] = ex.w;
+                                }
+#pragma unroll
+                                for (int h = 0; h < MAXG; ++h)
+#pragma unroll
+                                    for (int v = 0; v < PV; ++v) ffma2(acc[par][h][v], make_float2(qh[h], qh[h]), P[v]);
+                                Ec = En;
+                                Dc = Dn;
+                                En = En2;
+                            }
                         }
+#pragma unroll
+                        for (int h = 0; h < MAXG; ++h)
+#pragma unroll
+                            for (int v = 0; v < PV; ++v) cur[h][v] = __fadd2_rn(acc[0][h][v], acc[1][h][v]);
+                        // balanced pairwise tree over the slots: merge while the low bits of i are ones
+#pragma unroll
+                        for (int l = 0; l < TOP; ++l)
+                            if (((i + 1) & ((2 << l) - 1)) == 0)
+#pragma unroll
+                                for (int h = 0; h < MAXG; ++h)
+#pragma unroll
+                                    for (int v = 0; v < PV; ++v) cur[h][v] = __fadd2_rn(stk[l][h][v], cur[h][v]);
+                        // then keep it at the level of its trailing ones (the last slot leaves the total in cur)
+#pragma unroll
+                        for (int l = 0; l < TOP; ++l)
+                            if (((i + 1) & ((2 << l) - 1)) == (1 << l))
+#pragma unroll
+                                for (int h = 0; h < MAXG; ++h)
+#pragma unroll
+                                    for (int v = 0; v < PV; ++v) stk[l][h][v] = cur[h][v];
                     }
 #pragma unroll
                     for (int h = 0; h < MAXG; ++h)
 #pragma unroll
-                        for (int v = 0; v < PV; ++v) cur[h][v] = __fadd2_rn(acc[0][h][v], acc[1][h][v]);
-                    // balanced pairwise tree over the slots: merge while the low bits of i are ones
-#pragma unroll
-                    for (int l = 0; l < TOP; ++l)
-                        if (((i + 1) & ((2 << l) - 1)) == 0)
-#pragma unroll
-                            for (int h = 0; h < MAXG; ++h)
-#pragma unroll
-                                for (int v = 0; v < PV; ++v) cur[h][v] = __fadd2_rn(stk[l][h][v], cur[h][v]);
-                    // then keep it at the level of its trailing ones (the last slot leaves the total in cur)
-#pragma unroll
-                    for (int l = 0; l < TOP; ++l)
-                        if (((i + 1) & ((2 << l) - 1)) == (1 << l))
-#pragma unroll
-                            for (int h = 0; h < MAXG; ++h)
-#pragma unroll
-                                for (int v = 0; v < PV; ++v) stk[l][h][v] = cur[h][v];
+                        for (int v = 0; v < PV; ++v) {
+                            if (jj == 0) A[h][v] = cur[h][v];
+                            if (jj == 1) A[h][v] = __fadd2_rn(A[h][v], cur[h][v]);
+                            if (jj == 2) B[h][v] = cur[h][v];
+                            if (jj == 3) B[h][v] = __fadd2_rn(B[h][v], cur[h][v]);
+                        }
                 }
-#pragma unroll
-                for (int h = 0; h < MAXG; ++h)
-#pragma unroll
-                    for (int v = 0; v < PV; ++v) {
-                        if (jj == 0) A[h][v] = cur[h][v];
-                        if (jj == 1) A[h][v] = __fadd2_rn(A[h][v], cur[h][v]);
-                        if (jj == 2) B[h][v] = cur[h][v];
-                        if (jj == 3) B[h][v] = __fadd2_rn(B[h][v], cur[h][v]);
-                    }
             }
+            __syncthreads();  // the half's rows are free for the next tile
+            if (warp == 0 && t + 1 < ntile) issue(t + 1, half);
+        }
+        if (active) {
             const int pa = tp0 + lp;
 #pragma unroll
             for (int h = 0; h < MAXG; ++h) {
@@ -1322,7 +1362,6 @@ __global__ void __launch_bounds__(kSumScanNT, 3) hsa_sumscan_kernel(const HsaArg
                 }
             }
         }
-        __syncthreads();  // the buffer is refilled for the next tile
     }
 }
 
@@ -1337,14 +1376,15 @@ int num_sms() {
 template <typename T, int D, int MAXG>
 int launch_t(HsaArgs a, int batch, cudaStream_t st) {
     if (a.nchunks > 0 && a.summary) {
-        // page logits from the summaries.  Tile: PPL pages per lane, whole warps, as many as the tile
-        // budget holds for the r selected runs (three CTAs per SM overlap their tiles)
-        constexpr int PPL = sumscan_ppl(MAXG), WP = 32 * PPL;
+        // page logits from the summaries.  Tile: whole columns of 32 PPL pages (a warp each), as many as
+        // the budget holds for the r selected rows (three CTAs per SM)
+        constexpr int PPL = sumscan_ppl(MAXG, (int)sizeof(T), D), COLP = 32 * PPL;
         const int nr = a.r < D ? a.r : D;
         const size_t run_b = (size_t)nr * sizeof(T);  // bytes per tile page
-        int tp = run_b > 0 ? (int)(kSumTileBudget / run_b) / WP * WP : kSumScanNT * PPL;
-        if (tp > kSumScanNT * PPL) tp = kSumScanNT * PPL;
-        if (tp < WP) tp = WP;
+        int tp = (int)(kSumTileBudget / run_b) / COLP * COLP;
+        if (tp > kSumScanWarps * COLP) tp = kSumScanWarps * COLP;
+        if (tp < COLP) tp = COLP;
+        a.stage_rows = tp;
         // enough CTAs to cover the GPU
         const long long units = (long long)batch * a.head_count;
         const long long want = 3LL * num_sms();
@@ -1352,7 +1392,6 @@ int launch_t(HsaArgs a, int batch, cudaStream_t st) {
         const int max_splits = (a.nchunks + tp - 1) / tp;
         if (splits > max_splits) splits = max_splits;
         if (splits < 1) splits = 1;
-        a.stage_rows = tp;
         a.pages_per_split = ((a.nchunks + splits - 1) / splits + tp - 1) / tp * tp;  // whole tiles
         a.splits = (a.nchunks + a.pages_per_split - 1) / a.pages_per_split;
         const size_t tile = run_b * tp, scratch = (size_t)sumscan_scratch(MAXG, D);
