@@ -969,16 +969,25 @@ __global__ void __launch_bounds__(kNT, 3) hsa_attn_kernel(const HsaArgs a) {
 
 constexpr int kSumBuildNT = 256;
 
+// Zeroes every item's non-finite masks ([KV head][D / 32] words after its extrema); one CTA per item.
+__global__ void hsa_summary_mask_clear(uint8_t* summary, long long sum_stride, long long mask_off, int words) {
+    uint32_t* m = reinterpret_cast<uint32_t*>(summary + (size_t)blockIdx.x * sum_stride + mask_off);
+    for (int x = threadIdx.x; x < words; x += blockDim.x) m[x] = 0u;
+}
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kSumBuildNT) hsa_summary_build_kernel(const uint8_t* K, long long kv_stride,
                                                                          int len_k, int C, int Lc, int nchunks,
                                                                          int npp, int TP, uint8_t* summary,
-                                                                         long long sum_stride) {
+                                                                         long long sum_stride, long long mask_off) {
     constexpr int ES = (int)sizeof(T), RB = D * ES, W = RB / 4;  // 32-bit words per row
     constexpr uint32_t FLIP = ES == 2 ? 0x80008000u : 0x80000000u;
     extern __shared__ __align__(16) uint8_t smraw[];
+    __shared__ uint32_t nfm[D / 32];        // dimensions with an extremum of -inf or NaN on this tile
     T* tile = reinterpret_cast<T*>(smraw);  // [2][D][TP]
     const int pt = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+    if (threadIdx.x < D / 32) nfm[threadIdx.x] = 0u;
+    __syncthreads();
     const int p0 = pt * TP;
     const uint8_t* Kh = K + (size_t)b * kv_stride + (size_t)hk * len_k * RB;
     for (int x = threadIdx.x; x < TP * W; x += kSumBuildNT) {
@@ -995,6 +1004,21 @@ __global__ void __launch_bounds__(kSumBuildNT) hsa_summary_build_kernel(const ui
                 n = Chunk<T>::wmax(n, v ^ FLIP);
             }
         }
+        if (page < nchunks) {  // -inf or NaN: the scan clamps such a representative at -FLT_MAX
+            uint32_t bits = 0u;
+            if (ES == 2) {
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                    const uint32_t x = (m >> (16 * hf)) & 0xffffu, y = (n >> (16 * hf)) & 0xffffu;
+                    if ((x & 0x7fffu) > 0x7f80u || x == 0xff80u || (y & 0x7fffu) > 0x7f80u || y == 0xff80u)
+                        bits |= 1u << ((2 * wd + hf) & 31);
+                }
+            } else if ((m & 0x7fffffffu) > 0x7f800000u || m == 0xff800000u || (n & 0x7fffffffu) > 0x7f800000u ||
+                       n == 0xff800000u) {
+                bits = 1u << (wd & 31);
+            }
+            if (bits) atomicOr(&nfm[(ES == 2 ? 2 * wd : wd) >> 5], bits);
+        }
         if (ES == 2) {
             tile[(0 * D + 2 * wd) * TP + p] = (T)(m & 0xffffu);
             tile[(0 * D + 2 * wd + 1) * TP + p] = (T)(m >> 16);
@@ -1006,6 +1030,9 @@ __global__ void __launch_bounds__(kSumBuildNT) hsa_summary_build_kernel(const ui
         }
     }
     __syncthreads();
+    if (threadIdx.x < D / 32 && nfm[threadIdx.x])
+        atomicOr(reinterpret_cast<uint32_t*>(summary + (size_t)b * sum_stride + mask_off) + hk * (D / 32) + threadIdx.x,
+                 nfm[threadIdx.x]);
     // rows of TP pages out, 16 bytes at a time (npp and TP are multiples of 8 pages)
     const int np = min(TP, npp - p0);
     const int vpr = np * ES / 16;
@@ -1051,6 +1078,111 @@ template <>
 struct VecBytes<8> { using type = uint2; };
 template <>
 struct VecBytes<16> { using type = uint4; };
+
+// One half of a tile for one warp (the blocks of quad lanes 0, 2 for HALF 0, of 1, 3 for HALF 1): the lane's
+// PPL pages over the half's list entries; A = l0 + l2, B = l1 + l3.  CLAMP: representatives clamped at
+// -FLT_MAX (needed only where a selected dimension has an extremum of -inf or NaN somewhere in the unit).
+template <typename T, int D, int MAXG, bool CLAMP, int HALF>
+__device__ __forceinline__ void sumscan_score_half(const float* ent, const unsigned char* cnt, int e_first,
+                                                   const uint8_t* col,
+                                                   float2 (&A)[MAXG][sumscan_ppl(MAXG, (int)sizeof(T), D) / 2],
+                                                   float2 (&B)[MAXG][sumscan_ppl(MAXG, (int)sizeof(T), D) / 2]) {
+    constexpr int ES = (int)sizeof(T);
+    constexpr int CD = 16 / ES, NCH = D / CD, NSL = NCH / 4;
+    constexpr int TOP = NSL >= 16 ? 4 : NSL >= 8 ? 3 : NSL >= 4 ? 2 : 1;  // log2(NSL)
+    constexpr int PPL = sumscan_ppl(MAXG, ES, D), PV = PPL / 2;
+    constexpr int QW = (MAXG + 1 + 3) / 4 * 4;
+    using RowV = typename VecBytes<ES * PPL>::type;
+    const float4* ep = reinterpret_cast<const float4*>(ent + e_first * QW);
+    // the entry stream, prefetched: entry e and its extrema, entry e + 1 (reads past the half stay in
+    // the tile and are not used)
+    float4 Ec = ep[0];
+    RowV Dc = *reinterpret_cast<const RowV*>(col + __float_as_int(Ec.x));
+    float4 En = ep[QW / 4];
+#pragma unroll
+    for (int jh = 0; jh < 2; ++jh) {
+        const int jj = 2 * HALF + jh;
+        const int j = jj == 0 ? 0 : jj == 1 ? 2 : jj == 2 ? 1 : 3;  // quad lanes 0, 2, 1, 3
+        float2 stk[TOP][MAXG][PV];
+        float2 cur[MAXG][PV];
+#pragma unroll
+        for (int i = 0; i < NSL; ++i) {
+            const int c = j + 4 * i;
+            float2 acc[2][MAXG][PV];
+#pragma unroll
+            for (int par = 0; par < 2; ++par) {
+#pragma unroll
+                for (int h = 0; h < MAXG; ++h)
+#pragma unroll
+                    for (int v = 0; v < PV; ++v) acc[par][h][v] = make_float2(0.0f, 0.0f);
+                const int n = cnt[2 * c + par];  // the same on every lane
+                for (int u = 0; u < n; ++u, ep += QW / 4) {
+                    const float4 En2 = ep[2 * (QW / 4)];                                         // e + 2
+                    const RowV Dn = *reinterpret_cast<const RowV*>(col + __float_as_int(En.x));  // e + 1
+                    const uint32_t* wv = reinterpret_cast<const uint32_t*>(&Dc);
+                    float2 P[PV];
+#pragma unroll
+                    for (int v = 0; v < PV; ++v) {
+                        if (ES == 2)
+                            P[v] = make_float2(__uint_as_float(wv[v] << 16),
+                                               __uint_as_float(wv[v] & 0xffff0000u));
+                        else
+                            P[v] = make_float2(__uint_as_float(wv[2 * v]), __uint_as_float(wv[2 * v + 1]));
+                        if (CLAMP) P[v] = make_float2(fmaxf(P[v].x, -FLT_MAX), fmaxf(P[v].y, -FLT_MAX));
+                    }
+                    float qh[QW];
+                    qh[0] = Ec.y;
+                    qh[1] = Ec.z;
+                    qh[2] = Ec.w;
+#pragma unroll
+                    for (int uu = 1; uu < QW / 4; ++uu) {
+                        const float4 ex = ep[uu];
+                        qh[4 * uu - 1] = ex.x;
+                        qh[4 * uu] = ex.y;
+                        qh[4 * uu + 1] = ex.z;
+                        qh[4 * uu + 2] = ex.w;
+                    }
+#pragma unroll
+                    for (int h = 0; h < MAXG; ++h)
+#pragma unroll
+                        for (int v = 0; v < PV; ++v) ffma2(acc[par][h][v], make_float2(qh[h], qh[h]), P[v]);
+                    Ec = En;
+                    Dc = Dn;
+                    En = En2;
+                }
+            }
+#pragma unroll
+            for (int h = 0; h < MAXG; ++h)
+#pragma unroll
+                for (int v = 0; v < PV; ++v) cur[h][v] = __fadd2_rn(acc[0][h][v], acc[1][h][v]);
+            // balanced pairwise tree over the slots: merge while the low bits of i are ones
+#pragma unroll
+            for (int l = 0; l < TOP; ++l)
+                if (((i + 1) & ((2 << l) - 1)) == 0)
+#pragma unroll
+                    for (int h = 0; h < MAXG; ++h)
+#pragma unroll
+                        for (int v = 0; v < PV; ++v) cur[h][v] = __fadd2_rn(stk[l][h][v], cur[h][v]);
+            // then keep it at the level of its trailing ones (the last slot leaves the total in cur)
+#pragma unroll
+            for (int l = 0; l < TOP; ++l)
+                if (((i + 1) & ((2 << l) - 1)) == (1 << l))
+#pragma unroll
+                    for (int h = 0; h < MAXG; ++h)
+#pragma unroll
+                        for (int v = 0; v < PV; ++v) stk[l][h][v] = cur[h][v];
+        }
+#pragma unroll
+        for (int h = 0; h < MAXG; ++h)
+#pragma unroll
+            for (int v = 0; v < PV; ++v) {
+                if (jj == 0) A[h][v] = cur[h][v];
+                if (jj == 1) A[h][v] = __fadd2_rn(A[h][v], cur[h][v]);
+                if (jj == 2) B[h][v] = cur[h][v];
+                if (jj == 3) B[h][v] = __fadd2_rn(B[h][v], cur[h][v]);
+            }
+    }
+}
 
 template <typename T, int D, int MAXG>
 __global__ void __launch_bounds__(kSumScanNT, 3) hsa_sumscan_kernel(const HsaArgs a) {
@@ -1153,10 +1285,13 @@ __global__ void __launch_bounds__(kSumScanNT, 3) hsa_sumscan_kernel(const HsaArg
         }
         cscale[tid] = __fsqrt_rn(__fmul_rn((float)D, __fdiv_rn(sk, __fadd_rn(sumall[tid], 1e-9f))));
     }
+    int nf = 0;  // a selected dimension with an extremum of -inf or NaN somewhere in the unit: clamp
     if (tid < D / 32) {
         uint32_t m = 0;
         for (int e = 0; e < 32; ++e) m |= (uint32_t)dsel[tid * 32 + e] << e;
         selw[tid] = m;
+        const uint32_t* nfm = reinterpret_cast<const uint32_t*>(a.summary + (size_t)b * a.sum_stride + a.sum_mask_off);
+        nf = (nfm[hk * (D / 32) + tid] & m) != 0u;
     }
     for (int x = tid; x < 2 * NCH; x += kSumScanNT) {  // list lengths: selected dimensions of a chunk and parity
         const int c = x >> 1, par = x & 1;
@@ -1200,7 +1335,7 @@ __global__ void __launch_bounds__(kSumScanNT, 3) hsa_sumscan_kernel(const HsaArg
     if (tid < 2) mbar_init(&full[tid], 1);
     fence_mbar_init();
     fence_proxy_async();  // the scratch's generic writes ordered before the tiles' async copies
-    __syncthreads();
+    const bool need_clamp = __syncthreads_or(nf) != 0;
 
     // ---- phase 1: page logits from the summaries ----
     // Tiles of TP pages; the rows of a tile are loaded in two halves (blocks 0-1 and 2-3), each on its own
@@ -1244,94 +1379,17 @@ __global__ void __launch_bounds__(kSumScanNT, 3) hsa_sumscan_kernel(const HsaArg
                 return;
             }
             if (active) {
-                const float4* ep = reinterpret_cast<const float4*>(ent + ejs[2 * half] * QW);
-                // the entry stream, prefetched: entry e and its extrema, entry e + 1 (reads past the half stay in
-                // the tile and are not used)
-                float4 Ec = ep[0];
-                RowV Dc = *reinterpret_cast<const RowV*>(col + __float_as_int(Ec.x));
-                float4 En = ep[QW / 4];
-#pragma unroll
-                for (int jh = 0; jh < 2; ++jh) {
-                    const int jj = 2 * half + jh;
-                    const int j = jj == 0 ? 0 : jj == 1 ? 2 : jj == 2 ? 1 : 3;  // quad lanes 0, 2, 1, 3
-                    float2 stk[TOP][MAXG][PV];
-                    float2 cur[MAXG][PV];
-#pragma unroll
-                    for (int i = 0; i < NSL; ++i) {
-                        const int c = j + 4 * i;
-                        float2 acc[2][MAXG][PV];
-#pragma unroll
-                        for (int par = 0; par < 2; ++par) {
-#pragma unroll
-                            for (int h = 0; h < MAXG; ++h)
-#pragma unroll
-                                for (int v = 0; v < PV; ++v) acc[par][h][v] = make_float2(0.0f, 0.0f);
-                            const int n = cnt[2 * c + par];  // the same on every lane
-                            for (int u = 0; u < n; ++u, ep += QW / 4) {
-                                const float4 En2 = ep[2 * (QW / 4)];                                         // e + 2
-                                const RowV Dn = *reinterpret_cast<const RowV*>(col + __float_as_int(En.x));  // e + 1
-                                const uint32_t* wv = reinterpret_cast<const uint32_t*>(&Dc);
-                                float2 P[PV];
-#pragma unroll
-                                for (int v = 0; v < PV; ++v) {
-                                    if (ES == 2)
-                                        P[v] = make_float2(__uint_as_float(wv[v] << 16),
-                                                           __uint_as_float(wv[v] & 0xffff0000u));
-                                    else
-                                        P[v] = make_float2(__uint_as_float(wv[2 * v]), __uint_as_float(wv[2 * v + 1]));
-                                    P[v] = make_float2(fmaxf(P[v].x, -FLT_MAX), fmaxf(P[v].y, -FLT_MAX));
-                                }
-                                float qh[QW];
-                                qh[0] = Ec.y;
-                                qh[1] = Ec.z;
-                                qh[2] = Ec.w;
-#pragma unroll
-                                for (int uu = 1; uu < QW / 4; ++uu) {
-                                    const float4 ex = ep[uu];
-                                    qh[4 * uu - 1] = ex.x;
-                                    qh[4 * uu] = ex.y;
-                                    qh[4 * uu + 1] = ex.z;
-                                    qh[4 * uu + 2] = ex.w;
-                                }
-#pragma unroll
-                                for (int h = 0; h < MAXG; ++h)
-#pragma unroll
-                                    for (int v = 0; v < PV; ++v) ffma2(acc[par][h][v], make_float2(qh[h], qh[h]), P[v]);
-                                Ec = En;
-                                Dc = Dn;
-                                En = En2;
-                            }
-                        }
-#pragma unroll
-                        for (int h = 0; h < MAXG; ++h)
-#pragma unroll
-                            for (int v = 0; v < PV; ++v) cur[h][v] = __fadd2_rn(acc[0][h][v], acc[1][h][v]);
-                        // balanced pairwise tree over the slots: merge while the low bits of i are ones
-#pragma unroll
-                        for (int l = 0; l < TOP; ++l)
-                            if (((i + 1) & ((2 << l) - 1)) == 0)
-#pragma unroll
-                                for (int h = 0; h < MAXG; ++h)
-#pragma unroll
-                                    for (int v = 0; v < PV; ++v) cur[h][v] = __fadd2_rn(stk[l][h][v], cur[h][v]);
-                        // then keep it at the level of its trailing ones (the last slot leaves the total in cur)
-#pragma unroll
-                        for (int l = 0; l < TOP; ++l)
-                            if (((i + 1) & ((2 << l) - 1)) == (1 << l))
-#pragma unroll
-                                for (int h = 0; h < MAXG; ++h)
-#pragma unroll
-                                    for (int v = 0; v < PV; ++v) stk[l][h][v] = cur[h][v];
-                    }
-#pragma unroll
-                    for (int h = 0; h < MAXG; ++h)
-#pragma unroll
-                        for (int v = 0; v < PV; ++v) {
-                            if (jj == 0) A[h][v] = cur[h][v];
-                            if (jj == 1) A[h][v] = __fadd2_rn(A[h][v], cur[h][v]);
-                            if (jj == 2) B[h][v] = cur[h][v];
-                            if (jj == 3) B[h][v] = __fadd2_rn(B[h][v], cur[h][v]);
-                        }
+                const int ef = ejs[2 * half];
+                if (half == 0) {
+                    if (need_clamp)
+                        sumscan_score_half<T, D, MAXG, true, 0>(ent, cnt, ef, col, A, B);
+                    else
+                        sumscan_score_half<T, D, MAXG, false, 0>(ent, cnt, ef, col, A, B);
+                } else {
+                    if (need_clamp)
+                        sumscan_score_half<T, D, MAXG, true, 1>(ent, cnt, ef, col, A, B);
+                    else
+                        sumscan_score_half<T, D, MAXG, false, 1>(ent, cnt, ef, col, A, B);
                 }
             }
             __syncthreads();  // the half's rows are free for the next tile
@@ -1546,7 +1604,8 @@ HsaSummaryShape hsa_summary_shape(const rkv_config& c, int dtype, int len_k, int
     s.Lc = h.Lc;
     s.nchunks = h.Lc > 0 ? (h.Lc + h.C - 1) / h.C : 0;  // every page, whether or not a call scores them
     s.npp = (s.nchunks + 7) / 8 * 8;
-    s.item_bytes = (long long)c.num_heads_kv * 2 * c.dim_head * s.npp * (dtype == RKV_F32 ? 4 : 2);
+    s.mask_off = (long long)c.num_heads_kv * 2 * c.dim_head * s.npp * (dtype == RKV_F32 ? 4 : 2);
+    s.item_bytes = s.mask_off + ((long long)c.num_heads_kv * (c.dim_head / 8) + 15) / 16 * 16;
     return s;
 }
 
@@ -1561,8 +1620,10 @@ static int build_t(const uint8_t* K, int HK, int len_k, long long kv_stride, con
     auto f = hsa_summary_build_kernel<T, D>;
     if (smem > 48 * 1024 && cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return RKV_ERR_CUDA;
+    hsa_summary_mask_clear<<<batch, 128, 0, st>>>(summary, s.item_bytes, s.mask_off, HK * (D / 32));
     dim3 grid((s.npp + TP - 1) / TP, HK, batch);
-    f<<<grid, kSumBuildNT, smem, st>>>(K, kv_stride, len_k, s.C, s.Lc, s.nchunks, s.npp, TP, summary, s.item_bytes);
+    f<<<grid, kSumBuildNT, smem, st>>>(K, kv_stride, len_k, s.C, s.Lc, s.nchunks, s.npp, TP, summary, s.item_bytes,
+                                        s.mask_off);
     return cudaGetLastError() == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
 }
 

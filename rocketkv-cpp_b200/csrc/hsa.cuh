@@ -42,13 +42,15 @@ struct HsaArgs {
     // NaN-ignoring max over a page's rows of x and of -x; the scan then reads these instead of K
     const uint8_t* summary;
     long long sum_stride;  // bytes between items
+    long long sum_mask_off;  // bytes from an item's summaries to its non-finite masks
     int npp;               // pages per summary row (nchunks rounded up to 8)
 };
 
 // Page-summary geometry for (cfg, len_k, recent_window): pages per row and bytes per item.
 struct HsaSummaryShape {
     int C, Lc, nchunks, npp;
-    long long item_bytes;
+    long long mask_off;    // bytes from an item's start to its masks: [KV head][D / 32] words, after the extrema
+    long long item_bytes;  // extrema [KV head][2][D][npp], then the masks (16-byte multiple)
 };
 HsaSummaryShape hsa_summary_shape(const rkv_config& c, int dtype, int len_k, int recent_window);
 int launch_hsa_summary_build(const uint8_t* K, int dtype, int D, int HK, int len_k, long long kv_stride,

@@ -508,6 +508,7 @@ int hsa_decode_impl(const void* Q, const void* K, const void* V, const void* sum
         const HsaSummaryShape sh = hsa_summary_shape(*cfg, dtype, len_k, recent_window);
         a.summary = static_cast<const uint8_t*>(summary);
         a.sum_stride = sh.item_bytes;
+        a.sum_mask_off = sh.mask_off;
         a.npp = sh.npp;
     }
     return launch_hsa(a, dtype, batch, st);

@@ -115,4 +115,6 @@ def test_summary_headline_batch_head_subset(cuda):
     assert rkv.lib().rkv_hsa_summary_size(__import__("ctypes").byref(to_rkv(cfg).c()), rkv.BF16, L, w, B,
                                           __import__("ctypes").byref(n)) == 0
     pages = (L - w + 1) // 2
-    assert n.value == B * 8 * 2 * 128 * ((pages + 7) // 8 * 8) * 2
+    # per item: the extrema [KV head][2][D][pages rounded to 8] in bf16, then a mask word per 32 dimensions
+    # and KV head (dimensions with an extremum of -inf or NaN), rounded to 16 bytes
+    assert n.value == B * (8 * 2 * 128 * ((pages + 7) // 8 * 8) * 2 + 8 * 128 // 8)
