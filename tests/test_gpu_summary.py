@@ -118,3 +118,31 @@ def test_summary_headline_batch_head_subset(cuda):
     # per item: the extrema [KV head][2][D][pages rounded to 8] in bf16, then a mask word per 32 dimensions
     # and KV head (dimensions with an extremum of -inf or NaN), rounded to 16 bytes
     assert n.value == B * (8 * 2 * 128 * ((pages + 7) // 8 * 8) * 2 + 8 * 128 // 8)
+
+
+def test_summary_survives_window_growth(cuda):
+    """Summaries built for (len_k, window) serve later steps whose appended
+    tokens joined the window (len_k + n, window + n): the compressed part, and
+    so the summaries, are unchanged.  Same selections and O as the stateless
+    call on the grown cache."""
+    import torch
+    B, L, w, n = 4, 1200, 8, 5
+    cfg = to_rkv(O.Config(num_heads=24, num_heads_kv=8, dim_head=128, topk_decode=128, chunk_size=2, r_dim=40))
+    g = torch.Generator(device=cuda).manual_seed(9)
+    Q = torch.randn((B, 24, 128), generator=g, device=cuda).to(torch.bfloat16)
+    K = torch.randn((B, 8, L + n, 128), generator=g, device=cuda).to(torch.bfloat16)
+    V = torch.randn((B, 8, L + n, 128), generator=g, device=cuda).to(torch.bfloat16)
+    S = rkv.HsaDecoder(cfg, L, B, cuda, recent_window=w).build_summary(K[:, :, :L].contiguous())
+    d = rkv.HsaDecoder(cfg, L + n, B, cuda, recent_window=w + n)
+    d(Q, K, V)
+    torch.cuda.synchronize()
+    ref = (d.O.cpu().numpy().copy(), d.sel.cpu().numpy().copy(), d.n_sel.cpu().numpy().copy())
+    d.O.zero_()
+    d.sel.zero_()
+    d.n_sel.zero_()
+    d(Q, K, V, summary=S)
+    torch.cuda.synchronize()
+    assert d.status() == 0
+    np.testing.assert_array_equal(d.n_sel.cpu().numpy(), ref[2])
+    np.testing.assert_array_equal(d.sel.cpu().numpy(), ref[1])
+    np.testing.assert_array_equal(d.O.cpu().numpy(), ref[0])
