@@ -146,3 +146,17 @@ def test_summary_survives_window_growth(cuda):
     np.testing.assert_array_equal(d.n_sel.cpu().numpy(), ref[2])
     np.testing.assert_array_equal(d.sel.cpu().numpy(), ref[1])
     np.testing.assert_array_equal(d.O.cpu().numpy(), ref[0])
+
+
+@pytest.mark.parametrize("D", [64, 128, 256])
+@pytest.mark.parametrize("G", [1, 2, 3, 4, 6])
+@pytest.mark.parametrize("bf16", [True, False])
+def test_summary_every_instantiation(D, G, bf16, cuda):
+    """Every head size, group size (kernel templates 1, 2, 3, 4, 8) and element
+    type of the summary scan, including fp32 at D 256 (two pages per lane):
+    the same selections and O as the stateless call."""
+    HK, L = 2, 333
+    cfg = O.Config(num_heads=G * HK, num_heads_kv=HK, dim_head=D, topk_decode=40, chunk_size=3, r_dim=D // 3)
+    q, K, V = rkvgen.stage2_inputs(100 + D + G, G * HK, HK, D, L)
+    for w in (0, 5):
+        both_paths(_dev(q[None], bf16, cuda), _dev(K[None], bf16, cuda), _dev(V[None], bf16, cuda), L, cfg, cuda, w=w)
