@@ -47,6 +47,15 @@ def set_workload(seqs: int, layers: int) -> None:
     SEQS, LAYERS = seqs, layers
 
 
+def ref_decode_params():
+    """The decode parameters through the reference's own compute_rocket_params
+    (oracle/_ref): the reference arm loads nothing of this repository's library."""
+    import types
+    import oracle
+    p = types.SimpleNamespace(**oracle.ref_compute_params(BUDGET, PROMPT, MAX_NEW, D, omp=True))
+    return p, p.prompt_budget + WINDOW
+
+
 def decode_params():
     import rocketkv_b200 as rkv
     p = rkv.compute_rocket_params(BUDGET, PROMPT, MAX_NEW, D)  # 3685 / 512 / 2 / 71
@@ -208,7 +217,7 @@ def cpu_decode_sample(n_items: int, seed: int = 1):
     import numpy as np
     import oracle
     import rkvgen
-    p, cache, _ = decode_params()
+    p, cache = ref_decode_params()
     cfg = oracle.Config(num_heads=H, num_heads_kv=HK, dim_head=D, topk_decode=p.k, chunk_size=p.chunk_size,
                         r_dim=p.r, compression_ratio=p.compression_ratio)
     L = oracle.ref(omp=True)
@@ -239,11 +248,11 @@ def cpu_evict_sample(n_calls: int):
 def run_reference(args, world, rank):
     if rank != 0:
         return
-    _, cache, _ = decode_params()
     if not ref_lib_available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/librocket_ref_omp.so was not built "
                           "(reference sources absent when build() ran)"}))
         return
+    _, cache = ref_decode_params()
     items_per_step = 16
     per_item = []
     for i in range(args.warmup + args.steps):
@@ -502,6 +511,279 @@ def e2e_resident_decode(dec, S, Qs, K, V, steps):
     return sum(ts), len(ts), h2d, oh.numel() * 4
 
 
+def _flush_events(device):
+    import torch
+    return torch.empty(256 << 20, dtype=torch.uint8, device=device), torch.cuda.current_stream()
+
+
+def _decode_call(cfg_c, Q, K, V, summary, dt, len_k, w, items, O, sel, sel_stride, nsel, ws, ws_bytes, stream):
+    """One stage-2 call through the C ABI with an explicit len_k and window
+    (the cache buffers keep room for the window's growth)."""
+    import ctypes
+    import rocketkv_b200 as rkv
+    common = (dt, len_k, w, items, Q[0].nbytes, K[0].nbytes, ctypes.byref(cfg_c), 0, 1, rkv._ptr(O), rkv._ptr(sel),
+              sel_stride, rkv._ptr(nsel), rkv._ptr(ws), ws_bytes, stream)
+    if summary is None:
+        st = rkv.lib().rkv_hsa_decode(rkv._ptr(Q), rkv._ptr(K), rkv._ptr(V), *common)
+    else:
+        st = rkv.lib().rkv_hsa_decode_summary(rkv._ptr(Q), rkv._ptr(K), rkv._ptr(V), rkv._ptr(summary), *common)
+    assert st == 0, rkv.status_string(st)
+
+
+class GrowingCache:
+    """A decode workload whose recent window grows by one token per step.
+    Every (sequence, layer, KV head) is its own item of one KV head (its 3
+    query heads; stage 2 has no cross-head coupling, so the results are those
+    of the full-head call) with room for the window's rows after the
+    compressed cache, so the window grows in place: step t decodes with
+    len_k = Lc + w and recent_window = w, w = t + 1."""
+
+    def __init__(self, device, seed, units, Lc, wmax, topk, C, r):
+        import torch
+        import rocketkv_b200 as rkv
+        self.units, self.Lc, self.wmax = units, Lc, wmax
+        self.cfg = rkv.RocketConfig(num_heads=H // HK, num_heads_kv=1, dim_head=D, topk_decode=topk, chunk_size=C,
+                                    r_dim=r, compression_ratio=4.0)
+        self.c = self.cfg.c()
+        g = torch.Generator(device=device).manual_seed(seed)
+        rows = Lc + wmax
+        self.K = torch.empty((units, 1, rows, D), dtype=torch.bfloat16, device=device)
+        self.V = torch.empty_like(self.K)
+        for i in range(0, units, 1024):
+            j = min(units, i + 1024)
+            k = torch.randn((j - i, 1, rows, D), generator=g, device=device)
+            out = torch.rand((j - i, 1, rows, 1), generator=g, device=device) < 0.01
+            out[:, :, Lc:] = False
+            self.K[i:j] = torch.where(out, k * 8, k)
+            self.V[i:j] = torch.randn((j - i, 1, rows, D), generator=g, device=device)
+        self.Qs = [torch.randn((units, H // HK, D), generator=g, device=device).to(torch.bfloat16) for _ in range(4)]
+        self.cap = rkv.hsa_sel_capacity(self.cfg, Lc + wmax, wmax)
+        self.ws_bytes = rkv.hsa_workspace_size(self.cfg, Lc + wmax, wmax, units, 1)
+        self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=device)
+        self.O = torch.zeros((units, H // HK, D), dtype=torch.float32, device=device)
+        self.sel = torch.zeros((units, 1, self.cap), dtype=torch.int32, device=device)
+        self.nsel = torch.zeros((units, 1), dtype=torch.int32, device=device)
+        self.S = None
+
+    def build_summary(self, stream):
+        import ctypes
+        import torch
+        import rocketkv_b200 as rkv
+        n = ctypes.c_size_t(0)
+        assert rkv.lib().rkv_hsa_summary_size(ctypes.byref(self.c), rkv.BF16, self.Lc, 0, self.units,
+                                              ctypes.byref(n)) == 0
+        if self.S is None:
+            self.S = torch.empty(n.value, dtype=torch.uint8, device=self.K.device)
+        assert rkv.lib().rkv_hsa_build_summary(rkv._ptr(self.K), rkv.BF16, self.Lc, 0, self.units, self.K[0].nbytes,
+                                               ctypes.byref(self.c), rkv._ptr(self.S), stream) == 0
+
+    def step(self, t, stream, summary=False):
+        w = t + 1
+        _decode_call(self.c, self.Qs[t % len(self.Qs)], self.K, self.V, self.S if summary else None, 1,
+                     self.Lc + w, w, self.units, self.O, self.sel, self.cap, self.nsel, self.ws, self.ws_bytes, stream)
+
+    def unit_bytes(self, w, summary=False):
+        k = min(self.cfg.topk_decode, self.Lc)
+        if summary:
+            return unit_bytes_summary(self.Lc + w, k, w, self.cfg.r_dim, self.cfg.chunk_size)
+        return unit_bytes(self.Lc + w, k, w)
+
+
+def time_growing(gc, steps, warmup, world, gpu_index):
+    """steps/s of `steps` decode steps with the window growing 1..steps,
+    stateless and through page summaries (build timed separately); each pass
+    over the horizon is one timed region.  Returns the stateless and summary
+    results with their rooflines."""
+    import torch
+    st = torch.cuda.current_stream()
+    peak, _ = peaks()
+    out = {}
+    for mode in ("stateless", "summary"):
+        summary = mode == "summary"
+        if summary:
+            b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            b0.record(st)
+            gc.build_summary(st.cuda_stream)
+            b1.record(st)
+            torch.cuda.synchronize()
+            build_ms = allreduce_max(b0.elapsed_time(b1), world)
+        for i in range(warmup):
+            gc.step(i % steps, st.cuda_stream, summary)
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(gpu_index) as cs:
+            e0.record(st)
+            for t in range(steps):
+                gc.step(t, st.cuda_stream, summary)
+            e1.record(st)
+            torch.cuda.synchronize()
+        ms = allreduce_max(e0.elapsed_time(e1), world)
+        barrier(world)
+        nbytes = sum(gc.unit_bytes(t + 1, summary) for t in range(steps)) * gc.units
+        ach = nbytes / (ms / 1e3) / 1e9
+        r = {"value": round(world * steps / (ms / 1e3), 3), "unit": "steps/s", "ms_per_step": round(ms / steps, 4),
+             "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                          "frac": round(ach / peak, 4), "algorithmic_bytes_per_horizon": nbytes},
+             "clocks": cs.summary()}
+        if summary:
+            r["build_ms"] = round(build_ms, 3)
+            amort = (ms + build_ms) / steps
+            r["amortised"] = {"value": round(world * 1e3 / amort, 3), "unit": "steps/s",
+                              "ms_per_step": round(amort, 4),
+                              "what": f"the summary build once per cache plus the {steps}-step horizon"}
+        out[mode] = r
+    return out
+
+
+def time_config1(device, reps, warmup):
+    """One decode step of one layer: q [24, 128], K/V [8, 2048, 128] bf16
+    N(0,1) with 1 % of K rows x8, page 16, r 32, top-k 256; without a recent
+    window (the reference's semantics) and with 32 recent tokens.  us per call
+    (three kernel launches), L2 flushed before each, and the whole-call
+    roofline against the algorithmic bytes."""
+    import torch
+    import rocketkv_b200 as rkv
+    L = 2048
+    cfg = rkv.RocketConfig(num_heads=H, num_heads_kv=HK, dim_head=D, topk_decode=256, chunk_size=16, r_dim=32,
+                           compression_ratio=4.0)
+    g = torch.Generator(device=device).manual_seed(21)
+    q = torch.randn((1, H, D), generator=g, device=device).to(torch.bfloat16)
+    Kf = torch.randn((1, HK, L, D), generator=g, device=device)
+    rows = torch.rand((1, HK, L, 1), generator=g, device=device) < 0.01
+    K = torch.where(rows, Kf * 8, Kf).to(torch.bfloat16)
+    V = torch.randn((1, HK, L, D), generator=g, device=device).to(torch.bfloat16)
+    flush, st = _flush_events(device)
+    peak, _ = peaks()
+    out = {}
+    for w, nbytes in ((0, 4737024), (32, 4868096)):
+        dec = rkv.HsaDecoder(cfg, L, 1, device, recent_window=w)
+        for _ in range(warmup):
+            dec(q, K, V)
+        ts = []
+        for _ in range(reps):
+            flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            dec(q, K, V)
+            e1.record(st)
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        assert dec.status() == 0
+        us = statistics.median(ts) * 1e3
+        out[f"w{w}"] = {"us_per_layer_step": round(us, 2), "algorithmic_bytes": nbytes,
+                        "gbs": round(nbytes / (us / 1e6) / 1e9, 1), "frac_of_hbm": round(nbytes / (us / 1e6) / 1e9 / peak, 4)}
+    out["workload"] = ("q [24,128], K/V [8,2048,128] bf16, 1% K rows x8, page 16, r 32, top-k 256, one layer, "
+                       "one step; median of %d calls, L2 flushed before each" % reps)
+    return out
+
+
+def long_context(device, world, rank, steps, warmup, gpu_index):
+    """The long-context configuration: 8 sequences at S = 131072, K/V/Q bf16
+    N(0,1) with 0.5 % of K rows x8, sharded by KV head over the ranks (one
+    head per GPU at 8 GPUs).  Stage 1 at budget 4096 (window 32, kernel 63):
+    each rank pools its heads, the pooled rows are all-gathered (NCCL) and
+    every rank selects the same kept set.  Then `steps` decode steps over 28
+    layers on the 4096-row caches (page 16, r 32, top-k 256, the window
+    growing by a token per step): each rank decodes its heads of all
+    8 x 28 (sequence, layer) items in one call, and one all-gather per step
+    assembles O.  Compute and all-gather times are reported separately (CUDA
+    events on the launching stream, max over ranks)."""
+    import torch
+    import rocketkv_b200 as rkv
+    import sharded
+    B, S, budget, layers = 8, 131072, 4096, 28
+    G = H // HK
+    h0, nh = sharded.head_range(HK, world, rank)
+    st = torch.cuda.current_stream()
+    peak, _ = peaks()
+    g = torch.Generator(device=device).manual_seed(77 + 1000 * h0)
+    K = torch.empty((B, nh, S, D), dtype=torch.bfloat16, device=device)
+    for b in range(B):
+        k = torch.randn((nh, S, D), generator=g, device=device)
+        out = torch.rand((nh, S, 1), generator=g, device=device) < 0.005
+        K[b] = torch.where(out, k * 8, k)
+    Qw = torch.randn((B, nh * G, 32, D), generator=g, device=device).to(torch.bfloat16)
+    cfg = rkv.RocketConfig(num_heads=H, num_heads_kv=HK, dim_head=D, prompt_budget=budget)
+    lcfg = rkv.RocketConfig(num_heads=nh * G, num_heads_kv=nh, dim_head=D, prompt_budget=budget)
+    local_ev = rkv.Evictor(lcfg, 32, S, B, rkv.BF16, device)
+    full_ev = rkv.Evictor(cfg, 32, S, B, rkv.BF16, device)
+    nk = S - 32
+    pooled_local = torch.empty((B, nh, nk), dtype=torch.float32, device=device)
+    counts = [sharded.head_range(HK, world, r)[1] for r in range(world)]
+
+    def evict_once(ev_t):
+        ev_t[0].record(st)
+        local_ev.pool_heads(Qw, K, 0, nh, pooled_local)
+        ev_t[1].record(st)
+        pooled = sharded.gather_rows(pooled_local, counts) if world > 1 else pooled_local
+        ev_t[2].record(st)
+        kept, n = full_ev.select_pooled(pooled)
+        ev_t[3].record(st)
+        return kept, n
+
+    for _ in range(warmup):
+        evict_once([torch.cuda.Event(enable_timing=True) for _ in range(4)])
+    barrier(world)
+    reps = 3
+    acc = [0.0, 0.0, 0.0]
+    for _ in range(reps):
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        kept, n = evict_once(evs)
+        torch.cuda.synchronize()
+        for j in range(3):
+            acc[j] += evs[j].elapsed_time(evs[j + 1]) / reps
+    assert rkv.lib().rkv_workspace_status(rkv._ptr(local_ev.ws), 0) == 0
+    pool_ms, gather_ms, select_ms = (allreduce_max(x, world) for x in acc)
+    ev_bytes = nh * (S - 32) * D * 2 + nh * G * 32 * D * 2  # this rank's K rows and window queries, per sequence
+    ev_ms_seq = (pool_ms + gather_ms + select_ms) / B
+    eviction = {"ms_per_sequence_layer": round(ev_ms_seq, 4), "pool_ms_per_call": round(pool_ms, 4),
+                "allgather_ms_per_call": round(gather_ms, 4), "select_ms_per_call": round(select_ms, 4),
+                "sequences_per_call": B, "pooled_bytes_gathered_per_call": B * HK * nk * 4,
+                "pool_gbs_per_gpu": round(B * ev_bytes / (pool_ms / 1e3) / 1e9, 1),
+                "pool_frac_of_hbm": round(B * ev_bytes / (pool_ms / 1e3) / 1e9 / peak, 4)}
+    del K, local_ev, full_ev, pooled_local
+    torch.cuda.empty_cache()
+    # decode: this rank's KV heads of every (sequence, layer), one item per head
+    units = B * layers * nh
+    gc = GrowingCache(device, 900 + rank, units, budget, steps, 256, 16, 32)
+    O_all = torch.empty((B * layers, H, D), dtype=torch.float32, device=device)
+    for i in range(warmup):
+        gc.step(i % steps, st.cuda_stream)
+    barrier(world)
+    dec_ms = ag_ms = 0.0
+    with ClockSampler(gpu_index) as cs:
+        for t in range(steps):
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            e[0].record(st)
+            gc.step(t, st.cuda_stream)
+            e[1].record(st)
+            if world > 1:
+                local = gc.O.view(B * layers, nh * G, D)
+                O_all.copy_(sharded.gather_rows(local, [c * G for c in counts]))
+            else:
+                O_all.copy_(gc.O.view(B * layers, H, D))
+            e[2].record(st)
+            torch.cuda.synchronize()
+            dec_ms += e[0].elapsed_time(e[1])
+            ag_ms += e[1].elapsed_time(e[2])
+    assert rkv.lib().rkv_workspace_status(rkv._ptr(gc.ws), 0) == 0
+    dec_ms, ag_ms = allreduce_max(dec_ms, world), allreduce_max(ag_ms, world)
+    nbytes = sum(gc.unit_bytes(t + 1) for t in range(steps)) * units
+    ach = nbytes / (dec_ms / 1e3) / 1e9
+    decode = {"steps_per_s": round(steps / ((dec_ms + ag_ms) / 1e3), 3),
+              "compute_ms_per_step": round(dec_ms / steps, 4), "allgather_ms_per_step": round(ag_ms / steps, 4),
+              "O_bytes_gathered_per_step": B * layers * H * D * 4,
+              "roofline_compute": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                                   "frac": round(ach / peak, 4)},
+              "clocks": cs.summary()}
+    del gc
+    torch.cuda.empty_cache()
+    return {"workload": "8 sequences x S 131072 bf16 (0.5% K rows x8), KV heads sharded over the ranks "
+                        f"({nh} per rank); stage 1 budget 4096 w32 ks63; {steps} decode steps x 28 layers on the "
+                        "4096-row caches (page 16, r 32, top-k 256, window growing by one token per step)",
+            "heads_per_rank": nh, "eviction": eviction, "decode": decode}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -583,6 +865,45 @@ def main():
                             "instead of every K row",
                     "break_even_steps": round(build_ms / max(ms_sl / args.steps - step_ms, 1e-9), 2)}
 
+    # the amortised headline: the summary build once per cache over a 32-step decode horizon
+    horizon = 32
+    amort_ms = step_ms + build_ms / horizon
+    summary_info["amortised"] = {"value": round(world * 1e3 / amort_ms, 3), "unit": "steps/s",
+                                 "ms_per_step": round(amort_ms, 4), "horizon_steps": horizon,
+                                 "what": "value with the page-summary build charged once per cache over a "
+                                         f"{horizon}-step decode horizon"}
+
+    e2e = e2e_res = None
+    if not args.no_e2e:
+        n_e2e = max(1, min(args.steps, 3))
+        tot, cnt, h2d, d2h = e2e_decode(cfg, cache, Qs, K, V, n_e2e)
+        tot = allreduce_max(tot, world)
+        e2e = {"value": world * cnt / tot, "unit": "steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "path": "rkv_hsa_decode_host_ex: pinned host Q and K copied in, the selected V rows read in place "
+                       "from pinned host memory, O copied back; steps=%d" % cnt}
+        tot_r, cnt_r, h2d_r, d2h_r = e2e_resident_decode(dec, S, Qs, K, V, 10)
+        tot_r = allreduce_max(tot_r, world)
+        e2e_res = {"value": round(world * cnt_r / tot_r, 3), "unit": "steps/s", "h2d_bytes_per_step": h2d_r,
+                   "d2h_bytes_per_step": d2h_r,
+                   "path": "cache resident on the device with its page summaries: per step the query and the new "
+                           "token's K and V rows from pinned host memory, rkv_hsa_decode_summary, O back to pinned "
+                           "host memory (wall clock); steps=%d" % cnt_r}
+    del Qs, K, V, S, dec
+    torch.cuda.empty_cache()
+
+    # the batched-decode configuration as stated: 64 sequences x 28 layers, a 2048-token cache per
+    # (sequence, layer) plus a recent window growing from 1 to 32 tokens over 32 steps
+    gc = GrowingCache(device, 555 + rank, SEQS * LAYERS * HK, 2048, 32, 256, 16, 32)
+    grow = time_growing(gc, 32, args.warmup, world, gpu_index)
+    assert rkv.lib().rkv_workspace_status(rkv._ptr(gc.ws), 0) == 0, "in-kernel wait timed out"
+    del gc
+    torch.cuda.empty_cache()
+    grow["workload"] = (f"{SEQS} sequences x {LAYERS} layers per GPU, 2048-token bf16 caches (1% K rows x8) plus a "
+                        "recent window growing 1..32 over 32 steps; page 16, r 32, top-k 256; every (sequence, "
+                        "layer, KV head) an item with room for the window")
+    cfg1 = time_config1(device, 50, args.warmup)
+    longctx = long_context(device, world, rank, 64, args.warmup, gpu_index)
+
     ev_ms, ev_e2e_ms, ev_kernels = time_evict(device, max(args.steps, 5), args.warmup)
     ev_ms = allreduce_max(ev_ms, world)
     ev_ach = EVICT_BYTES / (ev_ms / 1e3) / 1e9
@@ -602,22 +923,7 @@ def main():
     comp["frac_of_hbm_out_of_place"] = round(comp["gbs_out_of_place"] / peak, 4)
     eviction["kv_compaction"] = comp
 
-    e2e = e2e_res = None
-    if not args.no_e2e:
-        n_e2e = max(1, min(args.steps, 3))
-        tot, cnt, h2d, d2h = e2e_decode(cfg, cache, Qs, K, V, n_e2e)
-        tot = allreduce_max(tot, world)
-        e2e = {"value": world * cnt / tot, "unit": "steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "path": "rkv_hsa_decode_host_ex: pinned host Q and K copied in, the selected V rows read in place "
-                       "from pinned host memory, O copied back; steps=%d" % cnt}
-        eviction["cpu_baseline_ms"] = None
-        tot_r, cnt_r, h2d_r, d2h_r = e2e_resident_decode(dec, S, Qs, K, V, 10)
-        tot_r = allreduce_max(tot_r, world)
-        e2e_res = {"value": round(world * cnt_r / tot_r, 3), "unit": "steps/s", "h2d_bytes_per_step": h2d_r,
-                   "d2h_bytes_per_step": d2h_r,
-                   "path": "cache resident on the device with its page summaries: per step the query and the new "
-                           "token's K and V rows from pinned host memory, rkv_hsa_decode_summary, O back to pinned "
-                           "host memory (wall clock); steps=%d" % cnt_r}
+    eviction["cpu_baseline_ms"] = None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu and ref_lib_available():
@@ -639,7 +945,8 @@ def main():
             "config": workload_config(cache), "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": 3 * args.steps, "clocks": clocks, "decode_path": "persistent page summaries",
             "page_summaries": summary_info, "stateless_decode": stateless, "eviction": eviction,
-            "e2e_resident_cache": e2e_res,
+            "e2e_resident_cache": e2e_res, "config1_single_step": cfg1, "config3_window_growth": grow,
+            "long_context": longctx,
         }
         print(json.dumps(line))
     if world > 1:

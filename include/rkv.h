@@ -235,13 +235,24 @@ int rkv_hsa_decode_summary(const void* Q, const void* K, const void* V, const vo
  * rkv_hsa_workspace_size exceeds 4 MiB returns RKV_ERR_WORKSPACE and launches
  * nothing.  No call allocates.  The first call on each device looks up that
  * device's copy of the array (cudaGetSymbolAddress); make it before any
- * stream capture.  All calls share the one array, so calls that overlap on
- * the GPU (other streams, other host threads) race: serialise them. */
+ * stream capture.  The address is remembered with the id of the CUDA context
+ * it belongs to, so the first call after the device's context is reset
+ * (cudaDeviceReset) looks it up again and is likewise a set-up call.  All
+ * calls share the one array, so calls that overlap on the GPU (other streams,
+ * other host threads) race: serialise them. */
 int rkv_hsa_decode_noalloc(const void* Q, const void* K, const void* V, int dtype, int len_k,
                            int recent_window, int batch, long long q_item_stride,
                            long long kv_item_stride, const rkv_config* cfg, int head_begin,
                            int head_count, float* O, int* sel, int sel_stride, int* n_sel,
                            void* stream);
+
+/* Status of rkv_hsa_decode_noalloc calls (no counterpart in the reference):
+ * the no-allocation entry point has no workspace for rkv_workspace_status to
+ * read, so this synchronises `stream`, reads the error word of the current
+ * device's fixed scratch (RKV_ERR_DEVICE_TIMEOUT when a bounded in-kernel
+ * wait of a call on that device ran out, with O and sel then incomplete),
+ * clears it and returns it (RKV_OK otherwise).  Allocates nothing. */
+int rkv_hsa_decode_noalloc_status(void* stream);
 
 /* ---- KV-cache compaction ---------------------------------------------------
  * Applies stage 1's kept indices to the KV cache on the device: for every
@@ -257,9 +268,12 @@ int rkv_hsa_decode_noalloc(const void* Q, const void* K, const void* V, int dtyp
  * [batch][num_heads_kv][out_len] rows at out_item_stride bytes per item,
  * rows from n_kept on left as they are.  In place when K_out == K (and
  * V_out == V): then out_len must equal len_k and the strides must match, and
- * the kept lists must be ascending; K and V must not overlap.  Out of place
- * the output must not overlap the input.  Asynchronous on `stream`;
- * allocates nothing. */
+ * the kept lists must be strictly ascending (as rkv_evict writes them); K and
+ * V must not overlap.  The order is not checked: in place, a list that is not
+ * strictly ascending gives undefined rows (a row may be read after it was
+ * overwritten), though every access stays inside the cache.  Out of place the
+ * output must not overlap the input and any order works.  Asynchronous on
+ * `stream`; allocates nothing. */
 int rkv_compact_kv(const void* K, const void* V, int dtype, int head_dim, int num_heads_kv,
                    int len_k, int batch, long long kv_item_stride, const int* kept,
                    const int* n_kept, int kept_stride, void* K_out, void* V_out, int out_len,

@@ -35,7 +35,7 @@ EXPORTS = [
     "rkv_evict_max_kept", "rkv_evict_workspace_size", "rkv_evict", "rkv_evict_pool_heads",
     "rkv_evict_select_pooled", "rkv_prefill_eviction_host", "rkv_hsa_sel_capacity",
     "rkv_hsa_workspace_size", "rkv_hsa_decode", "rkv_hybrid_sparse_decode_host",
-    "rkv_hsa_decode_host_ex", "rkv_workspace_status", "rkv_hsa_decode_noalloc",
+    "rkv_hsa_decode_host_ex", "rkv_workspace_status", "rkv_hsa_decode_noalloc", "rkv_hsa_decode_noalloc_status",
     "rkv_selftest_wait_timeout", "rkv_compact_kv", "rkv_hsa_summary_size", "rkv_hsa_build_summary",
     "rkv_hsa_decode_summary",
 ]
@@ -132,6 +132,7 @@ def lib() -> ctypes.CDLL:
         "rkv_selftest_wait_timeout": ([_VP, _VP], _I),
         "rkv_hsa_decode_noalloc": ([_VP, _VP, _VP, _I, _I, _I, _I, _LL, _LL, _CFGP, _I, _I, _VP, _VP, _I, _VP,
                                     _VP], _I),
+        "rkv_hsa_decode_noalloc_status": ([_VP], _I),
         "rkv_compact_kv": ([_VP, _VP, _I, _I, _I, _I, _I, _LL, _VP, _VP, _I, _VP, _VP, _I, _LL, _VP], _I),
         "rkv_hsa_summary_size": ([_CFGP, _I, _I, _I, _I, ctypes.POINTER(_SZ)], _I),
         "rkv_hsa_build_summary": ([_VP, _I, _I, _I, _I, _LL, _CFGP, _VP, _VP], _I),

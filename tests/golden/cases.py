@@ -19,6 +19,8 @@ STAGE1 = [
     ("s1_q8", dict(H=24, HK=8, D=128, len_q=1024, len_k=1024, window=32, ks=63, budget=256, seed=15, kind="q8_0")),
     ("s1_bf16", dict(H=24, HK=8, D=128, len_q=1000, len_k=1000, window=32, ks=63, budget=300, seed=16, kind="bf16")),
     ("s1_evenks", dict(H=12, HK=4, D=96, len_q=777, len_k=777, window=16, ks=10, budget=200, seed=17, kind="normal")),
+    # the single-layer fp32 configuration: K [8, 8192, 128], window queries Q [24, 32, 128], budget 1024
+    ("s1_config0", dict(H=24, HK=8, D=128, len_q=32, len_k=8192, window=32, ks=63, budget=1024, seed=42, kind="normal")),
 ]
 
 # ---- stage 2 ------------------------------------------------------------------

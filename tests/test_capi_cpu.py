@@ -69,3 +69,31 @@ def test_sizes_and_argument_errors():
     assert rkv.hsa_sel_capacity(c2, 3717, 32) == 544
     assert rkv.hsa_sel_capacity(c2, 100, 32) == 100
     assert rkv.hsa_workspace_size(c2, 3717, 32, 4, 8) > 4 * 8 * 3 * 1843 * 4
+
+
+CHECK = os.path.join(ROOT, "tests", "_bin", "rocket_h_check")
+
+
+def _check(mode, d):
+    import subprocess
+    assert os.path.exists(CHECK), f"{CHECK} missing: make -C tests"
+    r = subprocess.run([CHECK, mode, str(d)], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, r.stderr
+    return r.stdout
+
+
+def test_rocket_h_cpp_params_golden_grid(tmp_path):
+    """rocket.h's compute_rocket_params called from C++ (tests/rocket_h_check.cpp)
+    on part of the golden grid of the reference's outputs."""
+    for g, want in list(zip(GOLD["params/in"], GOLD["params/out"]))[::37]:
+        (tmp_path / "args.txt").write_text(" ".join(str(int(x)) for x in g) + "\n")
+        _check("params", tmp_path)
+        f = (tmp_path / "params.txt").read_text().split()
+        got = [int(x) for x in f[:8]] + [int(np.float32(float(f[8])).view(np.int32))]
+        assert got == [int(x) for x in want], g
+
+
+def test_rocket_h_cpp_invalid_config_throws(tmp_path):
+    """A config the reference cannot size raises std::invalid_argument through
+    rocket.h (its return type carries no status); no device is touched."""
+    assert _check("bad", tmp_path).strip() == "invalid_argument"

@@ -193,3 +193,88 @@ def test_stage1_invalid_sizes(cuda):
     with pytest.raises(rkv.RkvError) as e:  # len_k < window rows: rocket.cpp cannot size its buffer
         rkv.compute_prefill_eviction(np.zeros((6, 64, 64), np.float32), np.zeros((2, 10, 64), np.float32), 64, 10, cfg)
     assert e.value.status == rkv.RKV_ERR_INVALID_ARG
+
+
+def test_stage1_config2_full_size_q8(cuda):
+    """The 28-layer q8_0 configuration at full size: K [28][8, 8192, 128] and
+    window queries Q [28][24, 32, 128] stored q8_0 (int8 uniform in
+    [-127, 127], fp16 scales |N(0, 0.02)|), all layers in one call, budgets
+    512, 1024 and 2048.  Every layer's kept set equals the oracle's (pooled
+    rows per layer from the oracle's scoring, its own selection per budget)."""
+    import torch
+    layers, S = 28, 8192
+    base = O.Config(num_heads=24, num_heads_kv=8, dim_head=128)
+
+    def oracle_layer(l):
+        qp, Qf = rkvgen.q8_0_inputs(3000 + 2 * l, (24, 32), 128)
+        kp, Kf = rkvgen.q8_0_inputs(3001 + 2 * l, (8, S), 128)
+        return qp, kp, O.evict_pool_heads(Qf, Kf, 32, S, base, 0, 8)
+
+    with ThreadPoolExecutor(8) as ex:
+        per_layer = list(ex.map(oracle_layer, range(layers)))
+    Qt = torch.stack([torch.from_numpy(q) for q, _, _ in per_layer]).to(cuda)
+    Kt = torch.stack([torch.from_numpy(k) for _, k, _ in per_layer]).to(cuda)
+    for budget in (512, 1024, 2048):
+        cfg = O.Config(num_heads=24, num_heads_kv=8, dim_head=128, prompt_budget=budget)
+        ev = rkv.Evictor(to_rkv(cfg), 32, S, layers, rkv.Q8_0, cuda)
+        kept, n = ev(Qt, Kt)
+        kept, n = kept.cpu().numpy(), n.cpu().numpy()
+        assert rkv.lib().rkv_workspace_status(rkv._ptr(ev.ws), 0) == 0
+        for l, (_, _, pooled) in enumerate(per_layer):
+            want = O.evict_select_pooled(pooled, 32, S, cfg)
+            got = kept[l, : n[l]]
+            assert len(want) == budget
+            assert np.array_equal(got, want), (budget, l, boundary_report(pooled.sum(0), got, want))
+
+
+def test_long_context_pipeline(cuda):
+    """The long-context configuration on one GPU, end to end for two sequences:
+    S = 131072 bf16 K/V/Q (N(0,1), 0.5 % of K rows x8), stage 1 at budget 4096
+    (window 32, kernel 63), the KV cache compacted to the kept rows, then one
+    stage-2 decode step over the 4096-row cache (page 16, r 32, top-k 256, the
+    last 32 rows as the recent window).  Kept indices equal the oracle's per
+    sequence (oracle pooling per KV head in host threads); the decode's
+    selections equal the oracle's on the compacted cache and O is within
+    1e-3 / 1e-4."""
+    import torch
+    B, S, H, HK, D, budget = 2, 131072, 24, 8, 128, 4096
+    g = torch.Generator(device=cuda).manual_seed(4444)
+    K = torch.randn((B, HK, S, D), generator=g, device=cuda)
+    rows = torch.rand((B, HK, S, 1), generator=g, device=cuda) < 0.005
+    K = torch.where(rows, K * 8, K).to(torch.bfloat16).contiguous()
+    V = torch.randn((B, HK, S, D), generator=g, device=cuda).to(torch.bfloat16)
+    Qw = torch.randn((B, H, 32, D), generator=g, device=cuda).to(torch.bfloat16)  # the window rows
+    q = torch.randn((B, H, D), generator=g, device=cuda).to(torch.bfloat16)        # the decode query
+    cfg = O.Config(num_heads=H, num_heads_kv=HK, dim_head=D, prompt_budget=budget)
+    ev = rkv.Evictor(to_rkv(cfg), 32, S, B, rkv.BF16, cuda)
+    kept, n = ev(Qw, K)
+    torch.cuda.synchronize()
+    assert rkv.lib().rkv_workspace_status(rkv._ptr(ev.ws), 0) == 0
+    kept_h, n_h = kept.cpu().numpy(), n.cpu().numpy()
+    assert np.all(n_h == budget)
+    for b in range(B):
+        Qf, Kf = Qw[b].float().cpu().numpy(), K[b].float().cpu().numpy()
+        with ThreadPoolExecutor(8) as ex:
+            pooled = np.concatenate(list(ex.map(lambda h: O.evict_pool_heads(Qf, Kf, 32, S, cfg, h, 1), range(HK))))
+        want = O.evict_select_pooled(pooled, 32, S, cfg)
+        got = kept_h[b, : n_h[b]]
+        assert np.array_equal(got, want), (b, boundary_report(pooled.sum(0), got, want))
+    del Kf
+    # the cache left by eviction: the kept rows of every KV head, in order
+    Kc = torch.empty((B, HK, budget, D), dtype=torch.bfloat16, device=cuda)
+    Vc = torch.empty_like(Kc)
+    rkv.compact_kv(K, V, kept, n, D, K_out=Kc, V_out=Vc)
+    cfg2 = O.Config(num_heads=H, num_heads_kv=HK, dim_head=D, topk_decode=256, chunk_size=16, r_dim=32,
+                    compression_ratio=4.0)
+    dec = rkv.HsaDecoder(to_rkv(cfg2), budget, B, cuda, recent_window=32)
+    dec(q, Kc, Vc)
+    torch.cuda.synchronize()
+    assert dec.status() == 0
+    for b in range(B):
+        idx = kept_h[b, :budget]
+        Kb, Vb = K[b].float().cpu().numpy()[:, idx], V[b].float().cpu().numpy()[:, idx]
+        assert np.array_equal(Kc[b].float().cpu().numpy(), Kb)
+        Oo, so = O.hsa_decode(q[b].float().cpu().numpy(), Kb, Vb, budget, cfg2, recent_window=32)
+        for h in range(HK):
+            assert np.array_equal(dec.sel[b, h, : int(dec.n_sel[b, h])].cpu().numpy(), so[h]), (b, h)
+        np.testing.assert_allclose(dec.O[b].cpu().numpy(), Oo, rtol=1e-3, atol=1e-4)
