@@ -1493,6 +1493,11 @@ int launch_t(HsaArgs a, int batch, cudaStream_t st) {
         a.nstage = ns;
         a.ngrp = a.carry_mode ? 1 : (kScanConsumers / 32) / a.wg;
         if (a.ngrp > ns - 1) a.ngrp = ns - 1;
+        // Group g takes stages g, g + ngrp, ... in ring slot s % ns.  With ngrp dividing ns every
+        // slot belongs to one group, which uses it in order; otherwise a group could wait on a slot
+        // two phases ahead of its last completed phase, which a parity wait cannot tell from the
+        // previous phase (it would pass before the copy lands).
+        while (ns % a.ngrp != 0) --a.ngrp;
         // enough scan CTAs to cover the GPU; every split keeps at least 4 stages of pages
         const long long units = (long long)batch * a.head_count;
         const long long want = 2LL * num_sms();

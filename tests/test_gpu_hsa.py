@@ -219,3 +219,26 @@ def test_stage2_headline_items_vs_reference(cuda):
         np.testing.assert_allclose(Og[b], Oref, rtol=RTOL, atol=ATOL)
         gaps += [stage2_boundary_gap(qs[b], Ks[b], cfg, L, 0, h) for h in range(8)]
     print(f"smallest float64 boundary gap over {len(gaps)} units: {min(gaps):.3e}")
+
+
+@pytest.mark.parametrize("C", [3, 4, 5, 8, 16])
+def test_stage2_scan_ring_refill(C, cuda):
+    """Enough units for one scan CTA per unit and a cache long enough that the
+    K-row ring is refilled many times, at page sizes whose scan groups (one or
+    two warps per stage) take stages in turn: every unit's selection equals
+    the oracle's and O is within tolerance."""
+    import torch
+    B, L, w = 40, 1024, 8
+    cfg = O.Config(num_heads=24, num_heads_kv=8, dim_head=128, topk_decode=160, chunk_size=C, r_dim=37)
+    g = torch.Generator(device=cuda).manual_seed(300 + C)
+    Q = torch.randn((B, 24, 128), generator=g, device=cuda).to(torch.bfloat16)
+    K = torch.randn((B, 8, L, 128), generator=g, device=cuda).to(torch.bfloat16)
+    V = torch.randn((B, 8, L, 128), generator=g, device=cuda).to(torch.bfloat16)
+    d = rkv.HsaDecoder(to_rkv(cfg), L, B, cuda, recent_window=w)
+    d(Q, K, V)
+    torch.cuda.synchronize()
+    assert d.status() == 0
+    sel, nsel, Og = d.sel.cpu().numpy(), d.n_sel.cpu().numpy(), d.O.cpu().numpy()
+    Qh, Kh, Vh = Q.float().cpu().numpy(), K.float().cpu().numpy(), V.float().cpu().numpy()
+    for b in range(B):
+        check_against_oracle(Qh[b], Kh[b], Vh[b], L, cfg, Og[b], sel[b], nsel[b], w=w)
