@@ -673,7 +673,7 @@ def time_config1(device, reps, warmup):
         out[f"w{w}"] = {"us_per_layer_step": round(us, 2), "algorithmic_bytes": nbytes,
                         "gbs": round(nbytes / (us / 1e6) / 1e9, 1), "frac_of_hbm": round(nbytes / (us / 1e6) / 1e9 / peak, 4)}
     out["workload"] = ("q [24,128], K/V [8,2048,128] bf16, 1% K rows x8, page 16, r 32, top-k 256, one layer, "
-                       "one step; median of %d calls, L2 flushed before each" % reps)
+                       f"one step; median of {reps} calls, L2 flushed before each")
     return out
 
 

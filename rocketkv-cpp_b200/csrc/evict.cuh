@@ -65,6 +65,10 @@ int launch_evict_fold(const EvictArgs& a, int batch, cudaStream_t st);
 // persistent warp-specialised tcgen05 scoring (evict_tc.cu): fp32, bf16, q8_0 (D = 128), G * obs_w <= 128
 bool evict_tc_supported(const EvictArgs& a, int batch);
 int launch_evict_tc(const EvictArgs& a, int batch, cudaStream_t st);
+// q8_0 K and Q on kind::i8 tensor-core products (evict_q8.cu): D = 128, G * obs_w <= 128, 16-byte
+// aligned K tiles; launch_evict_tc takes it for q8_0 wherever it applies
+bool evict_q8_supported(const EvictArgs& a, int batch);
+int launch_evict_q8(const EvictArgs& a, int batch, cudaStream_t st);
 int launch_evict_pool(const PoolArgs& a, int batch, cudaStream_t st);
 int launch_evict_select(const SelectArgs& a, int batch, cudaStream_t st);
 int launch_evict_keep_all(int* kept, int kept_stride, int* n_kept, int len_k, int batch, cudaStream_t st);

@@ -817,7 +817,7 @@ int launch_evict_tc(const EvictArgs& a, int batch, cudaStream_t st) {
     switch (kind_of(a.dtype)) {
         case KIND_F32: return launch_kind<KIND_F32>(a, batch, st);
         case KIND_BF16: return launch_kind<KIND_BF16>(a, batch, st);
-        default: return launch_kind<KIND_Q8>(a, batch, st);
+        default: return evict_q8_supported(a, batch) ? launch_evict_q8(a, batch, st) : launch_kind<KIND_Q8>(a, batch, st);
     }
 }
 
