@@ -440,7 +440,7 @@ __global__ void __launch_bounds__(kQ8Threads, 1) evict_q8_kernel(const EvictArgs
         float4* rtab = reinterpret_cast<float4*>(sm + P.off_rtab);   // [64]
         float* red = reinterpret_cast<float*>(sm + P.off_red);       // [2][128]
         bool ok = true;
-        int hv = -1, prev = -1;
+        int hv = -1, prev = -1, rt_head = -1;
         const bool one_launch = P.p0 == 0 && P.p1 == 1;
 
         auto fold_row = [&](size_t xr, float& M, float& inv) {  // one warp, row xr of [item][head][R]
@@ -484,7 +484,12 @@ __global__ void __launch_bounds__(kQ8Threads, 1) evict_q8_kernel(const EvictArgs
                 prev = head;
                 const bool w = mbar_wait_or_abort(&B.q_full[hv & 1], (uint32_t)((hv >> 1) & 1), a.err, abort_flag);
                 if (!group_all(kBarEpiQ8, kQ8Epi, w)) return false;
-                if (pass == 1) {  // this head's row statistics (-M_r, inv_r), as row pairs
+            }
+            // pass 1 needs the head's row statistics (-M_r, inv_r), as row pairs; its first tile continues
+            // pass 0's last head, so the table is keyed on the pass as well as the head
+            if (pass == 1 && head != rt_head) {
+                rt_head = head;
+                {
                     if (one_launch) {
                         for (int p = et; p < NP / 2; p += kQ8Epi) {
                             const int r = 2 * p;
