@@ -975,72 +975,116 @@ __global__ void hsa_summary_mask_clear(uint8_t* summary, long long sum_stride, l
     for (int x = threadIdx.x; x < words; x += blockDim.x) m[x] = 0u;
 }
 
+// The extrema of one page (rows p C .. min(p C + C, Lc) - 1) over two 16-byte
+// chunks of the row: NaN-ignoring max of x and of -x, word by word, the first
+// row first -- the scan's operations in its sign-flipped domain.
+template <typename T, int RB>
+__device__ __forceinline__ void page_extrema(const uint8_t* Kh, int p, int C, int Lc, int ch, uint4 (&m)[2],
+                                             uint4 (&n)[2]) {
+    constexpr uint32_t FLIP = sizeof(T) == 2 ? 0x80008000u : 0x80000000u;
+    const uint4 fl = make_uint4(FLIP, FLIP, FLIP, FLIP);
+    const int r0 = p * C, r1 = min(r0 + C, Lc);
+    const uint4* row = reinterpret_cast<const uint4*>(Kh + (size_t)r0 * RB) + ch;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        m[u] = __ldg(row + u);
+        n[u] = make_uint4(m[u].x ^ fl.x, m[u].y ^ fl.y, m[u].z ^ fl.z, m[u].w ^ fl.w);
+    }
+    for (int r = r0 + 1; r < r1; ++r) {
+        row += RB / 16;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const uint4 v = __ldg(row + u);
+            m[u] = max4<T>(m[u], v);
+            n[u] = max4<T>(n[u], make_uint4(v.x ^ fl.x, v.y ^ fl.y, v.z ^ fl.z, v.w ^ fl.w));
+        }
+    }
+}
+
+// Non-finite flags (-inf or NaN: the scan clamps such a representative at -FLT_MAX) of the dimensions of
+// one 32-bit word of the extrema, as bits at the dimensions' positions modulo 32.
+template <typename T>
+__device__ __forceinline__ uint32_t nonfinite_bits(uint32_t m, uint32_t n, int d0) {
+    uint32_t bits = 0u;
+    if (sizeof(T) == 2) {
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+            const uint32_t x = (m >> (16 * hf)) & 0xffffu, y = (n >> (16 * hf)) & 0xffffu;
+            if ((x & 0x7fffu) > 0x7f80u || x == 0xff80u || (y & 0x7fffu) > 0x7f80u || y == 0xff80u)
+                bits |= 1u << ((d0 + hf) & 31);
+        }
+    } else if ((m & 0x7fffffffu) > 0x7f800000u || m == 0xff800000u || (n & 0x7fffffffu) > 0x7f800000u ||
+               n == 0xff800000u) {
+        bits = 1u << (d0 & 31);
+    }
+    return bits;
+}
+
+// One warp per 64 pages of an (item, KV head): lane l takes pages 2l and
+// 2l + 1 of the warp's group and reads their rows 32 bytes at a time (whole
+// sectors), and per dimension stores the two pages' extrema as one 4-byte
+// (bf16) or 8-byte (fp32) word, so a warp writes 128 or 256 contiguous bytes
+// of a dimension's row per store.  No shared-memory transpose.  Pages from
+// nchunks to npp (the row padding) are written as zeros.
+constexpr int kBuildPagesPerWarp = 64;
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kSumBuildNT) hsa_summary_build_kernel(const uint8_t* K, long long kv_stride,
                                                                          int len_k, int C, int Lc, int nchunks,
-                                                                         int npp, int TP, uint8_t* summary,
+                                                                         int npp, uint8_t* summary,
                                                                          long long sum_stride, long long mask_off) {
-    constexpr int ES = (int)sizeof(T), RB = D * ES, W = RB / 4;  // 32-bit words per row
-    constexpr uint32_t FLIP = ES == 2 ? 0x80008000u : 0x80000000u;
-    extern __shared__ __align__(16) uint8_t smraw[];
-    __shared__ uint32_t nfm[D / 32];        // dimensions with an extremum of -inf or NaN on this tile
-    T* tile = reinterpret_cast<T*>(smraw);  // [2][D][TP]
-    const int pt = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
-    if (threadIdx.x < D / 32) nfm[threadIdx.x] = 0u;
-    __syncthreads();
-    const int p0 = pt * TP;
+    constexpr int ES = (int)sizeof(T), RB = D * ES, NCH = RB / 16;  // 16-byte chunks per row
+    constexpr int WPC = 4;                                          // 32-bit words per chunk
+    constexpr int DPW = 4 / ES;                                     // dimensions per word
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int hk = blockIdx.y, b = blockIdx.z;
+    const int g0 = (blockIdx.x * (kSumBuildNT / 32) + warp) * kBuildPagesPerWarp;
+    if (g0 >= npp) return;  // warp-uniform
+    const int pa = g0 + 2 * lane, pb = pa + 1;  // npp is a multiple of 8: pa < npp implies pb < npp
     const uint8_t* Kh = K + (size_t)b * kv_stride + (size_t)hk * len_k * RB;
-    for (int x = threadIdx.x; x < TP * W; x += kSumBuildNT) {
-        const int p = x / W, wd = x % W, page = p0 + p;
-        uint32_t m = 0u, n = 0u;
-        if (page < nchunks) {
-            const int r0 = page * C, r1 = min(r0 + C, Lc);
-            const uint32_t v0 = *reinterpret_cast<const uint32_t*>(Kh + (size_t)r0 * RB + 4 * wd);
-            m = v0;
-            n = v0 ^ FLIP;
-            for (int r = r0 + 1; r < r1; ++r) {
-                const uint32_t v = *reinterpret_cast<const uint32_t*>(Kh + (size_t)r * RB + 4 * wd);
-                m = Chunk<T>::wmax(m, v);
-                n = Chunk<T>::wmax(n, v ^ FLIP);
-            }
-        }
-        if (page < nchunks) {  // -inf or NaN: the scan clamps such a representative at -FLT_MAX
-            uint32_t bits = 0u;
-            if (ES == 2) {
+    T* Sm = reinterpret_cast<T*>(summary + (size_t)b * sum_stride + (size_t)hk * 2 * D * npp * ES);  // [2][D][npp]
+    const bool va = pa < nchunks, vb = pb < nchunks, wr = pa < npp;
+    uint32_t nf[D / 32];
 #pragma unroll
-                for (int hf = 0; hf < 2; ++hf) {
-                    const uint32_t x = (m >> (16 * hf)) & 0xffffu, y = (n >> (16 * hf)) & 0xffffu;
-                    if ((x & 0x7fffu) > 0x7f80u || x == 0xff80u || (y & 0x7fffu) > 0x7f80u || y == 0xff80u)
-                        bits |= 1u << ((2 * wd + hf) & 31);
+    for (int i = 0; i < D / 32; ++i) nf[i] = 0u;
+#pragma unroll 1
+    for (int ch = 0; ch < NCH; ch += 2) {
+        uint4 ma[2] = {}, na[2] = {}, mb[2] = {}, nb[2] = {};
+        if (va) page_extrema<T, RB>(Kh, pa, C, Lc, ch, ma, na);
+        if (vb) page_extrema<T, RB>(Kh, pb, C, Lc, ch, mb, nb);
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+#pragma unroll
+            for (int w = 0; w < WPC; ++w) {
+                const uint32_t am = w == 0 ? ma[u].x : w == 1 ? ma[u].y : w == 2 ? ma[u].z : ma[u].w;
+                const uint32_t an = w == 0 ? na[u].x : w == 1 ? na[u].y : w == 2 ? na[u].z : na[u].w;
+                const uint32_t bm = w == 0 ? mb[u].x : w == 1 ? mb[u].y : w == 2 ? mb[u].z : mb[u].w;
+                const uint32_t bn = w == 0 ? nb[u].x : w == 1 ? nb[u].y : w == 2 ? nb[u].z : nb[u].w;
+                const int d0 = ((ch + u) * WPC + w) * DPW;  // first dimension of the word
+                uint32_t bits = 0u;
+                if (va) bits |= nonfinite_bits<T>(am, an, d0);
+                if (vb) bits |= nonfinite_bits<T>(bm, bn, d0);
+#pragma unroll
+                for (int i = 0; i < D / 32; ++i)
+                    if (i == d0 / 32) nf[i] |= bits;
+                if (!wr) continue;
+                if (ES == 2) {
+                    *reinterpret_cast<uint32_t*>(Sm + (size_t)d0 * npp + pa) = __byte_perm(am, bm, 0x5410);
+                    *reinterpret_cast<uint32_t*>(Sm + (size_t)(d0 + 1) * npp + pa) = __byte_perm(am, bm, 0x7632);
+                    *reinterpret_cast<uint32_t*>(Sm + (size_t)(D + d0) * npp + pa) = __byte_perm(an, bn, 0x5410);
+                    *reinterpret_cast<uint32_t*>(Sm + (size_t)(D + d0 + 1) * npp + pa) = __byte_perm(an, bn, 0x7632);
+                } else {
+                    *reinterpret_cast<uint2*>(Sm + (size_t)d0 * npp + pa) = make_uint2(am, bm);
+                    *reinterpret_cast<uint2*>(Sm + (size_t)(D + d0) * npp + pa) = make_uint2(an, bn);
                 }
-            } else if ((m & 0x7fffffffu) > 0x7f800000u || m == 0xff800000u || (n & 0x7fffffffu) > 0x7f800000u ||
-                       n == 0xff800000u) {
-                bits = 1u << (wd & 31);
             }
-            if (bits) atomicOr(&nfm[(ES == 2 ? 2 * wd : wd) >> 5], bits);
-        }
-        if (ES == 2) {
-            tile[(0 * D + 2 * wd) * TP + p] = (T)(m & 0xffffu);
-            tile[(0 * D + 2 * wd + 1) * TP + p] = (T)(m >> 16);
-            tile[(1 * D + 2 * wd) * TP + p] = (T)(n & 0xffffu);
-            tile[(1 * D + 2 * wd + 1) * TP + p] = (T)(n >> 16);
-        } else {
-            reinterpret_cast<uint32_t*>(tile)[(0 * D + wd) * TP + p] = m;
-            reinterpret_cast<uint32_t*>(tile)[(1 * D + wd) * TP + p] = n;
         }
     }
-    __syncthreads();
-    if (threadIdx.x < D / 32 && nfm[threadIdx.x])
-        atomicOr(reinterpret_cast<uint32_t*>(summary + (size_t)b * sum_stride + mask_off) + hk * (D / 32) + threadIdx.x,
-                 nfm[threadIdx.x]);
-    // rows of TP pages out, 16 bytes at a time (npp and TP are multiples of 8 pages)
-    const int np = min(TP, npp - p0);
-    const int vpr = np * ES / 16;
-    uint8_t* Sb = summary + (size_t)b * sum_stride + (size_t)hk * 2 * D * npp * ES;
-    for (int x = threadIdx.x; x < 2 * D * vpr; x += kSumBuildNT) {
-        const int row = x / vpr, v = x % vpr;
-        *reinterpret_cast<uint4*>(Sb + ((size_t)row * npp + p0) * ES + 16 * v) =
-            *reinterpret_cast<const uint4*>(smraw + ((size_t)row * TP) * ES + 16 * v);
+    uint32_t* mask = reinterpret_cast<uint32_t*>(summary + (size_t)b * sum_stride + mask_off) + hk * (D / 32);
+#pragma unroll
+    for (int i = 0; i < D / 32; ++i) {
+        const uint32_t m = __reduce_or_sync(0xffffffffu, nf[i]);
+        if (lane == 0 && m) atomicOr(mask + i, m);
     }
 }
 
@@ -1617,18 +1661,11 @@ HsaSummaryShape hsa_summary_shape(const rkv_config& c, int dtype, int len_k, int
 template <typename T, int D>
 static int build_t(const uint8_t* K, int HK, int len_k, long long kv_stride, const HsaSummaryShape& s,
                    uint8_t* summary, int batch, cudaStream_t st) {
-    const int rowb = D * (int)sizeof(T);
-    int TP = 16384 / rowb;
-    if (TP > 64) TP = 64;
-    if (TP < 8) TP = 8;
-    const size_t smem = (size_t)2 * D * TP * sizeof(T);
-    auto f = hsa_summary_build_kernel<T, D>;
-    if (smem > 48 * 1024 && cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-        return RKV_ERR_CUDA;
     hsa_summary_mask_clear<<<batch, 128, 0, st>>>(summary, s.item_bytes, s.mask_off, HK * (D / 32));
-    dim3 grid((s.npp + TP - 1) / TP, HK, batch);
-    f<<<grid, kSumBuildNT, smem, st>>>(K, kv_stride, len_k, s.C, s.Lc, s.nchunks, s.npp, TP, summary, s.item_bytes,
-                                        s.mask_off);
+    constexpr int pages_per_cta = (kSumBuildNT / 32) * kBuildPagesPerWarp;
+    dim3 grid((s.npp + pages_per_cta - 1) / pages_per_cta, HK, batch);
+    hsa_summary_build_kernel<T, D><<<grid, kSumBuildNT, 0, st>>>(K, kv_stride, len_k, s.C, s.Lc, s.nchunks, s.npp,
+                                                                 summary, s.item_bytes, s.mask_off);
     return cudaGetLastError() == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
 }
 
