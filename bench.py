@@ -451,6 +451,34 @@ def time_evict_q8(device, steps, warmup, layers=28):
                         "seeded on the device (scales |N(0,0.02)|, int8 uniform [-127,127])"}
 
 
+def time_summary_build(device, steps, warmup):
+    """The page-summary build of the headline caches (64 sequences x 28 layers
+    of bf16 K [8, 3717, 128], page 2): ms per call and GB/s of K read plus
+    summaries written."""
+    import torch
+    p, cache, cfg = decode_params()
+    items = SEQS * LAYERS
+    g = torch.Generator(device=device).manual_seed(5)
+    K = torch.randn((items, HK, cache, D), generator=g, device=device).to(torch.bfloat16)
+    import rocketkv_b200 as rkv
+    dec = rkv.HsaDecoder(cfg, cache, items, device, recent_window=WINDOW)
+    S = dec.build_summary(K)
+    st = torch.cuda.current_stream()
+    for _ in range(warmup):
+        dec.build_summary(K)
+    ts = []
+    for _ in range(steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        dec.build_summary(K)
+        e1.record(st)
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    ms = statistics.median(ts)
+    moved = items * HK * (cache - WINDOW) * D * 2 + int(S.numel())
+    return {"ms": round(ms, 3), "bytes_moved": moved, "gbs": round(moved / (ms / 1e3) / 1e9, 1)}
+
+
 def e2e_decode(cfg, cache, Qs, K, V, steps):
     """Same step through the host-buffer C ABI: pinned host Q/K/V in, O out."""
     import torch
@@ -796,9 +824,24 @@ def main():
                     help="sequences per GPU (smaller values are profiling cases, not the benchmark)")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layers per step (smaller values are profiling cases, not the benchmark)")
+    ap.add_argument("--only", default=None, choices=["q8_eviction", "fp32_eviction", "config1", "summary_build"],
+                    help="run one bench item alone and print its result (profiling case, not the benchmark line)")
     args = ap.parse_args()
     set_workload(args.seqs, args.layers)
     args.warmup = max(args.warmup, 3)
+    if args.only:
+        import torch
+        device = torch.device("cuda", 0)
+        if args.only == "q8_eviction":
+            out = time_evict_q8(device, args.steps, args.warmup, layers=args.layers)
+        elif args.only == "fp32_eviction":
+            out = dict(zip(("ms_per_layer", "e2e_ms_per_layer", "kernels"), time_evict(device, args.steps, args.warmup)))
+        elif args.only == "config1":
+            out = time_config1(device, args.steps, args.warmup)
+        else:
+            out = time_summary_build(device, args.steps, args.warmup)
+        print(json.dumps({"only": args.only, "result": out}))
+        return
 
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -30,20 +30,21 @@
 // repacking and MMAs of pass 1 run ahead while the epilogue waits at the grid
 // barrier.  If the cooperative launch is refused, one launch per pass.
 //
-// Tensor memory: two slots, each holding one half of a tile's query rows
-// (NH = NP / 2 columns per block, four blocks), so the epilogue drains one
-// half while the MMAs of the next half run.
+// Tensor memory: a ring of four slots, each holding the four block
+// accumulators of one part of a tile (32 query rows: the MMA N), so the MMAs
+// run up to three parts ahead of the epilogue and their latency is hidden.
 //
-// Warp roles (448 threads):
+// Warp roles (640 threads):
 //   warp 0      producer: one bulk copy per tile visit of the tile's rows
 //               (128 rows of 136 bytes, contiguous in K) into a raw ring;
 //   warp 1      tensor memory and the MMAs (one elected lane issues);
-//   warps 2-5   converters: each thread repacks one raw row into the int8
+//   warps 2-3   converters: each thread repacks two raw rows into the int8
 //               operand (four 32-byte blocks in a 128-byte row, the K-major
 //               128-byte-swizzle layout) and the key's block scales; at a new
 //               KV head, the window query rows and their scales;
-//   warps 6-13  epilogue, two warps per tensor-memory lane quarter, each
-//               taking half of the columns (query rows) of a half-tile.
+//   warps 4-19  epilogue, four warps per tensor-memory lane quarter, each
+//               taking 8 of a part's 32 query rows (one 8-column chunk of
+//               every block accumulator).
 // Every wait is bounded; a role that times out sets a CTA-wide abort flag.
 #include "evict.cuh"
 #include "tc_common.cuh"
@@ -53,8 +54,10 @@
 namespace rkv {
 namespace {
 
-constexpr int kQ8Threads = 448;
-constexpr int kQ8Epi = 256;
+constexpr int kQ8Threads = 640;
+constexpr int kQ8Epi = 512;       // epilogue threads: four warps per tensor-memory lane quarter
+constexpr int kEpiMembers = 4;     // epilogue warps per lane quarter, 8 of a part's 32 query rows each
+constexpr int kQ8Conv = 64;  // converter threads (two warps, two rows each per tile)
 constexpr int kQ8RowB = 136;                 // bytes of one q8_0 row of 128 values
 constexpr int kQ8TileB = 128 * kQ8RowB;      // raw bytes of a full tile (17408, a multiple of 16)
 constexpr int kOpB = 128 * 128;              // repacked int8 operand of a tile
@@ -66,8 +69,11 @@ constexpr int kBarConvQ8 = 1, kBarEpiQ8 = 2;
 constexpr uint32_t kMagicBits = 0x4B400000u;  // 1.5 * 2^23
 constexpr float kMagic = 12582912.0f;
 
+constexpr int kPartRows = 32;  // query rows of one MMA part (N)
+constexpr int kSlots = 4;      // tensor-memory slots of 4 blocks x kPartRows columns
+
 struct Q8Plan {
-    int NP, NH;  // query rows padded to a multiple of 32, and half of that (the MMA N)
+    int NP, NPT;  // query rows padded to a multiple of 32, and the parts of a tile (NP / 32)
     int SR;      // raw ring stages
     int off_raw, off_op, off_q, off_dq, off_dk, off_part, off_rtab, off_red, total;
     int nwork, nheads, p0, p1;
@@ -76,7 +82,7 @@ struct Q8Plan {
 inline Q8Plan q8_plan(int R) {
     Q8Plan P{};
     P.NP = (R + 31) & ~31;
-    P.NH = P.NP / 2;
+    P.NPT = P.NP / kPartRows;
     int off = 1024;  // barriers, tensor-memory slot, abort flag
     P.off_op = off;
     off += kOpStages * kOpB;
@@ -91,7 +97,7 @@ inline Q8Plan q8_plan(int R) {
     P.off_rtab = off;
     off += 64 * 16;  // pass 1: [row pair] (-M_r, -M_r+1, inv_r, inv_r+1)
     P.off_red = off;
-    off += 2 * 128 * 4;  // pass 1: [member][key] partial head scores
+    off += kEpiMembers * 128 * 4;  // pass 1: [member][key] partial head scores
     off = (off + 127) & ~127;
     P.off_raw = off;
     const int room = 227 * 1024 - 1024 - off;
@@ -106,7 +112,7 @@ struct Q8Bars {
 };
 __device__ __forceinline__ Q8Bars q8_bars(uint8_t* sm) {
     uint64_t* b = reinterpret_cast<uint64_t*>(sm);
-    return Q8Bars{b, b + 8, b + 16, b + 18, b + 20, b + 24, b + 28, b + 30, b + 32, b + 34, b + 36, b + 38};
+    return Q8Bars{b, b + 8, b + 16, b + 18, b + 20, b + 24, b + 28, b + 32, b + 36, b + 38, b + 40, b + 42};
 }
 
 __device__ __forceinline__ void unit_of(const EvictArgs& a, int w, int& b, int& hc, int& tile) {
@@ -141,27 +147,32 @@ __device__ __forceinline__ void q8_range(const Q8Plan& P, int ntiles, int& w0, i
 
 __device__ __forceinline__ int sw128_off(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
 
-// One raw q8_0 row (34 words: the 136 bytes of four {fp16 d; int8 q[32]}
-// blocks) -> the four int8 blocks as 32 words (block b at words 8b .. 8b+7)
-// and the four scales.  Blocks 0 and 2 start two bytes into a word.
-__device__ __forceinline__ void q8_row_split(const uint32_t (&w)[34], uint32_t (&o)[32], float (&d)[4]) {
+// Half H of a raw q8_0 row (four {fp16 d; int8 q[32]} blocks, 136 bytes, 8-byte aligned; shared or global
+// memory): blocks 2H and 2H + 1, bytes 68H .. 68H + 67, read as the 18 words from word 16H -> the two int8
+// blocks at 16-byte chunks 4H .. 4H + 3 of operand row r (K-major, 128-byte swizzle), and their scales.
+template <int H>
+__device__ __forceinline__ void q8_half_repack(const uint8_t* raw_row, uint8_t* op, int r, float* d) {
+    const uint2* src = reinterpret_cast<const uint2*>(raw_row) + 8 * H;
+    uint32_t w[18];
+#pragma unroll
+    for (int t = 0; t < 9; ++t) {
+        const uint2 u = src[t];
+        w[2 * t] = u.x;
+        w[2 * t + 1] = u.y;
+    }
+    // in the half's words: block 2H starts two bytes into word H (its scale is the low half of word H),
+    // block 2H + 1 at word H + 9 (its scale is the high half of word H + 8)
+    uint32_t o[16];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-        o[j] = __funnelshift_r(w[j], w[j + 1], 16);
-        o[8 + j] = w[9 + j];
-        o[16 + j] = __funnelshift_r(w[17 + j], w[18 + j], 16);
-        o[24 + j] = w[26 + j];
+        o[j] = __funnelshift_r(w[H + j], w[H + j + 1], 16);
+        o[8 + j] = w[H + 9 + j];
     }
-    d[0] = __half2float(__ushort_as_half((unsigned short)(w[0] & 0xFFFFu)));
-    d[1] = __half2float(__ushort_as_half((unsigned short)(w[8] >> 16)));
-    d[2] = __half2float(__ushort_as_half((unsigned short)(w[17] & 0xFFFFu)));
-    d[3] = __half2float(__ushort_as_half((unsigned short)(w[25] >> 16)));
-}
-
-__device__ __forceinline__ void store_op_row(uint8_t* op, int r, const uint32_t (&o)[32]) {
+    d[0] = __half2float(__ushort_as_half((unsigned short)(w[H] & 0xFFFFu)));
+    d[1] = __half2float(__ushort_as_half((unsigned short)(w[H + 8] >> 16)));
 #pragma unroll
-    for (int c = 0; c < 8; ++c)
-        *reinterpret_cast<uint4*>(op + sw128_off(r, c)) = make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+    for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<uint4*>(op + sw128_off(r, 4 * H + c)) = make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
 }
 
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
@@ -237,26 +248,28 @@ __global__ void __launch_bounds__(kQ8Threads, 1) evict_q8_kernel(const EvictArgs
     int w0, nt;
     q8_range(P, a.ntiles, w0, nt);
     Visit V{P.p0 == 0 ? 0 : nt, P.p1 == 1 ? 2 * nt : nt, nt, w0};
-    const int SR = P.SR, NP = P.NP, NH = P.NH;
+    const int SR = P.SR, NP = P.NP, NPT = P.NPT;
     auto head_of = [&](int v) { return V.unit(v) / a.ntiles; };
 
     if (tid == 0) {
         for (int i = 0; i < SR; ++i) {
             mbar_init(&B.raw_full[i], 1);
-            mbar_init(&B.raw_empty[i], 4);  // one arrival per converter warp
+            mbar_init(&B.raw_empty[i], kQ8Conv / 32);  // one arrival per converter warp
         }
         for (int i = 0; i < kOpStages; ++i) {
-            mbar_init(&B.op_full[i], 4);
+            mbar_init(&B.op_full[i], kQ8Conv / 32);
             mbar_init(&B.op_empty[i], 1);
         }
         for (int i = 0; i < kScStages; ++i) {
-            mbar_init(&B.dk_full[i], 4);
+            mbar_init(&B.dk_full[i], kQ8Conv / 32);
             mbar_init(&B.dk_empty[i], kQ8Epi / 32);
         }
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < kSlots; ++i) {
             mbar_init(&B.acc_full[i], 1);
             mbar_init(&B.acc_empty[i], kQ8Epi / 32);
-            mbar_init(&B.q_full[i], 4);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&B.q_full[i], kQ8Conv / 32);
             mbar_init(&B.q_empty_mma[i], 1);
             mbar_init(&B.q_empty_epi[i], kQ8Epi / 32);
         }
@@ -299,7 +312,7 @@ __global__ void __launch_bounds__(kQ8Threads, 1) evict_q8_kernel(const EvictArgs
         __syncwarp();
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
-        const uint32_t idesc = idesc_i8((uint32_t)NH);
+        const uint32_t idesc = idesc_i8((uint32_t)kPartRows);
         int hv = -1, prev = -1;
         bool ok = true;
         for (int v = V.v0; v < V.v1 && ok; ++v) {
@@ -316,19 +329,21 @@ __global__ void __launch_bounds__(kQ8Threads, 1) evict_q8_kernel(const EvictArgs
             if (!__all_sync(0xffffffffu,
                             mbar_wait_or_abort(&B.op_full[o], (uint32_t)((x / kOpStages) & 1), a.err, abort_flag)))
                 break;
-            for (int h = 0; h < 2; ++h) {
-                const int j = 2 * x + h, slot = j & 1;
-                if (!__all_sync(0xffffffffu,
-                                mbar_wait_or_abort(&B.acc_empty[slot], (uint32_t)((j >> 1) & 1), a.err, abort_flag))) {
+            for (int pt = 0; pt < NPT; ++pt) {  // one part of 32 query rows per tensor-memory slot
+                const int j = x * NPT + pt, slot = j % kSlots;
+                if (!__all_sync(0xffffffffu, mbar_wait_or_abort(&B.acc_empty[slot], (uint32_t)((j / kSlots) & 1),
+                                                                a.err, abort_flag))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint64_t dA = mma_desc_sw128(smem_u32(sm + P.off_op + o * kOpB));
-                const uint64_t dB = mma_desc_sw128(smem_u32(sm + P.off_q + (hv & 1) * NP * 128 + h * NH * 128));
+                const uint64_t dB =
+                    mma_desc_sw128(smem_u32(sm + P.off_q + (hv & 1) * NP * 128 + pt * kPartRows * 128));
 #pragma unroll
                 for (int blk = 0; blk < 4; ++blk)  // a 32-byte K step adds 2 to the start-address field
-                    mma_i8_w(tbase + (uint32_t)(slot * 4 * NH + blk * NH), dA + 2 * blk, dB + 2 * blk, idesc);
+                    mma_i8_w(tbase + (uint32_t)(slot * 4 * kPartRows + blk * kPartRows), dA + 2 * blk, dB + 2 * blk,
+                             idesc);
                 mma_commit_w(&B.acc_full[slot]);
             }
             if (!ok) break;
@@ -338,7 +353,7 @@ __global__ void __launch_bounds__(kQ8Threads, 1) evict_q8_kernel(const EvictArgs
         mma_commit_w(B.mma_done);
         mbar_wait_bounded(B.mma_done, 0u, a.err);
         __syncwarp();
-    } else if (warp < 6) {
+    } else if (warp < 4) {
         // ---------------- converters ----------------
         const int ct = tid - 64;
         const float qscale = a.inv_sqrt_d * 1.4426950408889634f;  // 1/sqrt(D) * log2(e)
@@ -358,35 +373,24 @@ __global__ void __launch_bounds__(kQ8Threads, 1) evict_q8_kernel(const EvictArgs
                     if (w)
                         w = mbar_wait_or_abort(&B.q_empty_epi[qb], (uint32_t)(((hv >> 1) + 1) & 1), a.err, abort_flag);
                 }
-                if (!group_all(kBarConvQ8, 128, w)) break;
+                if (!group_all(kBarConvQ8, kQ8Conv, w)) break;
                 // window row ct of the KV head's query group (rocket.cpp:85-90)
                 uint8_t* qop = sm + P.off_q + qb * NP * 128;
                 float2* dqt = reinterpret_cast<float2*>(sm + P.off_dq) + qb * (NP / 2) * 4;
-                if (ct < NP) {
-                    uint32_t o[32];
-                    float d[4];
-                    if (ct < a.R) {
+                for (int rr = ct; rr < NP; rr += kQ8Conv) {
+                    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    if (rr < a.R) {
                         const int hk = a.head_begin + hc;
-                        const int h = hk * a.G + ct / a.obs_w, pos = a.q_row0 + ct % a.obs_w;
-                        const uint2* src = reinterpret_cast<const uint2*>(a.Q + (size_t)b * a.q_stride +
-                                                                          ((size_t)h * a.q_head_rows + pos) * kQ8RowB);
-                        uint32_t wv[34];
-#pragma unroll
-                        for (int t = 0; t < 17; ++t) {
-                            const uint2 u = __ldg(src + t);
-                            wv[2 * t] = u.x;
-                            wv[2 * t + 1] = u.y;
-                        }
-                        q8_row_split(wv, o, d);
+                        const int h = hk * a.G + rr / a.obs_w, pos = a.q_row0 + rr % a.obs_w;
+                        const uint8_t* qrow = a.Q + (size_t)b * a.q_stride + ((size_t)h * a.q_head_rows + pos) * kQ8RowB;
+                        q8_half_repack<0>(qrow, qop, rr, d);
+                        q8_half_repack<1>(qrow, qop, rr, d + 2);
                     } else {
 #pragma unroll
-                        for (int t = 0; t < 32; ++t) o[t] = 0u;
-#pragma unroll
-                        for (int t = 0; t < 4; ++t) d[t] = 0.0f;
+                        for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(qop + sw128_off(rr, c)) = make_uint4(0u, 0u, 0u, 0u);
                     }
-                    store_op_row(qop, ct, o);
 #pragma unroll
-                    for (int t = 0; t < 4; ++t) reinterpret_cast<float*>(dqt + (ct >> 1) * 4 + t)[ct & 1] = d[t] * qscale;
+                    for (int t = 0; t < 4; ++t) reinterpret_cast<float*>(dqt + (rr >> 1) * 4 + t)[rr & 1] = d[t] * qscale;
                 }
                 fence_proxy_async();
                 __syncwarp();
@@ -399,30 +403,24 @@ __global__ void __launch_bounds__(kQ8Threads, 1) evict_q8_kernel(const EvictArgs
                 w = mbar_wait_or_abort(&B.op_empty[o], (uint32_t)(((x / kOpStages) + 1) & 1), a.err, abort_flag);
             if (w && x >= kScStages)
                 w = mbar_wait_or_abort(&B.dk_empty[ds], (uint32_t)(((x / kScStages) + 1) & 1), a.err, abort_flag);
-            if (!group_all(kBarConvQ8, 128, w)) break;
+            if (!group_all(kBarConvQ8, kQ8Conv, w)) break;
             const int nkeys = min(kMmaM, a.nk - tile * kMmaM);
-            uint32_t ob[32];
-            float d[4];
-            if (ct < nkeys) {
-                const uint2* src = reinterpret_cast<const uint2*>(sm + P.off_raw + (size_t)s * kQ8TileB + ct * kQ8RowB);
-                uint32_t wv[34];
+#pragma unroll 1
+            for (int rr = ct; rr < kMmaM; rr += kQ8Conv) {
+                float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                uint8_t* orow = sm + P.off_op + o * kOpB;
+                if (rr < nkeys) {
+                    const uint8_t* raw_row = sm + P.off_raw + (size_t)s * kQ8TileB + rr * kQ8RowB;
+                    q8_half_repack<0>(raw_row, orow, rr, d);
+                    q8_half_repack<1>(raw_row, orow, rr, d + 2);
+                } else {
 #pragma unroll
-                for (int t = 0; t < 17; ++t) {
-                    const uint2 u = src[t];
-                    wv[2 * t] = u.x;
-                    wv[2 * t + 1] = u.y;
+                    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(orow + sw128_off(rr, c)) = make_uint4(0u, 0u, 0u, 0u);
                 }
-                q8_row_split(wv, ob, d);
-            } else {
-#pragma unroll
-                for (int t = 0; t < 32; ++t) ob[t] = 0u;
-#pragma unroll
-                for (int t = 0; t < 4; ++t) d[t] = 0.0f;
+                *reinterpret_cast<float4*>(sm + P.off_dk + (size_t)(ds * 128 + rr) * 16) = make_float4(d[0], d[1], d[2], d[3]);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive1(&B.raw_empty[s]);  // the raw rows are read
-            store_op_row(sm + P.off_op + o * kOpB, ct, ob);
-            *reinterpret_cast<float4*>(sm + P.off_dk + (size_t)(ds * 128 + ct) * 16) = make_float4(d[0], d[1], d[2], d[3]);
             fence_proxy_async();
             __syncwarp();
             if (lane == 0) {
@@ -432,8 +430,7 @@ __global__ void __launch_bounds__(kQ8Threads, 1) evict_q8_kernel(const EvictArgs
         }
     } else {
         // ---------------- epilogue ----------------
-        const int ep = warp - 6, et = tid - 192, q = warp & 3, mem = ep >> 2;
-        const int HC = NH / 2;  // columns (query rows) of a half-tile this warp takes
+        const int ep = warp - 4, et = tid - 128, q = warp & 3, mem = ep >> 2;
         const int kk = q * 32 + lane;
         const uint32_t tlane = tbase + ((uint32_t)(q * 32) << 16);
         float2* part = reinterpret_cast<float2*>(sm + P.off_part);  // [2][4][128]
@@ -459,17 +456,15 @@ __global__ void __launch_bounds__(kQ8Threads, 1) evict_q8_kernel(const EvictArgs
             inv = 1.0f / (S + 1e-9f);
         };
 
-        // both slots start free: their accumulators are preset
-        for (int sl = 0; sl < 2; ++sl)
+        // every slot starts free: its accumulators are preset
+        for (int sl = 0; sl < kSlots; ++sl)
             for (int blk = 0; blk < 4; ++blk)
-                for (int c = 0; c < HC; c += 8) tmem_st8_magic(tlane + (uint32_t)(sl * 4 * NH + blk * NH + mem * HC + c));
+                tmem_st8_magic(tlane + (uint32_t)(sl * 4 * kPartRows + blk * kPartRows + mem * 8));
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-            mbar_arrive1(&B.acc_empty[0]);
-            mbar_arrive1(&B.acc_empty[1]);
-        }
+        if (lane == 0)
+            for (int sl = 0; sl < kSlots; ++sl) mbar_arrive1(&B.acc_empty[sl]);
 
         // one tile visit of the epilogue; false when a wait gave up
         auto visit = [&](int v) -> bool {
@@ -498,7 +493,7 @@ __global__ void __launch_bounds__(kQ8Threads, 1) evict_q8_kernel(const EvictArgs
                             rtab[p] = make_float4(-s0.x, -s1.x, s0.y, s1.y);
                         }
                     } else {
-                        for (int r = ep; r < NP; r += 8) {
+                        for (int r = ep; r < NP; r += kQ8Epi / 32) {
                             float M = 0.0f, inv = 0.0f;
                             if (r < a.R) fold_row(row_base + r, M, inv);
                             if (lane == 0) {
@@ -514,109 +509,123 @@ __global__ void __launch_bounds__(kQ8Threads, 1) evict_q8_kernel(const EvictArgs
             const float2* dqt = reinterpret_cast<const float2*>(sm + P.off_dq) + (hv & 1) * (NP / 2) * 4;
             // this key's block scales and the exact addends -1.5 * 2^23 * dk
             const int ds = x % kScStages;
-            {
-                const bool w = mbar_wait_or_abort(&B.dk_full[ds], (uint32_t)((x / kScStages) & 1), a.err, abort_flag);
-                if (!group_all(kBarEpiQ8, kQ8Epi, w)) return false;
-            }
-            const float4 dk4 = *reinterpret_cast<const float4*>(sm + P.off_dk + (size_t)(ds * 128 + kk) * 16);
+            // waits are warp-level here; a failed one skips the warp's work and the tile's barrier below
+            // makes the exit decision uniform
+            bool good = __all_sync(0xffffffffu, mbar_wait_or_abort(&B.dk_full[ds], (uint32_t)((x / kScStages) & 1),
+                                                                    a.err, abort_flag));
+            const float4 dk4 =
+                good ? *reinterpret_cast<const float4*>(sm + P.off_dk + (size_t)(ds * 128 + kk) * 16) : make_float4(0, 0, 0, 0);
             __syncwarp();
-            if (lane == 0) mbar_arrive1(&B.dk_empty[ds]);
-            const float dk[4] = {dk4.x, dk4.y, dk4.z, dk4.w};
-            const float cdk[4] = {-kMagic * dk4.x, -kMagic * dk4.y, -kMagic * dk4.z, -kMagic * dk4.w};
-            const bool kvalid = kk < nkeys;
+            if (lane == 0 && good) mbar_arrive1(&B.dk_empty[ds]);
+            // the key's block scales and the exact addends -1.5 * 2^23 * dk, as pairs for the paired fma
+            const float2 dk2[4] = {make_float2(dk4.x, dk4.x), make_float2(dk4.y, dk4.y), make_float2(dk4.z, dk4.z),
+                                   make_float2(dk4.w, dk4.w)};
+            const float2 cdk2[4] = {make_float2(-kMagic * dk4.x, -kMagic * dk4.x), make_float2(-kMagic * dk4.y, -kMagic * dk4.y),
+                                    make_float2(-kMagic * dk4.z, -kMagic * dk4.z), make_float2(-kMagic * dk4.w, -kMagic * dk4.w)};
+            const bool kvalid = kk < nkeys, full = nkeys == kMmaM;  // full: every key of the tile is valid (uniform)
             float2 hsacc = make_float2(0.0f, 0.0f);
-            for (int h = 0; h < 2; ++h) {
-                const int j = 2 * x + h, slot = j & 1;
-                const bool w = mbar_wait_or_abort(&B.acc_full[slot], (uint32_t)((j >> 1) & 1), a.err, abort_flag);
-                if (!group_all(kBarEpiQ8, kQ8Epi, w)) return false;
-                tc_fence_after();
-                const int rb = h * NH + mem * HC;  // this warp's first query row of the half
-                for (int c = 0; c < HC; c += 8) {
-                    uint32_t xv[4][8];
+            // logits of rows r0 .. r0 + 7 (base-2 units) from one 8-column chunk of the four block
+            // accumulators, then the pass's use of them
+            auto chunk = [&](const uint32_t (&xv)[4][8], int r0) {
+                float l[8];
+                const float2* dq2 = dqt + (r0 >> 1) * 4;
 #pragma unroll
-                    for (int blk = 0; blk < 4; ++blk)
-                        tmem_ld8(tlane + (uint32_t)(slot * 4 * NH + blk * NH + mem * HC + c), xv[blk]);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int blk = 0; blk < 4; ++blk)
-                        tmem_st8_magic(tlane + (uint32_t)(slot * 4 * NH + blk * NH + mem * HC + c));
-                    // logits of rows rb + c .. rb + c + 7, base-2 units, in row pairs
-                    float l[8];
-                    const float2* dq2 = dqt + ((rb + c) >> 1) * 4;
-#pragma unroll
-                    for (int p = 0; p < 4; ++p) {
-                        const float4 s01 = *reinterpret_cast<const float4*>(dq2 + p * 4);      // blocks 0, 1
-                        const float4 s23 = *reinterpret_cast<const float4*>(dq2 + p * 4 + 2);  // blocks 2, 3
-                        const float2 sq[4] = {make_float2(s01.x, s01.y), make_float2(s01.z, s01.w),
-                                              make_float2(s23.x, s23.y), make_float2(s23.z, s23.w)};
-                        float2 acc;
-                        if (pass == 0) {
-                            acc = make_float2(0.0f, 0.0f);
-                        } else {
-                            const float4 rt = rtab[(rb + c) / 2 + p];
-                            acc = make_float2(rt.x, rt.y);  // -M_r: the chain ends at l - M_r
-                        }
-#pragma unroll
-                        for (int blk = 0; blk < 4; ++blk) {
-                            const float2 X = make_float2(__uint_as_float(xv[blk][2 * p]), __uint_as_float(xv[blk][2 * p + 1]));
-                            const float2 pb = __ffma2_rn(X, make_float2(dk[blk], dk[blk]), make_float2(cdk[blk], cdk[blk]));
-                            acc = __ffma2_rn(sq[blk], pb, acc);
-                        }
-                        l[2 * p] = acc.x;
-                        l[2 * p + 1] = acc.y;
-                    }
+                for (int p = 0; p < 4; ++p) {
+                    const float4 s01 = *reinterpret_cast<const float4*>(dq2 + p * 4);      // blocks 0, 1
+                    const float4 s23 = *reinterpret_cast<const float4*>(dq2 + p * 4 + 2);  // blocks 2, 3
+                    const float2 sq[4] = {make_float2(s01.x, s01.y), make_float2(s01.z, s01.w),
+                                          make_float2(s23.x, s23.y), make_float2(s23.z, s23.w)};
+                    float2 acc;
                     if (pass == 0) {
-                        // per-(row, lane quarter) max and sum of 2^(l - max) over this warp's 32 keys
-                        float e[8], mq[8];
+                        acc = make_float2(0.0f, 0.0f);
+                    } else {
+                        const float4 rt = rtab[r0 / 2 + p];
+                        acc = make_float2(rt.x, rt.y);  // -M_r: the chain ends at l - M_r
+                    }
+#pragma unroll
+                    for (int blk = 0; blk < 4; ++blk) {
+                        const float2 X = make_float2(__uint_as_float(xv[blk][2 * p]), __uint_as_float(xv[blk][2 * p + 1]));
+                        const float2 pb = __ffma2_rn(X, dk2[blk], cdk2[blk]);
+                        acc = __ffma2_rn(sq[blk], pb, acc);
+                    }
+                    l[2 * p] = acc.x;
+                    l[2 * p + 1] = acc.y;
+                }
+                if (pass == 0) {
+                    // per-(row, lane quarter) max and sum of 2^(l - max) over this warp's 32 keys
+                    float e[8], mq[8];
+                    if (full) {
+#pragma unroll
+                        for (int t = 0; t < 8; ++t) {
+                            mq[t] = warp_max(l[t]);
+                            e[t] = ex2_approx(l[t] - mq[t]);
+                        }
+                    } else {
 #pragma unroll
                         for (int t = 0; t < 8; ++t) {
                             const float lv = kvalid ? l[t] : -INFINITY;
                             mq[t] = warp_max(lv);
                             e[t] = kvalid ? ex2_approx(lv - mq[t]) : 0.0f;
                         }
-                        // sums over the 32 lanes by recursive halving: lane L ends with row
-                        // 4 ((L >> 4) & 1) + 2 ((L >> 3) & 1) + ((L >> 2) & 1)
-                        const bool u16 = lane & 16, u8 = lane & 8, u4 = lane & 4;
+                    }
+                    // sums over the 32 lanes by recursive halving: lane L ends with row
+                    // 4 ((L >> 4) & 1) + 2 ((L >> 3) & 1) + ((L >> 2) & 1)
+                    const bool u16 = lane & 16, u8 = lane & 8, u4 = lane & 4;
 #pragma unroll
-                        for (int t = 0; t < 4; ++t) {
-                            const float send = u16 ? e[t] : e[t + 4], keep = u16 ? e[t + 4] : e[t];
-                            e[t] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-                        }
+                    for (int t = 0; t < 4; ++t) {
+                        const float send = u16 ? e[t] : e[t + 4], keep = u16 ? e[t + 4] : e[t];
+                        e[t] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+                    }
 #pragma unroll
-                        for (int t = 0; t < 2; ++t) {
-                            const float send = u8 ? e[t] : e[t + 2], keep = u8 ? e[t + 2] : e[t];
-                            e[t] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-                        }
-                        {
-                            const float send = u4 ? e[0] : e[1], keep = u4 ? e[1] : e[0];
-                            e[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-                        }
-                        e[0] += __shfl_xor_sync(0xffffffffu, e[0], 2);
-                        e[0] += __shfl_xor_sync(0xffffffffu, e[0], 1);
-                        const int jr = (u16 ? 4 : 0) + (u8 ? 2 : 0) + (u4 ? 1 : 0);
-                        float mine = mq[0];
+                    for (int t = 0; t < 2; ++t) {
+                        const float send = u8 ? e[t] : e[t + 2], keep = u8 ? e[t + 2] : e[t];
+                        e[t] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+                    }
+                    {
+                        const float send = u4 ? e[0] : e[1], keep = u4 ? e[1] : e[0];
+                        e[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+                    }
+                    e[0] += __shfl_xor_sync(0xffffffffu, e[0], 2);
+                    e[0] += __shfl_xor_sync(0xffffffffu, e[0], 1);
+                    const int jr = (u16 ? 4 : 0) + (u8 ? 2 : 0) + (u4 ? 1 : 0);
+                    float mine = mq[0];
 #pragma unroll
-                        for (int t = 1; t < 8; ++t)
-                            if (t == jr) mine = mq[t];
-                        const int r = rb + c + jr;
-                        if ((lane & 3) == 0 && r < a.R) part[((x & 1) * 4 + q) * 128 + r] = make_float2(mine, e[0]);
-                    } else if (kvalid) {
-                        // head score terms 2^(l - M_r) * inv_r (rocket.cpp:114-116)
+                    for (int t = 1; t < 8; ++t)
+                        if (t == jr) mine = mq[t];
+                    const int r = r0 + jr;
+                    if ((lane & 3) == 0 && r < a.R) part[((x & 1) * 4 + q) * 128 + r] = make_float2(mine, e[0]);
+                } else if (kvalid) {
+                    // head score terms 2^(l - M_r) * inv_r (rocket.cpp:114-116)
 #pragma unroll
-                        for (int p = 0; p < 4; ++p) {
-                            const float4 rt = rtab[(rb + c) / 2 + p];
-                            const float2 ev = make_float2(ex2_approx(l[2 * p]), ex2_approx(l[2 * p + 1]));
-                            hsacc = __ffma2_rn(ev, make_float2(rt.z, rt.w), hsacc);
-                        }
+                    for (int p = 0; p < 4; ++p) {
+                        const float4 rt = rtab[r0 / 2 + p];
+                        const float2 ev = make_float2(ex2_approx(l[2 * p]), ex2_approx(l[2 * p + 1]));
+                        hsacc = __ffma2_rn(ev, make_float2(rt.z, rt.w), hsacc);
                     }
                 }
+            };
+            for (int pt = 0; pt < NPT && good; ++pt) {  // parts of 32 query rows, one per tensor-memory slot
+                const int j = x * NPT + pt, slot = j % kSlots;
+                good = __all_sync(0xffffffffu, mbar_wait_or_abort(&B.acc_full[slot], (uint32_t)((j / kSlots) & 1),
+                                                                   a.err, abort_flag));
+                if (!good) break;
+                tc_fence_after();
+                // this warp's 8 rows of the part: one 8-column chunk of each of the four blocks
+                const uint32_t col = (uint32_t)(slot * 4 * kPartRows + mem * 8);
+                uint32_t xa[4][8];
+#pragma unroll
+                for (int blk = 0; blk < 4; ++blk) tmem_ld8(tlane + col + (uint32_t)(blk * kPartRows), xa[blk]);
+                tmem_wait_ld();
+#pragma unroll
+                for (int blk = 0; blk < 4; ++blk) tmem_st8_magic(tlane + col + (uint32_t)(blk * kPartRows));
+                chunk(xa, pt * kPartRows + mem * 8);
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive1(&B.acc_empty[slot]);
             }
+            if (!group_all(kBarEpiQ8, kQ8Epi, good)) return false;
             if (pass == 0) {
-                group_sync(kBarEpiQ8, kQ8Epi);
                 if (et < a.R) {  // combine the four lane quarters of the tile
                     const float2* pr = part + (x & 1) * 4 * 128 + et;
                     float M = -INFINITY;
@@ -633,7 +642,8 @@ __global__ void __launch_bounds__(kQ8Threads, 1) evict_q8_kernel(const EvictArgs
             } else {
                 red[mem * 128 + kk] = hsacc.x + hsacc.y;
                 group_sync(kBarEpiQ8, kQ8Epi);
-                if (et < 128 && et < nkeys) a.hs[((size_t)b * a.head_count + hc) * a.nk + k0 + et] = red[et] + red[128 + et];
+                if (et < 128 && et < nkeys)  // the members' partial sums, in member order
+                    a.hs[((size_t)b * a.head_count + hc) * a.nk + k0 + et] = ((red[et] + red[128 + et]) + red[256 + et]) + red[384 + et];
                 group_sync(kBarEpiQ8, kQ8Epi);
             }
             if (v + 1 == V.v1 || head_of(v + 1) != head) {
@@ -653,7 +663,7 @@ __global__ void __launch_bounds__(kQ8Threads, 1) evict_q8_kernel(const EvictArgs
             ok = group_all(kBarEpiQ8, kQ8Epi, gb);
             if (ok) {
                 const size_t nrows = (size_t)P.nheads * a.R;
-                for (size_t xr = blockIdx.x + (size_t)gridDim.x * ep; xr < nrows; xr += (size_t)gridDim.x * 8) {
+                for (size_t xr = blockIdx.x + (size_t)gridDim.x * ep; xr < nrows; xr += (size_t)gridDim.x * (kQ8Epi / 32)) {
                     float M, inv;
                     fold_row(xr, M, inv);
                     if (lane == 0) __stcg(a.rstats + xr, make_float2(M, inv));
