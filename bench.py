@@ -444,8 +444,37 @@ def time_evict_q8(device, steps, warmup, layers=28):
             times.append(e0.elapsed_time(e1))
         assert rkv.lib().rkv_workspace_status(rkv._ptr(ev.ws), 0) == 0, "in-kernel wait timed out"
         out[str(budget)] = round(statistics.mean(times) / layers, 4)
+    # stage 1 and the KV-cache compaction at budget 1024: two calls against the fused call
+    V = q8_rows((layers, HK, PROMPT), gen, device)
+    cfg = rkv.RocketConfig(num_heads=H, num_heads_kv=HK, dim_head=D, prompt_budget=1024)
+    ev = rkv.Evictor(cfg, 32, PROMPT, layers, rkv.Q8_0, device)
+    Ko = torch.empty((layers, HK, 1024, K.shape[3]), dtype=torch.uint8, device=device)
+    Vo = torch.empty_like(Ko)
+
+    def two_calls():
+        kept, n = ev(Q, K)
+        rkv.compact_kv(K, V, kept, n, D, K_out=Ko, V_out=Vo)
+
+    def fused():
+        ev.evict_compact(Q, K, V, K_out=Ko, V_out=Vo)
+
+    res = {}
+    for name, fn in (("evict_then_compact", two_calls), ("evict_compact", fused)):
+        for _ in range(warmup):
+            fn()
+        ts = []
+        for _ in range(steps):
+            flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            fn()
+            e1.record(st)
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        res[name] = round(statistics.mean(ts) / layers, 4)
     kbytes = layers * HK * (PROMPT - 32) * (D // 32) * 34
     return {"ms_per_layer": out, "layers_per_call": layers,
+            "with_compaction_ms_per_layer": res,
             "algorithmic_bytes_per_layer": kbytes // layers + H * 32 * (D // 32) * 34,
             "workload": "stage1 q8_0 K[28][8,8192,128] Q[28][24,32,128] w32 ks63, budgets 512/1024/2048, "
                         "seeded on the device (scales |N(0,0.02)|, int8 uniform [-127,127])"}

@@ -46,18 +46,23 @@ typedef enum rkv_status {
 typedef enum rkv_dtype {
     RKV_F32 = 0,
     RKV_BF16 = 1,
-    RKV_Q8_0 = 2
+    RKV_Q8_0 = 2,
+    RKV_F16 = 3   /* source type of rkv_capture_rows only */
 } rkv_dtype;
 
 /* Stage-1 scoring engine. */
 typedef enum rkv_evict_engine {
     RKV_EVICT_AUTO = 0,   /* the fastest engine built for the inputs          */
     RKV_EVICT_SIMT = 1,   /* fp32 CUDA-core scoring                            */
-    RKV_EVICT_TENSOR = 2, /* tcgen05 tensor-core scoring: fp32 and q8_0 K/Q
-                             (q8_0 dequantised exactly to fp32 in shared
-                             memory) as three TF32 products per step, bf16
-                             directly.  The persistent kernel (one CTA per
-                             SM, TMA-staged K, window queries resident) takes
+    RKV_EVICT_TENSOR = 2, /* tcgen05 tensor-core scoring: fp32 K/Q as three
+                             TF32 products per step, bf16 directly, q8_0 as
+                             exact int8 block products (kind::i8, one int32
+                             accumulator per 32-value block, the fp16 scales
+                             applied exactly afterwards; q8_0 K tiles that are
+                             not 16-byte aligned are dequantised to fp32 and
+                             run as three TF32 products).  The persistent
+                             kernel (one CTA per SM, K tiles staged by bulk or
+                             tensor copies, window queries resident) takes
                              G * window <= 128 with fp32/bf16 rows 16-byte
                              aligned and a multiple of 32 bytes, or q8_0 at
                              dim_head 128; other fp32/bf16 shapes with such
@@ -146,6 +151,26 @@ int rkv_evict_pool_heads(const void* Q, const void* K, int dtype, int len_q, int
 int rkv_evict_select_pooled(const float* pooled, int len_q, int len_k, int batch,
                             const rkv_config* cfg, int* kept, int kept_stride, int* n_kept,
                             void* workspace, size_t workspace_bytes, void* stream);
+
+/* Capture side (the device analogue of the reference runner's eval callback,
+ * runner.cpp:25-92, which copies each micro-batch's post-RoPE Q or K tensor
+ * of the last layer to the host, converts it to fp32 and scatters it into
+ * [heads][prompt tokens][dim_head]).  Scatters one micro-batch of n_tokens
+ * rows as the producing attention left them -- element (t, h, d) at
+ * src + t * token_stride + h * head_stride + d * element size, strides in
+ * bytes, src_dtype RKV_F32, RKV_F16 or RKV_BF16 -- into item `item` of dst,
+ * laid out [n_heads][dst_tokens][dim_head] in dst_dtype (RKV_F32 from any
+ * source, exactly; RKV_BF16 from a BF16 source).  Row t of the micro-batch is
+ * global token token_offset + t and lands in dst row
+ * token_offset + t - dst_first; tokens outside [dst_first, dst_first +
+ * dst_tokens) are skipped (for Q, dst_first = prompt length - window keeps
+ * only the window rows stage 1 reads).  Items (layers) are dst_item_stride
+ * bytes apart, so every layer can be captured and scored in one batched
+ * rkv_evict call.  Device pointers; asynchronous on `stream`; no host copy. */
+int rkv_capture_rows(const void* src, int src_dtype, int n_tokens, int n_heads, int dim_head,
+                     long long token_stride, long long head_stride, int token_offset, void* dst,
+                     int dst_dtype, int dst_first, int dst_tokens, long long dst_item_stride, int item,
+                     void* stream);
 
 /* Host-buffer stage 1, the rocket.h drop-in path: fp32 host Q and K as
  * compute_prefill_eviction takes them; copies in, runs on the current
@@ -278,6 +303,21 @@ int rkv_compact_kv(const void* K, const void* V, int dtype, int head_dim, int nu
                    int len_k, int batch, long long kv_item_stride, const int* kept,
                    const int* n_kept, int kept_stride, void* K_out, void* V_out, int out_len,
                    long long out_item_stride, void* stream);
+
+/* Stage 1 and the KV-cache compaction in one call: rkv_evict on Q and the
+ * cache's own K rows, then rkv_compact_kv of K (and V) with the kept lists
+ * just written, so evicted rows are never moved (the reference runner scores
+ * and then removes the evicted ranges, runner.cpp:241-269).  The compaction
+ * is launched as a programmatic dependent of the selection kernel: its grid
+ * is scheduled while the selection still runs and waits in the kernel for
+ * the kept lists.  Arguments as rkv_evict (K's item stride is kv_item_stride)
+ * and rkv_compact_kv (V nullable; in place when K_out == K, which needs
+ * out_len == len_k).  Asynchronous on `stream`; allocates nothing. */
+int rkv_evict_compact(const void* Q, const void* K, const void* V, int dtype, int len_q, int len_k, int batch,
+                      long long q_item_stride, long long kv_item_stride, const rkv_config* cfg,
+                      int* kept, int kept_stride, int* n_kept, void* K_out, void* V_out, int out_len,
+                      long long out_item_stride, void* workspace, size_t workspace_bytes, int engine,
+                      void* stream);
 
 /* ---- errors raised inside kernels ----------------------------------------
  * Kernels record a failed bounded wait in the workspace.  This synchronises

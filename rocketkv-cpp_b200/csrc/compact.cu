@@ -34,6 +34,10 @@ struct CompactArgs {
 
 template <typename VT>
 __global__ void __launch_bounds__(kCompactNT) compact_kernel(const CompactArgs a) {
+    // Launched as a programmatic dependent of stage 1's selection (rkv_evict_compact) the grid may start
+    // while the selection still runs: this waits until it has completed and its kept lists are visible.
+    // Launched normally there is nothing to wait for.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int hk = blockIdx.y, b = blockIdx.z;
     const int* kept = a.kept + (size_t)b * a.kept_stride;
     const int n = min(a.n_kept[b], a.out_len);
@@ -76,10 +80,13 @@ __global__ void __launch_bounds__(kCompactNT) compact_kernel(const CompactArgs a
 
 using namespace rkv;
 
-extern "C" int rkv_compact_kv(const void* K, const void* V, int dtype, int head_dim, int num_heads_kv, int len_k,
-                              int batch, long long kv_item_stride, const int* kept, const int* n_kept,
-                              int kept_stride, void* K_out, void* V_out, int out_len, long long out_item_stride,
-                              void* stream) {
+namespace {
+
+// Validates, plans and launches one compaction; pdl: as a programmatic dependent launch of the previous
+// kernel on the stream.
+int compact_launch(const void* K, const void* V, int dtype, int head_dim, int num_heads_kv, int len_k, int batch,
+                   long long kv_item_stride, const int* kept, const int* n_kept, int kept_stride, void* K_out,
+                   void* V_out, int out_len, long long out_item_stride, bool pdl, cudaStream_t st) {
     if (dtype != RKV_F32 && dtype != RKV_BF16 && dtype != RKV_Q8_0) return RKV_ERR_INVALID_ARG;
     if (head_dim <= 0 || (dtype == RKV_Q8_0 && head_dim % 32 != 0)) return RKV_ERR_INVALID_ARG;
     if (num_heads_kv <= 0 || len_k < 0 || batch < 0 || out_len < 0 || kept_stride < 0) return RKV_ERR_INVALID_ARG;
@@ -119,13 +126,48 @@ extern "C" int rkv_compact_kv(const void* K, const void* V, int dtype, int head_
     const int chunk_rows = kCompactNT * kCompactVPT / a.vpr;
     const int chunks = out_len > 0 ? (out_len + chunk_rows - 1) / chunk_rows : 1;
     const int split = inplace ? 1 : (chunks < 64 ? chunks : 64);
-    dim3 grid(split > 0 ? split : 1, num_heads_kv, batch);
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(split > 0 ? split : 1, num_heads_kv, batch);
+    cfg.blockDim = dim3(kCompactNT);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaError_t e;
     switch (vb) {
-        case 16: compact_kernel<uint4><<<grid, kCompactNT, 0, st>>>(a); break;
-        case 8: compact_kernel<uint2><<<grid, kCompactNT, 0, st>>>(a); break;
-        case 4: compact_kernel<uint32_t><<<grid, kCompactNT, 0, st>>>(a); break;
-        default: compact_kernel<uint16_t><<<grid, kCompactNT, 0, st>>>(a); break;
+        case 16: e = cudaLaunchKernelEx(&cfg, compact_kernel<uint4>, a); break;
+        case 8: e = cudaLaunchKernelEx(&cfg, compact_kernel<uint2>, a); break;
+        case 4: e = cudaLaunchKernelEx(&cfg, compact_kernel<uint32_t>, a); break;
+        default: e = cudaLaunchKernelEx(&cfg, compact_kernel<uint16_t>, a); break;
     }
-    return cudaGetLastError() == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
+    if (e != cudaSuccess) (void)cudaGetLastError();
+    return e == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" int rkv_compact_kv(const void* K, const void* V, int dtype, int head_dim, int num_heads_kv, int len_k,
+                              int batch, long long kv_item_stride, const int* kept, const int* n_kept,
+                              int kept_stride, void* K_out, void* V_out, int out_len, long long out_item_stride,
+                              void* stream) {
+    return compact_launch(K, V, dtype, head_dim, num_heads_kv, len_k, batch, kv_item_stride, kept, n_kept, kept_stride,
+                          K_out, V_out, out_len, out_item_stride, false, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int rkv_evict_compact(const void* Q, const void* K, const void* V, int dtype, int len_q, int len_k,
+                                 int batch, long long q_item_stride, long long kv_item_stride, const rkv_config* cfg,
+                                 int* kept, int kept_stride, int* n_kept, void* K_out, void* V_out, int out_len,
+                                 long long out_item_stride, void* workspace, size_t workspace_bytes, int engine,
+                                 void* stream) {
+    if (!cfg || dtype == RKV_F16) return RKV_ERR_INVALID_ARG;
+    if (batch > 0 && (!K_out || (V && !V_out) || (!V && V_out))) return RKV_ERR_INVALID_ARG;
+    int rc = rkv_evict(Q, K, dtype, len_q, len_k, batch, q_item_stride, kv_item_stride, cfg, kept, kept_stride, n_kept,
+                       workspace, workspace_bytes, engine, stream);
+    if (rc != RKV_OK || batch == 0) return rc;
+    // the selection kernel is the last launch on the stream: the compaction starts behind it
+    return compact_launch(K, V, dtype, cfg->dim_head, cfg->num_heads_kv, len_k, batch, kv_item_stride, kept, n_kept,
+                          kept_stride, K_out, V_out, out_len, out_item_stride, true, static_cast<cudaStream_t>(stream));
 }

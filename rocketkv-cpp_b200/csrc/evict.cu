@@ -212,6 +212,7 @@ __global__ void __launch_bounds__(kNT) evict_pool_kernel(PoolArgs a) {
 }
 
 __global__ void __launch_bounds__(kSelNT) evict_select_kernel(SelectArgs a) {
+    asm volatile("griddepcontrol.launch_dependents;");  // a dependent compaction may start (it waits)
     __shared__ int hist[256];
     __shared__ int scan_tmp[66];
     __shared__ uint32_t s_prefix, s_lo[32], s_hi[32];
@@ -337,6 +338,7 @@ __global__ void __launch_bounds__(kSelNT) evict_select_kernel(SelectArgs a) {
 // threshold keys kept)).
 constexpr int kSelPer = 16;
 __global__ void __launch_bounds__(kSelNT) evict_select_reg_kernel(SelectArgs a) {
+    asm volatile("griddepcontrol.launch_dependents;");  // a dependent compaction may start (it waits)
     __shared__ int hist[256];
     __shared__ int scan_tmp[66];
     __shared__ uint32_t s_prefix, s_lo[32], s_hi[32];
@@ -505,6 +507,7 @@ struct SelCoop {
 };
 
 __global__ void __launch_bounds__(kCoopNT) evict_select_coop_kernel(SelectArgs a, SelCoop c) {
+    asm volatile("griddepcontrol.launch_dependents;");  // a dependent compaction may start (it waits)
     __shared__ int hist[256];
     __shared__ int scan_tmp[66];
     __shared__ uint32_t s_lo[16], s_hi[16], s_prefix;
@@ -665,6 +668,7 @@ __global__ void __launch_bounds__(kCoopNT) evict_select_coop_kernel(SelectArgs a
 }
 
 __global__ void evict_keep_all_kernel(int* kept, int kept_stride, int* n_kept, int len_k) {
+    asm volatile("griddepcontrol.launch_dependents;");  // a dependent compaction may start (it waits)
     const int b = blockIdx.y;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < len_k; i += gridDim.x * blockDim.x)
         kept[(size_t)b * kept_stride + i] = i;

@@ -26,7 +26,7 @@ RKV_ERR_WORKSPACE = 4
 RKV_ERR_DEVICE_TIMEOUT = 5
 RKV_ERR_NO_DEVICE = 6
 
-F32, BF16, Q8_0 = 0, 1, 2
+F32, BF16, Q8_0, F16 = 0, 1, 2, 3
 ENGINE_AUTO, ENGINE_SIMT, ENGINE_TENSOR, ENGINE_TENSOR_TILES = 0, 1, 2, 3
 
 # Every symbol include/rkv.h declares.
@@ -37,7 +37,7 @@ EXPORTS = [
     "rkv_hsa_workspace_size", "rkv_hsa_decode", "rkv_hybrid_sparse_decode_host",
     "rkv_hsa_decode_host_ex", "rkv_workspace_status", "rkv_hsa_decode_noalloc", "rkv_hsa_decode_noalloc_status",
     "rkv_selftest_wait_timeout", "rkv_compact_kv", "rkv_hsa_summary_size", "rkv_hsa_build_summary",
-    "rkv_hsa_decode_summary",
+    "rkv_hsa_decode_summary", "rkv_capture_rows", "rkv_evict_compact",
 ]
 
 
@@ -133,6 +133,9 @@ def lib() -> ctypes.CDLL:
         "rkv_hsa_decode_noalloc": ([_VP, _VP, _VP, _I, _I, _I, _I, _LL, _LL, _CFGP, _I, _I, _VP, _VP, _I, _VP,
                                     _VP], _I),
         "rkv_hsa_decode_noalloc_status": ([_VP], _I),
+        "rkv_capture_rows": ([_VP, _I, _I, _I, _I, _LL, _LL, _I, _VP, _I, _I, _I, _LL, _I, _VP], _I),
+        "rkv_evict_compact": ([_VP, _VP, _VP, _I, _I, _I, _I, _LL, _LL, _CFGP, _VP, _I, _VP, _VP, _VP, _I, _LL,
+                               _VP, _SZ, _I, _VP], _I),
         "rkv_compact_kv": ([_VP, _VP, _I, _I, _I, _I, _I, _LL, _VP, _VP, _I, _VP, _VP, _I, _LL, _VP], _I),
         "rkv_hsa_summary_size": ([_CFGP, _I, _I, _I, _I, ctypes.POINTER(_SZ)], _I),
         "rkv_hsa_build_summary": ([_VP, _I, _I, _I, _I, _LL, _CFGP, _VP, _VP], _I),
@@ -272,6 +275,8 @@ def _dtype_of(t) -> int:
         return F32
     if t.dtype == torch.bfloat16:
         return BF16
+    if t.dtype == torch.float16:
+        return F16
     if t.dtype == torch.uint8:
         return Q8_0
     raise TypeError(f"unsupported tensor dtype {t.dtype}")
@@ -302,6 +307,22 @@ class Evictor:
                                Q[0].nbytes if self.batch else 0, K[0].nbytes if self.batch else 0,
                                ctypes.byref(self.c), _ptr(self.kept), self.max_kept, _ptr(self.n_kept),
                                _ptr(self.ws), self.ws_bytes, engine, _stream(stream)), "rkv_evict")
+        return self.kept, self.n_kept
+
+    def evict_compact(self, Q, K, V=None, K_out=None, V_out=None, stream=None, engine: int = ENGINE_AUTO):
+        """Stage 1 on Q and the cache's K, then the cache compacted to the kept
+        rows in the same call (rkv_evict_compact): in place without K_out /
+        V_out, else into K_out / V_out [B, HK, out_len, D*].  Returns (kept, n_kept)."""
+        assert Q.is_contiguous() and K.is_contiguous() and (V is None or V.is_contiguous())
+        if K_out is None:
+            K_out, V_out = K, V
+        _check(lib().rkv_evict_compact(_ptr(Q), _ptr(K), _ptr(V) if V is not None else None, self.dtype, self.len_q,
+                                       self.len_k, self.batch, Q[0].nbytes if self.batch else 0,
+                                       K[0].nbytes if self.batch else 0, ctypes.byref(self.c), _ptr(self.kept),
+                                       self.max_kept, _ptr(self.n_kept), _ptr(K_out),
+                                       _ptr(V_out) if V_out is not None else None, K_out.shape[2],
+                                       K_out[0].nbytes if self.batch else 0, _ptr(self.ws), self.ws_bytes, engine,
+                                       _stream(stream)), "rkv_evict_compact")
         return self.kept, self.n_kept
 
     def pool_heads(self, Q, K, head_begin: int, head_count: int, pooled, stream=None, engine: int = ENGINE_AUTO):
@@ -340,6 +361,23 @@ def compact_kv(K, V, kept, n_kept, dim_head: int, K_out=None, V_out=None, stream
                                 _ptr(V_out) if V_out is not None else None, K_out.shape[2],
                                 K_out[0].nbytes if B else 0, _stream(stream)), "rkv_compact_kv")
     return K_out, V_out
+
+
+def capture_rows(src, dst, token_offset: int, dst_first: int = 0, item: int = 0, stream=None):
+    """The capture side on the device (rkv_capture_rows): one micro-batch of
+    post-RoPE rows src [n_tokens, n_heads, dim_head] (float32, float16 or
+    bfloat16, any strides along tokens and heads, unit stride along dim_head),
+    global tokens token_offset .., scattered into item `item` of dst
+    [items, n_heads, dst_tokens, dim_head] (float32, or bfloat16 from a
+    bfloat16 source), row token - dst_first.  Returns dst."""
+    assert src.dim() == 3 and src.stride(2) == 1 and dst.is_contiguous()
+    n_tokens, n_heads, dim_head = src.shape
+    es = src.element_size()
+    _check(lib().rkv_capture_rows(_ptr(src), _dtype_of(src), n_tokens, n_heads, dim_head, src.stride(0) * es,
+                                  src.stride(1) * es, token_offset, _ptr(dst), _dtype_of(dst), dst_first,
+                                  dst.shape[2], dst[0].nbytes if dst.shape[0] else 0, item, _stream(stream)),
+           "rkv_capture_rows")
+    return dst
 
 
 class HsaDecoder:

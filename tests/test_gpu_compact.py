@@ -120,3 +120,60 @@ def test_evict_then_compact(cuda):
     assert int(n[0]) == m
     np.testing.assert_array_equal(Kt[0, :, :m].cpu().numpy(), K[:, want])
     np.testing.assert_array_equal(Vt[0, :, :m].cpu().numpy(), V[:, want])
+
+
+@pytest.mark.parametrize("kind", ["f32", "bf16", "q8_0"])
+@pytest.mark.parametrize("inplace", [False, True])
+def test_evict_compact_equals_evict_then_compact(kind, inplace, cuda):
+    """rkv_evict_compact (stage 1, then the compaction launched as a dependent
+    of the selection) leaves the same kept lists and the same cache, bit for
+    bit, as rkv_evict followed by rkv_compact_kv."""
+    import torch
+    B, H, HK, D, L, w = 3, 24, 8, 128, 2000, 32
+    cfg = O.Config(num_heads=H, num_heads_kv=HK, dim_head=D, prompt_budget=500)
+    rcfg = rkv.RocketConfig(**{f: getattr(cfg, f) for f in cfg.__dataclass_fields__})
+    if kind == "q8_0":
+        Qh = np.stack([rkvgen.q8_0_inputs(80 + b, (H, w), D)[0] for b in range(B)])
+        Kh = np.stack([rkvgen.q8_0_inputs(90 + b, (HK, L), D)[0] for b in range(B)])
+        Vh = np.stack([rkvgen.q8_0_inputs(95 + b, (HK, L), D)[0] for b in range(B)])
+        to = lambda a: torch.from_numpy(a).to(cuda)
+        dt = rkv.Q8_0
+    else:
+        Qh = np.stack([rkvgen.stage1_inputs(80 + b, H, HK, D, w, L)[0] for b in range(B)])
+        Kh = np.stack([rkvgen.stage1_inputs(80 + b, H, HK, D, w, L)[1] for b in range(B)])
+        Vh = rkvgen.normalish(97, (B, HK, L, D))
+        if kind == "bf16":
+            Qh, Kh, Vh = rkvgen.bf16_bits(rkvgen.bf16_round(Qh)), rkvgen.bf16_bits(rkvgen.bf16_round(Kh)), rkvgen.bf16_bits(rkvgen.bf16_round(Vh))
+            to = lambda a: torch.from_numpy(a).view(torch.bfloat16).to(cuda)
+            dt = rkv.BF16
+        else:
+            to = lambda a: torch.from_numpy(a).to(cuda)
+            dt = rkv.F32
+    Q = to(Qh)
+    # reference: the two calls
+    ev = rkv.Evictor(rcfg, w, L, B, dt, cuda)
+    K1, V1 = to(Kh), to(Vh)
+    kept1, n1 = ev(Q, K1)
+    kept1, n1 = kept1.clone(), n1.clone()
+    out_len = L if inplace else int(cfg.prompt_budget)
+    if inplace:
+        rkv.compact_kv(K1, V1, kept1, n1, D)
+        refK, refV = K1, V1
+    else:
+        refK = torch.zeros((B, HK, out_len) + tuple(K1.shape[3:]), dtype=K1.dtype, device=cuda)
+        refV = torch.zeros_like(refK)
+        rkv.compact_kv(K1, V1, kept1, n1, D, K_out=refK, V_out=refV)
+    # the fused call
+    ev2 = rkv.Evictor(rcfg, w, L, B, dt, cuda)
+    K2, V2 = to(Kh), to(Vh)
+    if inplace:
+        kept2, n2 = ev2.evict_compact(Q, K2, V2)
+        gotK, gotV = K2, V2
+    else:
+        gotK, gotV = torch.zeros_like(refK), torch.zeros_like(refV)
+        kept2, n2 = ev2.evict_compact(Q, K2, V2, K_out=gotK, V_out=gotV)
+    torch.cuda.synchronize()
+    assert rkv.lib().rkv_workspace_status(rkv._ptr(ev2.ws), 0) == 0
+    assert torch.equal(n2, n1) and torch.equal(kept2, kept1)
+    assert torch.equal(gotK.view(torch.uint8), refK.view(torch.uint8))
+    assert torch.equal(gotV.view(torch.uint8), refV.view(torch.uint8))
