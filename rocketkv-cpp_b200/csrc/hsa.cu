@@ -252,6 +252,7 @@ __device__ __forceinline__ void quad_sum(float (&v)[MAXG]) {
 
 template <typename T, int D, int MAXG>
 __global__ void __launch_bounds__(kScanThreads, 2) hsa_scan_kernel(const HsaArgs a) {
+    asm volatile("griddepcontrol.launch_dependents;");  // the selection may be scheduled (it waits for this grid)
     constexpr int ES = (int)sizeof(T);
     constexpr int RB = D * ES;           // bytes per K row
     constexpr int CD = 16 / ES;          // dimensions per 16-byte chunk
@@ -549,6 +550,9 @@ constexpr int kSelThreads = 128;
 
 template <int MAXG, bool SMEM>
 __global__ void __launch_bounds__(kSelThreads, 8) hsa_select_kernel(const HsaArgs a) {
+    // launched as a programmatic dependent of the scan: its page logits are complete and visible after this
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");  // the attention may be scheduled (it waits for this grid)
     extern __shared__ __align__(128) uint8_t sm[];
     uint64_t* lbar = reinterpret_cast<uint64_t*>(sm);
     float* r0 = reinterpret_cast<float*>(sm + 128);  // staged logits [G][NP]
@@ -779,6 +783,8 @@ __global__ void __launch_bounds__(kNT, 3) hsa_attn_kernel(const HsaArgs a) {
     float* sc = SMEM ? sc_s : a.wscore + unit * (size_t)G * a.score_stride;  // [G][score_stride]
 
     for (int e = tid; e < G * D; e += kNT) qf[e] = to_f<T>(reinterpret_cast<const T*>(Qg)[e]);
+    // launched as a programmatic dependent of the selection: its lists are complete and visible after this
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     if (SMEM)
         for (int i = tid; i < n; i += kNT) sel_s[i] = sel_g[i];
     __syncthreads();
@@ -1029,7 +1035,7 @@ __device__ __forceinline__ uint32_t nonfinite_bits(uint32_t m, uint32_t n, int d
 constexpr int kBuildPagesPerWarp = 64;
 
 template <typename T, int D>
-__global__ void __launch_bounds__(kSumBuildNT) hsa_summary_build_kernel(const uint8_t* K, long long kv_stride,
+__global__ void __launch_bounds__(kSumBuildNT, sizeof(T) == 2 ? 4 : 3) hsa_summary_build_kernel(const uint8_t* K, long long kv_stride,
                                                                          int len_k, int C, int Lc, int nchunks,
                                                                          int npp, uint8_t* summary,
                                                                          long long sum_stride, long long mask_off) {
@@ -1044,11 +1050,10 @@ __global__ void __launch_bounds__(kSumBuildNT) hsa_summary_build_kernel(const ui
     const uint8_t* Kh = K + (size_t)b * kv_stride + (size_t)hk * len_k * RB;
     T* Sm = reinterpret_cast<T*>(summary + (size_t)b * sum_stride + (size_t)hk * 2 * D * npp * ES);  // [2][D][npp]
     const bool va = pa < nchunks, vb = pb < nchunks, wr = pa < npp;
-    uint32_t nf[D / 32];
-#pragma unroll
-    for (int i = 0; i < D / 32; ++i) nf[i] = 0u;
+    uint32_t* mask = reinterpret_cast<uint32_t*>(summary + (size_t)b * sum_stride + mask_off) + hk * (D / 32);
 #pragma unroll 1
     for (int ch = 0; ch < NCH; ch += 2) {
+        uint32_t nf = 0u;  // non-finite flags of this chunk pair's dimensions (they share one mask word)
         uint4 ma[2] = {}, na[2] = {}, mb[2] = {}, nb[2] = {};
         if (va) page_extrema<T, RB>(Kh, pa, C, Lc, ch, ma, na);
         if (vb) page_extrema<T, RB>(Kh, pb, C, Lc, ch, mb, nb);
@@ -1061,12 +1066,8 @@ __global__ void __launch_bounds__(kSumBuildNT) hsa_summary_build_kernel(const ui
                 const uint32_t bm = w == 0 ? mb[u].x : w == 1 ? mb[u].y : w == 2 ? mb[u].z : mb[u].w;
                 const uint32_t bn = w == 0 ? nb[u].x : w == 1 ? nb[u].y : w == 2 ? nb[u].z : nb[u].w;
                 const int d0 = ((ch + u) * WPC + w) * DPW;  // first dimension of the word
-                uint32_t bits = 0u;
-                if (va) bits |= nonfinite_bits<T>(am, an, d0);
-                if (vb) bits |= nonfinite_bits<T>(bm, bn, d0);
-#pragma unroll
-                for (int i = 0; i < D / 32; ++i)
-                    if (i == d0 / 32) nf[i] |= bits;
+                if (va) nf |= nonfinite_bits<T>(am, an, d0);
+                if (vb) nf |= nonfinite_bits<T>(bm, bn, d0);
                 if (!wr) continue;
                 if (ES == 2) {
                     *reinterpret_cast<uint32_t*>(Sm + (size_t)d0 * npp + pa) = __byte_perm(am, bm, 0x5410);
@@ -1079,12 +1080,9 @@ __global__ void __launch_bounds__(kSumBuildNT) hsa_summary_build_kernel(const ui
                 }
             }
         }
-    }
-    uint32_t* mask = reinterpret_cast<uint32_t*>(summary + (size_t)b * sum_stride + mask_off) + hk * (D / 32);
-#pragma unroll
-    for (int i = 0; i < D / 32; ++i) {
-        const uint32_t m = __reduce_or_sync(0xffffffffu, nf[i]);
-        if (lane == 0 && m) atomicOr(mask + i, m);
+        // a chunk pair's 16 (bf16) or 8 (fp32) dimensions lie in one 32-dimension mask word
+        const uint32_t m = __reduce_or_sync(0xffffffffu, nf);
+        if (lane == 0 && m) atomicOr(mask + (ch * WPC * DPW) / 32, m);
     }
 }
 
@@ -1230,6 +1228,7 @@ __device__ __forceinline__ void sumscan_score_half(const float* ent, const unsig
 
 template <typename T, int D, int MAXG>
 __global__ void __launch_bounds__(kSumScanNT, 3) hsa_sumscan_kernel(const HsaArgs a) {
+    asm volatile("griddepcontrol.launch_dependents;");  // the selection may be scheduled (it waits for this grid)
     constexpr int ES = (int)sizeof(T);
     constexpr int CD = 16 / ES, NCH = D / CD, NSL = NCH / 4;
     constexpr int TOP = NSL >= 16 ? 4 : NSL >= 8 ? 3 : NSL >= 4 ? 2 : 1;  // log2(NSL)
@@ -1566,8 +1565,22 @@ int launch_t(HsaArgs a, int batch, cudaStream_t st) {
     auto fsel = sel_smem ? hsa_select_kernel<MAXG, true> : hsa_select_kernel<MAXG, false>;
     if (cudaFuncSetAttribute(fsel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_sel) != cudaSuccess)
         return RKV_ERR_CUDA;
-    fsel<<<units, kSelThreads, smem_sel, st>>>(a);
-    if (cudaGetLastError() != cudaSuccess) return RKV_ERR_CUDA;
+    // the selection and the attention are programmatic dependent launches: each is scheduled while its
+    // predecessor's last wave runs and waits in the kernel for that grid's results
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t lc{};
+    lc.gridDim = dim3(units);
+    lc.blockDim = dim3(kSelThreads);
+    lc.dynamicSmemBytes = smem_sel;
+    lc.stream = st;
+    lc.attrs = pdl;
+    lc.numAttrs = 1;
+    if (cudaLaunchKernelEx(&lc, fsel, a) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return RKV_ERR_CUDA;
+    }
     // phase 3 shared memory: [merge buffer][indices][scores]
     constexpr int NGC = kNT / (int)(D * sizeof(T) / 16);
     const size_t merge = (size_t)NGC * MAXG * D * sizeof(float);
@@ -1578,8 +1591,14 @@ int launch_t(HsaArgs a, int batch, cudaStream_t st) {
     auto ft = smem_path ? hsa_attn_kernel<T, D, MAXG, true> : hsa_attn_kernel<T, D, MAXG, false>;
     if (cudaFuncSetAttribute(ft, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_t) != cudaSuccess)
         return RKV_ERR_CUDA;
-    ft<<<dim3(a.head_count, batch), kNT, smem_t, st>>>(a);
-    return cudaGetLastError() == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
+    lc.gridDim = dim3(a.head_count, batch);
+    lc.blockDim = dim3(kNT);
+    lc.dynamicSmemBytes = smem_t;
+    if (cudaLaunchKernelEx(&lc, ft, a) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return RKV_ERR_CUDA;
+    }
+    return RKV_OK;
 }
 
 template <typename T, int D>

@@ -398,15 +398,17 @@ class HsaDecoder:
         self.sel = torch.zeros((batch, self.head_count, self.sel_cap), dtype=torch.int32, device=device)
         self.n_sel = torch.zeros((batch, self.head_count), dtype=torch.int32, device=device)
 
-    def build_summary(self, K, stream=None):
+    def build_summary(self, K, stream=None, out=None):
         """Page summaries of K (every KV head) for this decoder's geometry:
-        later calls with summary=... read them instead of scanning every K row."""
+        later calls with summary=... read them instead of scanning every K row.
+        out: a buffer from an earlier call to rebuild into (no allocation)."""
         import torch
         dt = _dtype_of(K)
         n = ctypes.c_size_t(0)
         _check(lib().rkv_hsa_summary_size(ctypes.byref(self.c), dt, self.len_k, self.w, self.batch, ctypes.byref(n)),
                "rkv_hsa_summary_size")
-        S = torch.empty(max(n.value, 16), dtype=torch.uint8, device=K.device)
+        S = out if out is not None else torch.empty(max(n.value, 16), dtype=torch.uint8, device=K.device)
+        assert S.numel() >= n.value
         _check(lib().rkv_hsa_build_summary(_ptr(K), dt, self.len_k, self.w, self.batch, K[0].nbytes if self.batch else 0,
                                            ctypes.byref(self.c), _ptr(S), _stream(stream)), "rkv_hsa_build_summary")
         return S
