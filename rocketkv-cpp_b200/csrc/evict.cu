@@ -489,75 +489,6 @@ __global__ void __launch_bounds__(kSelNT) evict_select_reg_kernel(SelectArgs a) 
     if (tid == 0) a.n_kept[b] = a.target_keep + a.obs_w;
 }
 
-// The selection of up to kSortMax keys: one 1024-thread CTA per item sorts
-// the keys in shared memory with a bitonic network, descending by the 64-bit
-// composite (order-preserving score key, then 0xFFFFFFFF - index), i.e. by
-// (score desc, index asc) (rocket.cpp:150-155 with the lower index winning
-// ties); the first target_keep entries are marked in a bitmap of positions
-// and written out in ascending order by one block scan (rocket.cpp:161),
-// followed by the observation window (rocket.cpp:163-165).  The head-order
-// sum of the pooled rows is rocket.cpp:143-146.  No atomics on the keys, a
-// fixed number of passes.
-constexpr int kSortMax = 8192;
-constexpr int kSortNT = 1024;
-__global__ void __launch_bounds__(kSortNT) evict_select_sort_kernel(SelectArgs a, int N) {
-    asm volatile("griddepcontrol.launch_dependents;");  // a dependent compaction may start (it waits)
-    extern __shared__ __align__(16) unsigned long long sk[];  // [N] composite keys, then the bitmap
-    uint32_t* bits = reinterpret_cast<uint32_t*>(sk + N);  // [N / 32]
-    __shared__ int scan_tmp[33];
-    const int tid = threadIdx.x, b = blockIdx.x;
-    int* kept = a.kept + (size_t)b * a.kept_stride;
-    for (int i = tid; i < N; i += kSortNT) {
-        unsigned long long c = 0ull;  // padding sorts after every key
-        if (i < a.nk) {
-            float v = 0.0f;
-            for (int h = 0; h < a.HK; ++h) v = __fadd_rn(v, __ldg(a.pooled + ((size_t)b * a.HK + h) * a.nk + i));
-            c = ((unsigned long long)float_key(v) << 32) | (0xffffffffu - (uint32_t)i);
-        }
-        sk[i] = c;
-    }
-    for (int w = tid; w < N / 32; w += kSortNT) bits[w] = 0u;
-    __syncthreads();
-    for (int k = 2; k <= N; k <<= 1) {
-        for (int j = k >> 1; j > 0; j >>= 1) {
-            for (int i = tid; i < N; i += kSortNT) {
-                const int l = i ^ j;
-                if (l > i) {
-                    const unsigned long long x = sk[i], y = sk[l];
-                    // ascending runs where (i & k) != 0, descending elsewhere; the last merge is descending
-                    if (((i & k) == 0) == (x < y)) {
-                        sk[i] = y;
-                        sk[l] = x;
-                    }
-                }
-            }
-            __syncthreads();
-        }
-    }
-    // the kept set: the first target_keep positions of the sorted order, as a bitmap of token indices
-    for (int p = tid; p < a.target_keep && p < a.nk; p += kSortNT) {
-        const uint32_t idx = 0xffffffffu - (uint32_t)(sk[p] & 0xffffffffull);
-        atomicOr(&bits[idx >> 5], 1u << (idx & 31));
-    }
-    __syncthreads();
-    // ascending token order: thread t owns bitmap words t*W .. t*W + W - 1
-    const int words = N / 32, W = (words + kSortNT - 1) / kSortNT;
-    int cnt = 0;
-    for (int w = tid * W; w < tid * W + W && w < words; ++w) cnt += __popc(bits[w]);
-    int total;
-    int pos = block_exclusive_scan(cnt, scan_tmp, &total);
-    for (int w = tid * W; w < tid * W + W && w < words; ++w) {
-        uint32_t m = bits[w];
-        while (m) {
-            const int t = __ffs(m) - 1;
-            kept[pos++] = w * 32 + t;
-            m &= m - 1;
-        }
-    }
-    for (int t = tid; t < a.obs_w; t += kSortNT) kept[a.target_keep + t] = a.nk + t;
-    if (tid == 0) a.n_kept[b] = a.target_keep + a.obs_w;
-}
-
 // The selection of long prefixes over several CTAs per item (one cooperative
 // launch, every CTA resident): each CTA holds a contiguous chunk of up to
 // kCoopNT * kSelPer keys in registers; the key range (min, max), the radix
@@ -844,17 +775,6 @@ int launch_evict_pool(const PoolArgs& in, int batch, cudaStream_t st) {
 }
 
 int launch_evict_select(const SelectArgs& a, int batch, cudaStream_t st) {
-    if (a.nk <= kSortMax && a.target_keep <= a.nk) {
-        int N = 32;
-        while (N < a.nk) N <<= 1;
-        const size_t smem = (size_t)N * 8 + (size_t)N / 8;
-        if (smem > 48 * 1024 &&
-            cudaFuncSetAttribute(evict_select_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-                cudaSuccess)
-            return RKV_ERR_CUDA;
-        evict_select_sort_kernel<<<batch, kSortNT, smem, st>>>(a, N);
-        return cudaGetLastError() == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
-    }
     if (a.nk <= kSelNT * kSelPer) {
         evict_select_reg_kernel<<<batch, kSelNT, 0, st>>>(a);
         return cudaGetLastError() == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;

@@ -984,7 +984,7 @@ __global__ void hsa_summary_mask_clear(uint8_t* summary, long long sum_stride, l
 // The extrema of one page (rows p C .. min(p C + C, Lc) - 1) over two 16-byte
 // chunks of the row: NaN-ignoring max of x and of -x, word by word, the first
 // row first -- the scan's operations in its sign-flipped domain.
-template <typename T, int RB>
+template <typename T, int RB, bool LONG>
 __device__ __forceinline__ void page_extrema(const uint8_t* Kh, int p, int C, int Lc, int ch, uint4 (&m)[2],
                                              uint4 (&n)[2]) {
     constexpr uint32_t FLIP = sizeof(T) == 2 ? 0x80008000u : 0x80000000u;
@@ -996,7 +996,23 @@ __device__ __forceinline__ void page_extrema(const uint8_t* Kh, int p, int C, in
         m[u] = __ldg(row + u);
         n[u] = make_uint4(m[u].x ^ fl.x, m[u].y ^ fl.y, m[u].z ^ fl.z, m[u].w ^ fl.w);
     }
-    for (int r = r0 + 1; r < r1; ++r) {
+    int r = r0 + 1;
+    for (; LONG && r + 2 <= r1; r += 2) {  // long pages: two rows' loads in flight, folded in row order
+        uint4 v[2][2];
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+#pragma unroll
+            for (int u = 0; u < 2; ++u) v[q][u] = __ldg(row + (q + 1) * (RB / 16) + u);
+        row += 2 * (RB / 16);
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                m[u] = max4<T>(m[u], v[q][u]);
+                n[u] = max4<T>(n[u], make_uint4(v[q][u].x ^ fl.x, v[q][u].y ^ fl.y, v[q][u].z ^ fl.z, v[q][u].w ^ fl.w));
+            }
+    }
+    for (; r < r1; ++r) {
         row += RB / 16;
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
@@ -1034,8 +1050,8 @@ __device__ __forceinline__ uint32_t nonfinite_bits(uint32_t m, uint32_t n, int d
 // nchunks to npp (the row padding) are written as zeros.
 constexpr int kBuildPagesPerWarp = 64;
 
-template <typename T, int D>
-__global__ void __launch_bounds__(kSumBuildNT, sizeof(T) == 2 ? 4 : 3) hsa_summary_build_kernel(const uint8_t* K, long long kv_stride,
+template <typename T, int D, bool LONG>  // LONG: pages of four rows or more
+__global__ void __launch_bounds__(kSumBuildNT, sizeof(T) == 2 && !LONG ? 4 : 3) hsa_summary_build_kernel(const uint8_t* K, long long kv_stride,
                                                                          int len_k, int C, int Lc, int nchunks,
                                                                          int npp, uint8_t* summary,
                                                                          long long sum_stride, long long mask_off) {
@@ -1055,8 +1071,8 @@ __global__ void __launch_bounds__(kSumBuildNT, sizeof(T) == 2 ? 4 : 3) hsa_summa
     for (int ch = 0; ch < NCH; ch += 2) {
         uint32_t nf = 0u;  // non-finite flags of this chunk pair's dimensions (they share one mask word)
         uint4 ma[2] = {}, na[2] = {}, mb[2] = {}, nb[2] = {};
-        if (va) page_extrema<T, RB>(Kh, pa, C, Lc, ch, ma, na);
-        if (vb) page_extrema<T, RB>(Kh, pb, C, Lc, ch, mb, nb);
+        if (va) page_extrema<T, RB, LONG>(Kh, pa, C, Lc, ch, ma, na);
+        if (vb) page_extrema<T, RB, LONG>(Kh, pb, C, Lc, ch, mb, nb);
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
 #pragma unroll
@@ -1683,8 +1699,12 @@ static int build_t(const uint8_t* K, int HK, int len_k, long long kv_stride, con
     hsa_summary_mask_clear<<<batch, 128, 0, st>>>(summary, s.item_bytes, s.mask_off, HK * (D / 32));
     constexpr int pages_per_cta = (kSumBuildNT / 32) * kBuildPagesPerWarp;
     dim3 grid((s.npp + pages_per_cta - 1) / pages_per_cta, HK, batch);
-    hsa_summary_build_kernel<T, D><<<grid, kSumBuildNT, 0, st>>>(K, kv_stride, len_k, s.C, s.Lc, s.nchunks, s.npp,
-                                                                 summary, s.item_bytes, s.mask_off);
+    if (s.C >= 4)
+        hsa_summary_build_kernel<T, D, true><<<grid, kSumBuildNT, 0, st>>>(K, kv_stride, len_k, s.C, s.Lc, s.nchunks,
+                                                                           s.npp, summary, s.item_bytes, s.mask_off);
+    else
+        hsa_summary_build_kernel<T, D, false><<<grid, kSumBuildNT, 0, st>>>(K, kv_stride, len_k, s.C, s.Lc, s.nchunks,
+                                                                            s.npp, summary, s.item_bytes, s.mask_off);
     return cudaGetLastError() == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
 }
 
