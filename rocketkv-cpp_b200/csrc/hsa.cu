@@ -984,7 +984,7 @@ __global__ void hsa_summary_mask_clear(uint8_t* summary, long long sum_stride, l
 // The extrema of one page (rows p C .. min(p C + C, Lc) - 1) over two 16-byte
 // chunks of the row: NaN-ignoring max of x and of -x, word by word, the first
 // row first -- the scan's operations in its sign-flipped domain.
-template <typename T, int RB, bool LONG>
+template <typename T, int RB>
 __device__ __forceinline__ void page_extrema(const uint8_t* Kh, int p, int C, int Lc, int ch, uint4 (&m)[2],
                                              uint4 (&n)[2]) {
     constexpr uint32_t FLIP = sizeof(T) == 2 ? 0x80008000u : 0x80000000u;
@@ -996,23 +996,7 @@ __device__ __forceinline__ void page_extrema(const uint8_t* Kh, int p, int C, in
         m[u] = __ldg(row + u);
         n[u] = make_uint4(m[u].x ^ fl.x, m[u].y ^ fl.y, m[u].z ^ fl.z, m[u].w ^ fl.w);
     }
-    int r = r0 + 1;
-    for (; LONG && r + 2 <= r1; r += 2) {  // long pages: two rows' loads in flight, folded in row order
-        uint4 v[2][2];
-#pragma unroll
-        for (int q = 0; q < 2; ++q)
-#pragma unroll
-            for (int u = 0; u < 2; ++u) v[q][u] = __ldg(row + (q + 1) * (RB / 16) + u);
-        row += 2 * (RB / 16);
-#pragma unroll
-        for (int q = 0; q < 2; ++q)
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                m[u] = max4<T>(m[u], v[q][u]);
-                n[u] = max4<T>(n[u], make_uint4(v[q][u].x ^ fl.x, v[q][u].y ^ fl.y, v[q][u].z ^ fl.z, v[q][u].w ^ fl.w));
-            }
-    }
-    for (; r < r1; ++r) {
+    for (int r = r0 + 1; r < r1; ++r) {
         row += RB / 16;
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
@@ -1050,8 +1034,8 @@ __device__ __forceinline__ uint32_t nonfinite_bits(uint32_t m, uint32_t n, int d
 // nchunks to npp (the row padding) are written as zeros.
 constexpr int kBuildPagesPerWarp = 64;
 
-template <typename T, int D, bool LONG>  // LONG: pages of four rows or more
-__global__ void __launch_bounds__(kSumBuildNT, sizeof(T) == 2 && !LONG ? 4 : 3) hsa_summary_build_kernel(const uint8_t* K, long long kv_stride,
+template <typename T, int D>
+__global__ void __launch_bounds__(kSumBuildNT, sizeof(T) == 2 ? 4 : 3) hsa_summary_build_kernel(const uint8_t* K, long long kv_stride,
                                                                          int len_k, int C, int Lc, int nchunks,
                                                                          int npp, uint8_t* summary,
                                                                          long long sum_stride, long long mask_off) {
@@ -1071,8 +1055,8 @@ __global__ void __launch_bounds__(kSumBuildNT, sizeof(T) == 2 && !LONG ? 4 : 3) 
     for (int ch = 0; ch < NCH; ch += 2) {
         uint32_t nf = 0u;  // non-finite flags of this chunk pair's dimensions (they share one mask word)
         uint4 ma[2] = {}, na[2] = {}, mb[2] = {}, nb[2] = {};
-        if (va) page_extrema<T, RB, LONG>(Kh, pa, C, Lc, ch, ma, na);
-        if (vb) page_extrema<T, RB, LONG>(Kh, pb, C, Lc, ch, mb, nb);
+        if (va) page_extrema<T, RB>(Kh, pa, C, Lc, ch, ma, na);
+        if (vb) page_extrema<T, RB>(Kh, pb, C, Lc, ch, mb, nb);
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
 #pragma unroll
@@ -1101,6 +1085,81 @@ __global__ void __launch_bounds__(kSumBuildNT, sizeof(T) == 2 && !LONG ? 4 : 3) 
         if (lane == 0 && m) atomicOr(mask + (ch * WPC * DPW) / 32, m);
     }
 }
+
+// Long pages (four rows or more): one thread per (page, 32-bit word of the
+// row) reads the page's rows word by word, so consecutive threads read
+// consecutive words of a row (coalesced along the row), and the extrema pass
+// through a [2][D][TP] tile in shared memory to leave as 16-byte runs of a
+// dimension's pages.  Same values as hsa_summary_build_kernel.
+template <typename T, int D>
+__global__ void __launch_bounds__(kSumBuildNT) hsa_summary_build_rows_kernel(const uint8_t* K, long long kv_stride,
+                                                                         int len_k, int C, int Lc, int nchunks,
+                                                                         int npp, int TP, uint8_t* summary,
+                                                                         long long sum_stride, long long mask_off) {
+    constexpr int ES = (int)sizeof(T), RB = D * ES, W = RB / 4;  // 32-bit words per row
+    constexpr uint32_t FLIP = ES == 2 ? 0x80008000u : 0x80000000u;
+    extern __shared__ __align__(16) uint8_t smraw[];
+    __shared__ uint32_t nfm[D / 32];        // dimensions with an extremum of -inf or NaN on this tile
+    T* tile = reinterpret_cast<T*>(smraw);  // [2][D][TP]
+    const int pt = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+    if (threadIdx.x < D / 32) nfm[threadIdx.x] = 0u;
+    __syncthreads();
+    const int p0 = pt * TP;
+    const uint8_t* Kh = K + (size_t)b * kv_stride + (size_t)hk * len_k * RB;
+    for (int x = threadIdx.x; x < TP * W; x += kSumBuildNT) {
+        const int p = x / W, wd = x % W, page = p0 + p;
+        uint32_t m = 0u, n = 0u;
+        if (page < nchunks) {
+            const int r0 = page * C, r1 = min(r0 + C, Lc);
+            const uint32_t v0 = *reinterpret_cast<const uint32_t*>(Kh + (size_t)r0 * RB + 4 * wd);
+            m = v0;
+            n = v0 ^ FLIP;
+            for (int r = r0 + 1; r < r1; ++r) {
+                const uint32_t v = *reinterpret_cast<const uint32_t*>(Kh + (size_t)r * RB + 4 * wd);
+                m = Chunk<T>::wmax(m, v);
+                n = Chunk<T>::wmax(n, v ^ FLIP);
+            }
+        }
+        if (page < nchunks) {  // -inf or NaN: the scan clamps such a representative at -FLT_MAX
+            uint32_t bits = 0u;
+            if (ES == 2) {
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                    const uint32_t x = (m >> (16 * hf)) & 0xffffu, y = (n >> (16 * hf)) & 0xffffu;
+                    if ((x & 0x7fffu) > 0x7f80u || x == 0xff80u || (y & 0x7fffu) > 0x7f80u || y == 0xff80u)
+                        bits |= 1u << ((2 * wd + hf) & 31);
+                }
+            } else if ((m & 0x7fffffffu) > 0x7f800000u || m == 0xff800000u || (n & 0x7fffffffu) > 0x7f800000u ||
+                       n == 0xff800000u) {
+                bits = 1u << (wd & 31);
+            }
+            if (bits) atomicOr(&nfm[(ES == 2 ? 2 * wd : wd) >> 5], bits);
+        }
+        if (ES == 2) {
+            tile[(0 * D + 2 * wd) * TP + p] = (T)(m & 0xffffu);
+            tile[(0 * D + 2 * wd + 1) * TP + p] = (T)(m >> 16);
+            tile[(1 * D + 2 * wd) * TP + p] = (T)(n & 0xffffu);
+            tile[(1 * D + 2 * wd + 1) * TP + p] = (T)(n >> 16);
+        } else {
+            reinterpret_cast<uint32_t*>(tile)[(0 * D + wd) * TP + p] = m;
+            reinterpret_cast<uint32_t*>(tile)[(1 * D + wd) * TP + p] = n;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < D / 32 && nfm[threadIdx.x])
+        atomicOr(reinterpret_cast<uint32_t*>(summary + (size_t)b * sum_stride + mask_off) + hk * (D / 32) + threadIdx.x,
+                 nfm[threadIdx.x]);
+    // rows of TP pages out, 16 bytes at a time (npp and TP are multiples of 8 pages)
+    const int np = min(TP, npp - p0);
+    const int vpr = np * ES / 16;
+    uint8_t* Sb = summary + (size_t)b * sum_stride + (size_t)hk * 2 * D * npp * ES;
+    for (int x = threadIdx.x; x < 2 * D * vpr; x += kSumBuildNT) {
+        const int row = x / vpr, v = x % vpr;
+        *reinterpret_cast<uint4*>(Sb + ((size_t)row * npp + p0) * ES + 16 * v) =
+            *reinterpret_cast<const uint4*>(smraw + ((size_t)row * TP) * ES + 16 * v);
+    }
+}
+
 
 // Phases 0 and 1 from the page summaries.  A tile is TP pages, a column of
 // 32 PPL pages per warp: lane l scores PPL consecutive pages over every
@@ -1699,12 +1758,21 @@ static int build_t(const uint8_t* K, int HK, int len_k, long long kv_stride, con
     hsa_summary_mask_clear<<<batch, 128, 0, st>>>(summary, s.item_bytes, s.mask_off, HK * (D / 32));
     constexpr int pages_per_cta = (kSumBuildNT / 32) * kBuildPagesPerWarp;
     dim3 grid((s.npp + pages_per_cta - 1) / pages_per_cta, HK, batch);
-    if (s.C >= 4)
-        hsa_summary_build_kernel<T, D, true><<<grid, kSumBuildNT, 0, st>>>(K, kv_stride, len_k, s.C, s.Lc, s.nchunks,
-                                                                           s.npp, summary, s.item_bytes, s.mask_off);
-    else
-        hsa_summary_build_kernel<T, D, false><<<grid, kSumBuildNT, 0, st>>>(K, kv_stride, len_k, s.C, s.Lc, s.nchunks,
-                                                                            s.npp, summary, s.item_bytes, s.mask_off);
+    if (s.C >= 4) {  // long pages: coalesced row reads, extrema transposed through shared memory
+        const int rowb = D * (int)sizeof(T);
+        int TP = 16384 / rowb;
+        if (TP > 64) TP = 64;
+        if (TP < 8) TP = 8;
+        const size_t smem = (size_t)2 * D * TP * sizeof(T);
+        auto f = hsa_summary_build_rows_kernel<T, D>;
+        if (smem > 48 * 1024 && cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return RKV_ERR_CUDA;
+        f<<<dim3((s.npp + TP - 1) / TP, HK, batch), kSumBuildNT, smem, st>>>(K, kv_stride, len_k, s.C, s.Lc, s.nchunks,
+                                                                             s.npp, TP, summary, s.item_bytes, s.mask_off);
+    } else {
+        hsa_summary_build_kernel<T, D><<<grid, kSumBuildNT, 0, st>>>(K, kv_stride, len_k, s.C, s.Lc, s.nchunks, s.npp,
+                                                                     summary, s.item_bytes, s.mask_off);
+    }
     return cudaGetLastError() == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
 }
 
