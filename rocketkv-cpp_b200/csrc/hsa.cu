@@ -1162,31 +1162,33 @@ __global__ void __launch_bounds__(kSumBuildNT) hsa_summary_build_rows_kernel(con
 
 
 // Phases 0 and 1 from the page summaries.  A tile is TP pages, a column of
-// 32 PPL pages per warp: lane l scores PPL consecutive pages over every
-// selected dimension, so the list entries it reads (the dimension's row in
-// the tile and s q per head) are the same on every lane of the warp: one
-// broadcast load per entry, no padding, no shuffles.  The rows of a tile,
-// one bulk copy per selected dimension, are kept in the order the lists take
-// them and loaded in two halves (the blocks of quad lanes 0, 2 and of 1, 3),
-// each on its own mbarrier with bounded waits: one half of the next tile is in
-// flight while the other half of this one is scored; several CTAs per SM
-// overlap as well.  Per page and head the sum is hsa_scan_kernel's: per
-// 16-byte chunk an even and an odd fused multiply-add chain over the selected
-// dimensions (the unselected ones add exact zeros there, and a chain that
-// starts at +0 never reaches -0, so skipping them changes nothing), chunk
-// value even + odd; the chunks j, j + 4, ... of quad lane j added pairwise as
-// a balanced tree (kept here as a binary-counter stack), and the four lane
-// totals as (l0 + l2) + (l1 + l3); then the IEEE division by the head's
-// scale.  The representatives are clamped at -FLT_MAX, which is the scan's
-// result on every page (the clamp only changes a representative that makes a
-// page's sum non-finite, where the scan recomputes clamped).
+// 32 PPL pages per warp: lane l scores PPL consecutive pages.  Every
+// dimension has a fixed place ("position") in the order the sums take them:
+// for the quad lanes j = 0, 2, 1, 3 of the stateless scan, their chunks
+// j, j + 4, ..., and per chunk the even and then the odd dimensions.  The
+// position table in shared memory holds, per position, the byte offset of the
+// dimension's row in the tile and s q per head; the code walks the positions
+// as straight-line code (no lists, no loop-carried state), and the entry read
+// is the same on every lane of the warp (a broadcast).  Only the selected
+// dimensions' rows are loaded, one bulk copy each, in position order, in two
+// halves (the positions of quad lanes 0, 2 and of 1, 3), each on its own
+// mbarrier with bounded waits: one half of the next tile is in flight while
+// the other half of this one is scored; several CTAs per SM overlap as well.
+// An unselected position has q = +0 and reads a zero row, so it adds
+// fma(+0, +0, acc) = acc exactly (a chain that starts at +0 never reaches -0).
+// Per page and head the sum is therefore hsa_scan_kernel's: per 16-byte chunk
+// an even and an odd fused multiply-add chain over the selected dimensions,
+// chunk value even + odd; the chunks j, j + 4, ... of quad lane j added
+// pairwise as a balanced tree (kept here as a binary-counter stack), and the
+// four lane totals as (l0 + l2) + (l1 + l3); then the IEEE division by the
+// head's scale.  The representatives are clamped at -FLT_MAX, which is the
+// scan's result on every page (the clamp only changes a representative that
+// makes a page's sum non-finite, where the scan recomputes clamped).
 constexpr int kSumScanNT = 128;
 constexpr int kSumScanWarps = kSumScanNT / 32;
-constexpr int kSumTileBudget = 72704;  // tile bytes per CTA: three CTAs per SM with their static part
+constexpr int kSumScanCtas = 3;  // CTAs per SM the tile size is chosen for
 
 __host__ __device__ constexpr int sumscan_ppl(int maxg, int es, int d) { return maxg <= 4 && es * d <= 512 ? 4 : 2; }
-// phase-0 scratch at the start of the dynamic buffer (dead before the first tile lands)
-__host__ __device__ constexpr int sumscan_scratch(int maxg, int d) { return (maxg * d + 3 * d + maxg) * 4 + 2 * d; }
 template <int B>
 struct VecBytes;
 template <>
@@ -1196,76 +1198,74 @@ struct VecBytes<8> { using type = uint2; };
 template <>
 struct VecBytes<16> { using type = uint4; };
 
-// One half of a tile for one warp (the blocks of quad lanes 0, 2 for HALF 0, of 1, 3 for HALF 1): the lane's
-// PPL pages over the half's list entries; A = l0 + l2, B = l1 + l3.  CLAMP: representatives clamped at
+// dimension at position p, and position of dimension d (CD dimensions per 16-byte chunk, NSL chunks per quad
+// lane): p = ((jj NSL + i) 2 + parity) CD / 2 + u for the dimension (j + 4 i) CD + 2 u + parity, jj the rank
+// of quad lane j in the order 0, 2, 1, 3 (an involution: rank and lane map the same way)
+template <int CD, int NSL>
+__device__ __forceinline__ int sumscan_dim(int p) {
+    const int u = p % (CD / 2), par = (p / (CD / 2)) & 1, i = (p / CD) % NSL, jj = p / (CD * NSL);
+    const int j = jj == 1 ? 2 : jj == 2 ? 1 : jj;
+    return (j + 4 * i) * CD + 2 * u + par;
+}
+template <int CD, int NSL>
+__device__ __forceinline__ int sumscan_pos(int d) {
+    const int c = d / CD, x = d % CD, j = c & 3, i = c >> 2;
+    const int jj = j == 1 ? 2 : j == 2 ? 1 : j;
+    return ((jj * NSL + i) * 2 + (x & 1)) * (CD / 2) + (x >> 1);
+}
+
+// One half of a tile for one warp (the positions of quad lanes 0, 2 for HALF 0, of 1, 3 for HALF 1): the
+// lane's PPL pages over the half's positions; A = l0 + l2, B = l1 + l3.  CLAMP: representatives clamped at
 // -FLT_MAX (needed only where a selected dimension has an extremum of -inf or NaN somewhere in the unit).
 template <typename T, int D, int MAXG, bool CLAMP, int HALF>
-__device__ __forceinline__ void sumscan_score_half(const float* ent, const unsigned char* cnt, int e_first,
-                                                   const uint8_t* col,
+__device__ __forceinline__ void sumscan_score_half(const float4* qtab, const uint8_t* col,
                                                    float2 (&A)[MAXG][sumscan_ppl(MAXG, (int)sizeof(T), D) / 2],
                                                    float2 (&B)[MAXG][sumscan_ppl(MAXG, (int)sizeof(T), D) / 2]) {
     constexpr int ES = (int)sizeof(T);
-    constexpr int CD = 16 / ES, NCH = D / CD, NSL = NCH / 4;
+    constexpr int CD = 16 / ES, NCH = D / CD, NSL = NCH / 4, HCD = CD / 2;
     constexpr int TOP = NSL >= 16 ? 4 : NSL >= 8 ? 3 : NSL >= 4 ? 2 : 1;  // log2(NSL)
     constexpr int PPL = sumscan_ppl(MAXG, ES, D), PV = PPL / 2;
-    constexpr int QW = (MAXG + 1 + 3) / 4 * 4;
+    constexpr int NQ = (MAXG + 1 + 3) / 4;  // float4s per position
     using RowV = typename VecBytes<ES * PPL>::type;
-    const float4* ep = reinterpret_cast<const float4*>(ent + e_first * QW);
-    // the entry stream, prefetched: entry e and its extrema, entry e + 1 (reads past the half stay in
-    // the tile and are not used)
-    float4 Ec = ep[0];
-    RowV Dc = *reinterpret_cast<const RowV*>(col + __float_as_int(Ec.x));
-    float4 En = ep[QW / 4];
 #pragma unroll
     for (int jh = 0; jh < 2; ++jh) {
         const int jj = 2 * HALF + jh;
-        const int j = jj == 0 ? 0 : jj == 1 ? 2 : jj == 2 ? 1 : 3;  // quad lanes 0, 2, 1, 3
         float2 stk[TOP][MAXG][PV];
         float2 cur[MAXG][PV];
 #pragma unroll
         for (int i = 0; i < NSL; ++i) {
-            const int c = j + 4 * i;
             float2 acc[2][MAXG][PV];
 #pragma unroll
             for (int par = 0; par < 2; ++par) {
 #pragma unroll
-                for (int h = 0; h < MAXG; ++h)
+                for (int u = 0; u < HCD; ++u) {
+                    const int p = ((jj * NSL + i) * 2 + par) * HCD + u;
+                    float qh[4 * NQ];
 #pragma unroll
-                    for (int v = 0; v < PV; ++v) acc[par][h][v] = make_float2(0.0f, 0.0f);
-                const int n = cnt[2 * c + par];  // the same on every lane
-                for (int u = 0; u < n; ++u, ep += QW / 4) {
-                    const float4 En2 = ep[2 * (QW / 4)];                                         // e + 2
-                    const RowV Dn = *reinterpret_cast<const RowV*>(col + __float_as_int(En.x));  // e + 1
-                    const uint32_t* wv = reinterpret_cast<const uint32_t*>(&Dc);
+                    for (int k = 0; k < NQ; ++k) {
+                        const float4 e = qtab[p * NQ + k];
+                        qh[4 * k] = e.x;
+                        qh[4 * k + 1] = e.y;
+                        qh[4 * k + 2] = e.z;
+                        qh[4 * k + 3] = e.w;
+                    }
+                    const RowV X = *reinterpret_cast<const RowV*>(col + __float_as_int(qh[0]));
+                    const uint32_t* wv = reinterpret_cast<const uint32_t*>(&X);
                     float2 P[PV];
 #pragma unroll
                     for (int v = 0; v < PV; ++v) {
                         if (ES == 2)
-                            P[v] = make_float2(__uint_as_float(wv[v] << 16),
-                                               __uint_as_float(wv[v] & 0xffff0000u));
+                            P[v] = make_float2(__uint_as_float(wv[v] << 16), __uint_as_float(wv[v] & 0xffff0000u));
                         else
                             P[v] = make_float2(__uint_as_float(wv[2 * v]), __uint_as_float(wv[2 * v + 1]));
                         if (CLAMP) P[v] = make_float2(fmaxf(P[v].x, -FLT_MAX), fmaxf(P[v].y, -FLT_MAX));
                     }
-                    float qh[QW];
-                    qh[0] = Ec.y;
-                    qh[1] = Ec.z;
-                    qh[2] = Ec.w;
-#pragma unroll
-                    for (int uu = 1; uu < QW / 4; ++uu) {
-                        const float4 ex = ep[uu];
-                        qh[4 * uu - 1] = ex.x;
-                        qh[4 * uu] = ex.y;
-                        qh[4 * uu + 1] = ex.z;
-                        qh[4 * uu + 2] = ex.w;
-                    }
 #pragma unroll
                     for (int h = 0; h < MAXG; ++h)
 #pragma unroll
-                        for (int v = 0; v < PV; ++v) ffma2(acc[par][h][v], make_float2(qh[h], qh[h]), P[v]);
-                    Ec = En;
-                    Dc = Dn;
-                    En = En2;
+                        for (int v = 0; v < PV; ++v)
+                            acc[par][h][v] = __ffma2_rn(make_float2(qh[1 + h], qh[1 + h]), P[v],
+                                                        u == 0 ? make_float2(0.0f, 0.0f) : acc[par][h][v]);
                 }
             }
 #pragma unroll
@@ -1302,7 +1302,7 @@ __device__ __forceinline__ void sumscan_score_half(const float* ent, const unsig
 }
 
 template <typename T, int D, int MAXG>
-__global__ void __launch_bounds__(kSumScanNT, 3) hsa_sumscan_kernel(const HsaArgs a) {
+__global__ void __launch_bounds__(kSumScanNT, kSumScanCtas) hsa_sumscan_kernel(const HsaArgs a) {
     asm volatile("griddepcontrol.launch_dependents;");  // the selection may be scheduled (it waits for this grid)
     constexpr int ES = (int)sizeof(T);
     constexpr int CD = 16 / ES, NCH = D / CD, NSL = NCH / 4;
@@ -1310,25 +1310,15 @@ __global__ void __launch_bounds__(kSumScanNT, 3) hsa_sumscan_kernel(const HsaArg
     static_assert((1 << TOP) == NSL, "slots per quad lane: a power of two from 2 to 16");
     constexpr int PPL = sumscan_ppl(MAXG, ES, D), PV = PPL / 2;  // pages per lane, page pairs per lane
     constexpr int COLP = 32 * PPL;                         // pages per column: a warp's share of a tile
-    constexpr int QW = (MAXG + 1 + 3) / 4 * 4;             // floats per list entry
+    constexpr int NQ = (MAXG + 1 + 3) / 4;                 // float4s per position
+    constexpr int NPW = D / 32;                            // 32-position words
     constexpr int DPT = (D + kSumScanNT - 1) / kSumScanNT;  // dimensions per thread in phase 0
-    using RowV = typename VecBytes<ES * PPL>::type;         // a lane's extrema of one dimension
-    extern __shared__ __align__(128) uint8_t sbuf[];        // [nr][TP] extrema, list order (phase-0 scratch first)
-    __shared__ __align__(16) float ent[(D + 2) * QW];       // the lists, in processing order, + 2 blank
-    __shared__ unsigned short esrow[D];                     // summary row of entry e: s D + d
-    __shared__ unsigned char cnt[2 * NCH];                  // list lengths, [chunk][parity]
-    __shared__ int ejs[5];                                  // first entry of each block
-    __shared__ uint32_t selw[D / 32];
+    static_assert(NPW % 2 == 0 && NPW <= 32, "D from 64 to 1024");
+    extern __shared__ __align__(128) uint8_t sbuf[];  // [nr][TP] extrema in position order, then a zero row
+    __shared__ __align__(16) float4 qtab[D * NQ];     // per position: row offset, s q per head (sum |q| first)
+    __shared__ uint32_t selw[NPW], negw[NPW];         // selected dimensions, sign-flipped dimensions
     __shared__ float cscale[MAXG];
-    __shared__ int scan_tmp[33];
     __shared__ uint64_t full[2];
-    float* qf = reinterpret_cast<float*>(sbuf);  // [G][D]
-    float* sabs = qf + MAXG * D;
-    float* qsum = sabs + D;
-    int* Rl = reinterpret_cast<int*>(qsum + D);
-    float* sumall = reinterpret_cast<float*>(Rl + D);
-    unsigned char* dsel = reinterpret_cast<unsigned char*>(sumall + MAXG);
-    unsigned char* dneg = dsel + D;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int split = blockIdx.x, hc = blockIdx.y, b = blockIdx.z, hk = a.head_begin + hc;
@@ -1336,42 +1326,42 @@ __global__ void __launch_bounds__(kSumScanNT, 3) hsa_sumscan_kernel(const HsaArg
     const int p_beg = split * a.pages_per_split;
     const int p_end = min(a.nchunks, p_beg + a.pages_per_split);
     if (p_beg >= p_end) return;  // uniform
-    const uint8_t* Qg = a.Q + (size_t)b * a.q_stride + (size_t)hk * G * D * sizeof(T);
+    const T* Qg = reinterpret_cast<const T*>(a.Q + (size_t)b * a.q_stride + (size_t)hk * G * D * sizeof(T));
     float* wl = a.wlogits + ((size_t)b * a.head_count + hc) * (size_t)G * a.nch_pad;
-    for (int e = tid; e < G * D; e += kSumScanNT) qf[e] = to_f<T>(reinterpret_cast<const T*>(Qg)[e]);
-    __syncthreads();
+    const uint8_t* summ = a.summary + (size_t)b * a.sum_stride;
+    const uint32_t nfw = tid < NPW ? reinterpret_cast<const uint32_t*>(summ + a.sum_mask_off)[hk * NPW + tid] : 0u;
+    if (tid == 0) {
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
+        fence_mbar_init();
+    }
     // ---- phase 0: group query statistics (rocket.cpp:197-250), as hsa_scan_kernel ----
-    for (int d = tid; d < D; d += kSumScanNT) {
+    float* sabs = reinterpret_cast<float*>(qtab);  // sum over the heads of |q| per dimension (dead after the rank)
+    float qv[DPT][MAXG];
+    bool negd[DPT];
+#pragma unroll
+    for (int k = 0; k < DPT; ++k) {
+        const int d = tid + k * kSumScanNT;
         float sa = 0.0f, sv = 0.0f;
-        for (int h = 0; h < G; ++h) {
-            const float q = qf[h * D + d];
-            sa = __fadd_rn(sa, fabsf(q));
-            sv = __fadd_rn(sv, q);
-        }
-        sabs[d] = sa;
-        qsum[d] = sv;
-    }
-    if (lane == 0 && warp < G) {
-        for (int h = warp; h < G; h += kSumScanNT / 32) {
-            const float4* q4 = reinterpret_cast<const float4*>(qf + h * D);
-            float s = 0.0f;
-#pragma unroll 8
-            for (int v = 0; v < D / 4; ++v) {
-                const float4 x = q4[v];
-                s = __fadd_rn(s, fabsf(x.x));
-                s = __fadd_rn(s, fabsf(x.y));
-                s = __fadd_rn(s, fabsf(x.z));
-                s = __fadd_rn(s, fabsf(x.w));
+#pragma unroll
+        for (int h = 0; h < MAXG; ++h) {
+            qv[k][h] = 0.0f;
+            if (h < G && d < D) {
+                const float q = to_f<T>(Qg[h * D + d]);
+                qv[k][h] = q;
+                sa = __fadd_rn(sa, fabsf(q));
+                sv = __fadd_rn(sv, q);
             }
-            sumall[h] = s;
         }
+        if (d < D) sabs[d] = sa;
+        negd[k] = !(sv >= 0.0f);  // rocket.cpp:263: sign >= 0 takes the max
     }
     __syncthreads();
-    // top r by (sum |q| desc, dimension asc); thread t owns dimensions t DPT .. t DPT + DPT - 1
-    int myflags = 0, nmine = 0;
+    // top r by (sum |q| desc, dimension asc)
 #pragma unroll
-    for (int u = 0; u < DPT; ++u) {
-        const int d = tid * DPT + u;
+    for (int k = 0; k < DPT; ++k) {
+        const int d = tid + k * kSumScanNT;
+        bool s = false;
         if (d < D) {
             int rank = 0;
             const float me = sabs[d];
@@ -1380,103 +1370,107 @@ __global__ void __launch_bounds__(kSumScanNT, 3) hsa_sumscan_kernel(const HsaArg
                 const float o = sabs[e];
                 rank += (o > me || (o == me && e < d)) ? 1 : 0;
             }
-            const int f = (a.r >= D || rank < a.r) ? 1 : 0;
-            myflags |= f << u;
-            nmine += f;
-            dsel[d] = (unsigned char)f;
-            dneg[d] = !(qsum[d] >= 0.0f) ? 1 : 0;  // rocket.cpp:263: sign >= 0 takes the max
+            s = a.r >= D || rank < a.r;
+        }
+        const uint32_t bs = __ballot_sync(0xffffffffu, s), bn = __ballot_sync(0xffffffffu, negd[k] && d < D);
+        if (lane == 0 && warp + k * kSumScanWarps < NPW) {
+            selw[warp + k * kSumScanWarps] = bs;
+            negw[warp + k * kSumScanWarps] = bn;
         }
     }
-    int nr;
-    int pos = block_exclusive_scan(nmine, scan_tmp, &nr);
+    __syncthreads();  // masks ready; sabs dead
+    // every warp: which positions are selected, and the running counts, so a selected position's row
+    // (its entry) is known everywhere without another barrier
+    uint32_t pb[NPW];
+    int pbase[NPW + 1];
+    pbase[0] = 0;
 #pragma unroll
-    for (int u = 0; u < DPT; ++u)
-        if ((myflags >> u) & 1) Rl[pos++] = tid * DPT + u;  // the selected dimensions, ascending
-    __syncthreads();
-    if (tid < G) {
-        float sk;
-        if (a.r >= D) {
-            sk = sumall[tid];
-        } else {
-            sk = 0.0f;
-            for (int i = 0; i < nr; ++i) sk = __fadd_rn(sk, fabsf(qf[tid * D + Rl[i]]));
-        }
-        cscale[tid] = __fsqrt_rn(__fmul_rn((float)D, __fdiv_rn(sk, __fadd_rn(sumall[tid], 1e-9f))));
+    for (int k = 0; k < NPW; ++k) {
+        const int d = sumscan_dim<CD, NSL>(32 * k + lane);
+        pb[k] = __ballot_sync(0xffffffffu, (selw[d >> 5] >> (d & 31)) & 1u);
+        pbase[k + 1] = pbase[k] + __popc(pb[k]);
     }
-    int nf = 0;  // a selected dimension with an extremum of -inf or NaN somewhere in the unit: clamp
-    if (tid < D / 32) {
-        uint32_t m = 0;
-        for (int e = 0; e < 32; ++e) m |= (uint32_t)dsel[tid * 32 + e] << e;
-        selw[tid] = m;
-        const uint32_t* nfm = reinterpret_cast<const uint32_t*>(a.summary + (size_t)b * a.sum_stride + a.sum_mask_off);
-        nf = (nfm[hk * (D / 32) + tid] & m) != 0u;
-    }
-    for (int x = tid; x < 2 * NCH; x += kSumScanNT) {  // list lengths: selected dimensions of a chunk and parity
-        const int c = x >> 1, par = x & 1;
-        int n = 0;
-        for (int e = par; e < CD; e += 2) n += dsel[c * CD + e];
-        cnt[x] = (unsigned char)n;
-    }
-    __syncthreads();
-    if (tid < 4) {  // block tid (quad lane 0, 2, 1, 3 for tid 0, 1, 2, 3): its first entry
-        int e = 0;
-        for (int c2 = 0; c2 < NCH; ++c2) {
-            const int j2 = c2 & 3, r2 = j2 == 0 ? 0 : j2 == 2 ? 1 : j2 == 1 ? 2 : 3;
-            if (r2 < tid) e += cnt[2 * c2] + cnt[2 * c2 + 1];
-        }
-        ejs[tid] = e;
-        if (tid == 0) ejs[4] = nr;
-    }
-    if (tid < NCH) {  // chunk tid: its entries at their place in the processing order
-        const int c = tid, jc = c & 3, ic = c >> 2;
-        const int jrank = jc == 0 ? 0 : jc == 2 ? 1 : jc == 1 ? 2 : 3;
-        int e = 0;
-        for (int c2 = 0; c2 < NCH; ++c2) {
-            const int j2 = c2 & 3, r2 = j2 == 0 ? 0 : j2 == 2 ? 1 : j2 == 1 ? 2 : 3;
-            if (r2 < jrank || (r2 == jrank && (c2 >> 2) < ic)) e += cnt[2 * c2] + cnt[2 * c2 + 1];
-        }
-        int e_odd = e + cnt[2 * c];
-        for (int x = 0; x < CD; ++x) {
-            const int d = c * CD + x;
-            if (!dsel[d]) continue;
-            const int en_i = (x & 1) ? e_odd++ : e++;
-            float* en = ent + en_i * QW;
-            en[0] = __int_as_float(en_i * a.stage_rows * ES);  // byte offset of the row in the tile
-            for (int h = 0; h < QW - 1; ++h) {
-                const float q = h < G ? qf[h * D + d] : 0.0f;
-                en[1 + h] = dneg[d] ? -q : q;
-            }
-            esrow[en_i] = (unsigned short)(dneg[d] * D + d);
-        }
-    }
-    for (int x = tid; x < 2 * QW; x += kSumScanNT) ent[nr * QW + x] = 0.0f;  // blank entries for the prefetch
-    if (tid < 2) mbar_init(&full[tid], 1);
-    fence_mbar_init();
-    fence_proxy_async();  // the scratch's generic writes ordered before the tiles' async copies
-    const bool need_clamp = __syncthreads_or(nf) != 0;
-
-    // ---- phase 1: page logits from the summaries ----
-    // Tiles of TP pages; the rows of a tile are loaded in two halves (blocks 0-1 and 2-3), each on its own
-    // mbarrier, so that one half of the next tile is in flight while the other half of this one is scored.
-    const uint8_t* Sb = a.summary + (size_t)b * a.sum_stride + (size_t)hk * 2 * D * a.npp * ES;
+    const int nr = pbase[NPW], eh = pbase[NPW / 2];  // selected rows; rows of the first half
     const int TP = a.stage_rows;
+    const int rowb = TP * ES;
+    const uint8_t* Sb = summ + (size_t)hk * 2 * D * a.npp * ES;
     const int ntile = (p_end - p_beg + TP - 1) / TP;
-    const int wp0 = warp * COLP, lp = wp0 + lane * PPL;  // the warp's and the lane's first page in a tile
-    const int eh = ejs[2];                                // entries of the first half
-    auto issue = [&](int t, int half) {                   // warp 0: the copies of one half of tile t
+    auto issue = [&](int t, int half) {  // warp 0: the copies of one half of tile t
         const int tp0 = p_beg + t * TP;
         const int np = min(TP, a.npp - tp0);  // whole 8-page groups: bytes a multiple of 16
-        const int e0 = half ? eh : 0, e1 = half ? nr : eh;
-        if (lane == 0) mbar_arrive_expect_tx(&full[half], (uint32_t)((size_t)(e1 - e0) * np * ES));
+        if (lane == 0) mbar_arrive_expect_tx(&full[half], (uint32_t)((size_t)(half ? nr - eh : eh) * np * ES));
         __syncwarp();
-        for (int e = e0 + lane; e < e1; e += 32)
-            bulk_load(sbuf + (size_t)e * TP * ES, Sb + ((size_t)esrow[e] * a.npp + tp0) * ES, (uint32_t)(np * ES),
-                      &full[half]);
+#pragma unroll
+        for (int k = half * (NPW / 2); k < (half + 1) * (NPW / 2); ++k) {
+            if ((pb[k] >> lane) & 1u) {
+                const int d = sumscan_dim<CD, NSL>(32 * k + lane);
+                const int e = pbase[k] + __popc(pb[k] & ((1u << lane) - 1u));
+                const int row = (int)((negw[d >> 5] >> (d & 31)) & 1u) * D + d;
+                bulk_load(sbuf + (size_t)e * rowb, Sb + ((size_t)row * a.npp + tp0) * ES, (uint32_t)(np * ES),
+                          &full[half]);
+            }
+        }
     };
     if (warp == 0) {
         issue(0, 0);
         issue(0, 1);
     }
+    // the position table: this thread's dimensions
+#pragma unroll
+    for (int k = 0; k < DPT; ++k) {
+        const int d = tid + k * kSumScanNT;
+        if (d < D) {
+            const int p = sumscan_pos<CD, NSL>(d), w = p >> 5, l = p & 31;
+            uint32_t bw = 0;
+            int base = 0;
+#pragma unroll
+            for (int x = 0; x < NPW; ++x)
+                if (x == w) {
+                    bw = pb[x];
+                    base = pbase[x];
+                }
+            const bool s = (bw >> l) & 1u;
+            const int off = (s ? base + __popc(bw & ((1u << l) - 1u)) : nr) * rowb;
+            float e[4 * NQ];
+            e[0] = __int_as_float(off);
+#pragma unroll
+            for (int h = 0; h < 4 * NQ - 1; ++h) {
+                const float q = (s && h < MAXG) ? qv[k][h] : 0.0f;
+                e[1 + h] = negd[k] ? -q : q;
+            }
+            if (!s) {
+#pragma unroll
+                for (int h = 1; h < 4 * NQ; ++h) e[h] = 0.0f;  // +0: adds exactly nothing
+            }
+#pragma unroll
+            for (int x = 0; x < NQ; ++x) qtab[p * NQ + x] = make_float4(e[4 * x], e[4 * x + 1], e[4 * x + 2], e[4 * x + 3]);
+        }
+    }
+    // per-head scales (rocket.cpp:240-250): sum over all dimensions and over the selected ones, ascending
+    if (warp == (kSumScanWarps > 1 ? 1 : 0) && lane < G) {
+        const T* qh = Qg + lane * D;
+        float s_all = 0.0f, s_sel = 0.0f;
+#pragma unroll
+        for (int x = 0; x < NPW; ++x) {
+            const uint32_t m = selw[x];
+#pragma unroll
+            for (int y = 0; y < 32; ++y) {
+                const float q = fabsf(to_f<T>(qh[32 * x + y]));
+                s_all = __fadd_rn(s_all, q);
+                if ((m >> y) & 1u) s_sel = __fadd_rn(s_sel, q);
+            }
+        }
+        const float sk = a.r >= D ? s_all : s_sel;
+        cscale[lane] = __fsqrt_rn(__fmul_rn((float)D, __fdiv_rn(sk, __fadd_rn(s_all, 1e-9f))));
+    }
+    // the zero row the unselected positions read
+    for (int x = tid; x < rowb / 16; x += kSumScanNT)
+        *reinterpret_cast<uint4*>(sbuf + (size_t)nr * rowb + 16 * x) = make_uint4(0u, 0u, 0u, 0u);
+    // a selected dimension with an extremum of -inf or NaN somewhere in the unit: clamp
+    const bool need_clamp = __syncthreads_or(tid < NPW && (nfw & selw[tid]) != 0u) != 0;
+
+    // ---- phase 1: page logits from the summaries ----
+    const int wp0 = warp * COLP, lp = wp0 + lane * PPL;  // the warp's and the lane's first page in a tile
     float rscale[MAXG];
 #pragma unroll
     for (int h = 0; h < MAXG; ++h) rscale[h] = h < G ? cscale[h] : 1.0f;
@@ -1497,17 +1491,16 @@ __global__ void __launch_bounds__(kSumScanNT, 3) hsa_sumscan_kernel(const HsaArg
                 return;
             }
             if (active) {
-                const int ef = ejs[2 * half];
                 if (half == 0) {
                     if (need_clamp)
-                        sumscan_score_half<T, D, MAXG, true, 0>(ent, cnt, ef, col, A, B);
+                        sumscan_score_half<T, D, MAXG, true, 0>(qtab, col, A, B);
                     else
-                        sumscan_score_half<T, D, MAXG, false, 0>(ent, cnt, ef, col, A, B);
+                        sumscan_score_half<T, D, MAXG, false, 0>(qtab, col, A, B);
                 } else {
                     if (need_clamp)
-                        sumscan_score_half<T, D, MAXG, true, 1>(ent, cnt, ef, col, A, B);
+                        sumscan_score_half<T, D, MAXG, true, 1>(qtab, col, A, B);
                     else
-                        sumscan_score_half<T, D, MAXG, false, 1>(ent, cnt, ef, col, A, B);
+                        sumscan_score_half<T, D, MAXG, false, 1>(qtab, col, A, B);
                 }
             }
             __syncthreads();  // the half's rows are free for the next tile
@@ -1553,26 +1546,33 @@ template <typename T, int D, int MAXG>
 int launch_t(HsaArgs a, int batch, cudaStream_t st) {
     if (a.nchunks > 0 && a.summary) {
         // page logits from the summaries.  Tile: whole columns of 32 PPL pages (a warp each), as many as
-        // the budget holds for the r selected rows (three CTAs per SM)
+        // kSumScanCtas CTAs per SM hold for the r selected rows and the zero row
         constexpr int PPL = sumscan_ppl(MAXG, (int)sizeof(T), D), COLP = 32 * PPL;
+        auto fs = hsa_sumscan_kernel<T, D, MAXG>;
+        cudaFuncAttributes fa;
+        if (cudaFuncGetAttributes(&fa, fs) != cudaSuccess) return RKV_ERR_CUDA;
+        int dev = 0, sm_smem = 0, reserved = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&sm_smem, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) != cudaSuccess)
+            return RKV_ERR_CUDA;
+        const long long per_cta = (long long)sm_smem / kSumScanCtas - reserved - (long long)fa.sharedSizeBytes;
         const int nr = a.r < D ? a.r : D;
-        const size_t run_b = (size_t)nr * sizeof(T);  // bytes per tile page
-        int tp = (int)(kSumTileBudget / run_b) / COLP * COLP;
+        const size_t run_b = (size_t)(nr + 1) * sizeof(T);  // bytes per tile page
+        int tp = per_cta > 0 ? (int)((size_t)per_cta / run_b) / COLP * COLP : 0;
         if (tp > kSumScanWarps * COLP) tp = kSumScanWarps * COLP;
         if (tp < COLP) tp = COLP;
         a.stage_rows = tp;
         // enough CTAs to cover the GPU
         const long long units = (long long)batch * a.head_count;
-        const long long want = 3LL * num_sms();
+        const long long want = (long long)kSumScanCtas * num_sms();
         int splits = units >= want ? 1 : (int)((want + units - 1) / units);
         const int max_splits = (a.nchunks + tp - 1) / tp;
         if (splits > max_splits) splits = max_splits;
         if (splits < 1) splits = 1;
         a.pages_per_split = ((a.nchunks + splits - 1) / splits + tp - 1) / tp * tp;  // whole tiles
         a.splits = (a.nchunks + a.pages_per_split - 1) / a.pages_per_split;
-        const size_t tile = run_b * tp, scratch = (size_t)sumscan_scratch(MAXG, D);
-        const size_t smem = tile > scratch ? tile : scratch;
-        auto fs = hsa_sumscan_kernel<T, D, MAXG>;
+        const size_t smem = run_b * tp;
         if (cudaFuncSetAttribute(fs, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
             return RKV_ERR_CUDA;
         if (cudaFuncSetAttribute(fs, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
