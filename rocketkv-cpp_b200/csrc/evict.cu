@@ -32,6 +32,7 @@ constexpr int kPoolKT = 256;  // positions per pooling CTA
 constexpr int kSelNT = 1024;  // threads of the selection CTA
 
 __global__ void __launch_bounds__(kNT) evict_logits_kernel(EvictArgs a) {
+    asm volatile("griddepcontrol.launch_dependents;");
     extern __shared__ __align__(16) float sm[];
     const int DP = a.D + 4;
     float* Ks = sm;              // [kKT][DP]
@@ -153,6 +154,8 @@ __global__ void __launch_bounds__(kNT) evict_logits_kernel(EvictArgs a) {
 // its +-pad halo, then the clipped window max.  The cross-head sum happens in
 // the select kernel, in head order.
 __global__ void __launch_bounds__(kNT) evict_pool_kernel(PoolArgs a) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a dependent of the scorer
+    asm volatile("griddepcontrol.launch_dependents;");  // the selection may be scheduled (it waits)
     extern __shared__ __align__(16) float sm[];
     const int pe = a.pad_eff;
     const int NA = kPoolKT + 2 * pe;
@@ -338,6 +341,7 @@ __global__ void __launch_bounds__(kSelNT) evict_select_kernel(SelectArgs a) {
 // threshold keys kept)).
 constexpr int kSelPer = 16;
 __global__ void __launch_bounds__(kSelNT) evict_select_reg_kernel(SelectArgs a) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a dependent of the pooling
     asm volatile("griddepcontrol.launch_dependents;");  // a dependent compaction may start (it waits)
     __shared__ int hist[256];
     __shared__ int scan_tmp[66];
@@ -770,14 +774,20 @@ int launch_evict_pool(const PoolArgs& in, int batch, cudaStream_t st) {
     if (pool_smem(a.pad_eff, a.R, &smem) != RKV_OK) return RKV_ERR_UNSUPPORTED;
     if (set_smem_attr((const void*)evict_pool_kernel, smem) != RKV_OK) return RKV_ERR_CUDA;
     dim3 grid((a.nk + kPoolKT - 1) / kPoolKT, a.head_count, batch);
-    evict_pool_kernel<<<grid, kNT, smem, st>>>(a);
-    return cudaGetLastError() == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
+    if (launch_pdl(evict_pool_kernel, grid, dim3(kNT), smem, st, a) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return RKV_ERR_CUDA;
+    }
+    return RKV_OK;
 }
 
 int launch_evict_select(const SelectArgs& a, int batch, cudaStream_t st) {
     if (a.nk <= kSelNT * kSelPer) {
-        evict_select_reg_kernel<<<batch, kSelNT, 0, st>>>(a);
-        return cudaGetLastError() == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
+        if (launch_pdl(evict_select_reg_kernel, dim3(batch), dim3(kSelNT), 0, st, a) != cudaSuccess) {
+            (void)cudaGetLastError();
+            return RKV_ERR_CUDA;
+        }
+        return RKV_OK;
     }
     // long prefixes: several CTAs per item in one cooperative launch, bookkeeping in the keys region
     SelCoop c{};

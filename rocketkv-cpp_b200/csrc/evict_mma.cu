@@ -58,6 +58,7 @@ __host__ __device__ inline MmaLayout mma_layout(int R, int D, int es, int mode) 
 
 template <typename T, int MODE>
 __global__ void __launch_bounds__(kMmaNT) evict_mma_kernel(const EvictArgs a) {
+    asm volatile("griddepcontrol.launch_dependents;");
     constexpr int ES = (int)sizeof(T);
     constexpr bool TF32 = ES == 4;
     extern __shared__ __align__(128) uint8_t sm[];
@@ -252,6 +253,7 @@ __global__ void __launch_bounds__(kMmaNT) evict_mma_kernel(const EvictArgs a) {
 // then sum_t s_t * exp(m_t - M_r).
 constexpr int kFoldRows = 8;  // rows (warps) per CTA
 __global__ void __launch_bounds__(kFoldRows * 32) evict_fold_kernel(const EvictArgs a) {
+    asm volatile("griddepcontrol.launch_dependents;");
     const int lane = threadIdx.x & 31;
     const int r = blockIdx.x * kFoldRows + (threadIdx.x >> 5), hc = blockIdx.y, b = blockIdx.z;
     if (r >= a.R) return;  // warp-uniform

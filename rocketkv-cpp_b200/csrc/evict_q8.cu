@@ -238,6 +238,7 @@ struct Visit {
 };
 
 __global__ void __launch_bounds__(kQ8Threads, 1) evict_q8_kernel(const EvictArgs a, const Q8Plan P) {
+    asm volatile("griddepcontrol.launch_dependents;");  // the pooling may be scheduled (it waits for this grid)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const Q8Bars B = q8_bars(sm);

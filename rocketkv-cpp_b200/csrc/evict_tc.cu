@@ -203,6 +203,7 @@ template <int KIND>
 __global__ void __launch_bounds__(kTcThreads, 1)
     evict_tc_kernel(const EvictArgs a, const TcPlan P, const __grid_constant__ CUtensorMap tmk,
                     const __grid_constant__ CUtensorMap tmq) {
+    asm volatile("griddepcontrol.launch_dependents;");  // the pooling may be scheduled (it waits for this grid)
     constexpr bool TF32 = KIND != KIND_BF16;
     constexpr bool TMA = KIND != KIND_Q8;
     constexpr int EB = KIND == KIND_BF16 ? 2 : 4;

@@ -297,4 +297,24 @@ __device__ __forceinline__ int block_exclusive_scan2(int a, int b, int* tmp, int
     return before_a;
 }
 
+// Launch as a programmatic dependent of the kernel before it on the stream: the
+// launch is processed while that kernel runs, and the kernel waits for its
+// results with griddepcontrol.wait (a no-op in a kernel launched without the
+// attribute).  After a non-kernel operation the stream orders as usual.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*f)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t lc{};
+    lc.gridDim = grid;
+    lc.blockDim = block;
+    lc.dynamicSmemBytes = smem;
+    lc.stream = st;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    return cudaLaunchKernelEx(&lc, f, args...);
+}
+
 }  // namespace rkv
