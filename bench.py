@@ -736,7 +736,7 @@ def time_config1(device, reps, warmup):
     return out
 
 
-def long_context(device, world, rank, steps, warmup, gpu_index):
+def long_context(device, world, rank, steps, warmup, gpu_index, seqs=8):
     """The long-context configuration: 8 sequences at S = 131072, K/V/Q bf16
     N(0,1) with 0.5 % of K rows x8, sharded by KV head over the ranks (one
     head per GPU at 8 GPUs).  Stage 1 at budget 4096 (window 32, kernel 63):
@@ -750,7 +750,7 @@ def long_context(device, world, rank, steps, warmup, gpu_index):
     import torch
     import rocketkv_b200 as rkv
     import sharded
-    B, S, budget, layers = 8, 131072, 4096, 28
+    B, S, budget, layers = seqs, 131072, 4096, 28
     G = H // HK
     h0, nh = sharded.head_range(HK, world, rank)
     st = torch.cuda.current_stream()
@@ -837,7 +837,7 @@ def long_context(device, world, rank, steps, warmup, gpu_index):
               "clocks": cs.summary()}
     del gc
     torch.cuda.empty_cache()
-    return {"workload": "8 sequences x S 131072 bf16 (0.5% K rows x8), KV heads sharded over the ranks "
+    return {"workload": f"{B} sequences x S 131072 bf16 (0.5% K rows x8), KV heads sharded over the ranks "
                         f"({nh} per rank); stage 1 budget 4096 w32 ks63; {steps} decode steps x 28 layers on the "
                         "4096-row caches (page 16, r 32, top-k 256, window growing by one token per step)",
             "heads_per_rank": nh, "eviction": eviction, "decode": decode}
@@ -855,7 +855,7 @@ def main():
                     help="sequences per GPU (smaller values are profiling cases, not the benchmark)")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layers per step (smaller values are profiling cases, not the benchmark)")
-    ap.add_argument("--only", default=None, choices=["q8_eviction", "fp32_eviction", "config1", "summary_build"],
+    ap.add_argument("--only", default=None, choices=["q8_eviction", "fp32_eviction", "config1", "summary_build", "long_context"],
                     help="run one bench item alone and print its result (profiling case, not the benchmark line)")
     args = ap.parse_args()
     set_workload(args.seqs, args.layers)
@@ -869,6 +869,8 @@ def main():
             out = dict(zip(("ms_per_layer", "e2e_ms_per_layer", "kernels"), time_evict(device, args.steps, args.warmup)))
         elif args.only == "config1":
             out = time_config1(device, args.steps, args.warmup)
+        elif args.only == "long_context":
+            out = long_context(device, 1, 0, args.steps, args.warmup, 0, seqs=min(args.seqs, 8))
         else:
             out = time_summary_build(device, args.steps, args.warmup)
         print(json.dumps({"only": args.only, "result": out}))

@@ -39,13 +39,17 @@
 // Two passes over the CTA's tiles (rocket.cpp:91-116): pass 0 writes the
 // per-(row, tile) max and sum of exp(l - max) of l = (q . k) / sqrt(D); the
 // epilogue then folds a head's tile statistics into the row max M_r and
-// inv_r = 1 / (sum_r + 1e-9) (rocket.cpp:108-113), and pass 1 computes the
-// logits again and writes the head score of every key,
-// sum_r exp(l - M_r) * inv_r, for the pooling kernel.  Both passes run in one
-// cooperative launch when every CTA can be resident: a bounded grid barrier
-// holds only the epilogue between the passes while the copies and MMAs of
-// pass 1 already run (one layer's fp32 K, 33.5 MB, is read again from L2);
-// otherwise one launch per pass.
+// inv_r = 1 / (sum_r + 1e-9) (rocket.cpp:108-113), and pass 1 writes the head
+// score of every key, sum_r exp(l - M_r) * inv_r, for the pooling kernel.
+// Pass 1 has two forms.  While they fit in L2, pass 0 keeps every
+// exp(l - quarter max) and pass 1 streams them once (one exp per (row, tile,
+// quarter) rescales them).  For long prefixes, whose kept values would be
+// written to and read back from HBM, pass 1 instead runs the copies and MMAs
+// again over the tiles in reverse order (the first ones are still in L2) and
+// forms each key's score from the logits in tensor memory.  Both passes run
+// in one cooperative launch when every CTA can be resident: a bounded grid
+// barrier between them holds only the epilogue (in the recompute form the
+// copies and MMAs of pass 1 already run); otherwise one launch per pass.
 // Every wait is bounded; a role that times out sets a CTA-wide abort flag so
 // the others leave their loops; copies and MMAs in flight are waited for and
 // the tensor memory is freed on every path.
@@ -82,6 +86,8 @@ struct TcPlan {  // shared-memory offsets from the 1024-byte aligned base, and t
     int off_qhi, off_qlo, off_stg, off_epi, off_epi1, off_lo, off_raw, total;
     int nwork, nheads;  // work units (128-key tiles) and (item, KV head) pairs
     int p0, p1;         // the passes this launch runs: 0 = scores and statistics, 1 = head scores
+    int rc;             // pass 1 recomputes the logits through the copy / MMA pipeline instead of reading
+                        // the kept exp values (chosen when those would not fit in L2)
 };
 
 __host__ __device__ inline int align1k(int x) { return (x + 1023) & ~1023; }
@@ -216,8 +222,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     int w0, nt;
     cta_range(P, a.ntiles, w0, nt);
-    const int nv = P.p0 == 0 ? nt : 0;  // tiles through the copy / convert / MMA pipeline (pass 0)
-    auto wof = [&](int i) { return w0 + i; };
+    // visits of the copy / convert / MMA pipeline: pass 0's tiles in order, then (recompute form) pass 1's
+    // in reverse, so that pass 1 starts on the tiles pass 0 read last (still in L2)
+    const int nv0 = P.p0 == 0 ? nt : 0, nv1 = (P.rc && P.p1 == 1) ? nt : 0, nv = nv0 + nv1;
+    auto wof = [&](int v) { return w0 + (v < nv0 ? v : nt - 1 - (v - nv0)); };
     const int S = P.S;
 
     if (tid == 0) {
@@ -494,9 +502,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         float* csm = reinterpret_cast<float*>(sm + P.off_epi1 + 1024);   // pass 1: [128][4] quarter weights
         float* red = reinterpret_cast<float*>(sm + P.off_epi1 + 3072);   // pass 1: [8][128] partial sums
         bool ok = true;
-        // ---- pass 0: per-(row, tile) max and sum of exp(l - max) (rocket.cpp:91-107); every
-        // exp(l - quarter max) is kept (fp32, rows of nkp) with the quarter maxima for pass 1
-        for (int i = 0; i < nv && ok; ++i) {
+        // ---- pass 0: per-(row, tile) max and sum of exp(l - max) (rocket.cpp:91-107); unless pass 1
+        // recomputes, every exp(l - quarter max) is kept (fp32, rows of nkp) with the quarter maxima
+        for (int i = 0; i < nv0 && ok; ++i) {
             int b, hc, tile;
             work_unit(a, wof(i), b, hc, tile);
             const int k0 = tile * kMmaM, nkeys = min(kMmaM, a.nk - k0);
@@ -545,7 +553,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const int r = c * 16 + row;
                 if (kh == 0) {
                     part[q * 128 + r] = make_float2(m, s);
-                    if (r < a.R) __stcg(a.qmax + ((row_base + r) * a.ntiles + tile) * 4 + q, m);
+                    if (r < a.R && !P.rc) __stcg(a.qmax + ((row_base + r) * a.ntiles + tile) * 4 + q, m);
+                }
+                if (P.rc) {  // nothing kept: pass 1 recomputes
+                    __syncwarp();  // the transpose buffer is rewritten next
+                    continue;
                 }
                 // the exp values back through the transpose buffer, then one row per store
                 // instruction: 32 consecutive keys, 128 contiguous bytes
@@ -626,11 +638,71 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 ok = group_all(kBarEpi, kEpiThreads, gb);
             }
         }
+        int prev = -1;
+        // ---- pass 1, recompute form: head scores sum_r exp(l - M_r) * inv_r (rocket.cpp:114-116) from
+        // the logits in tensor memory.  A thread holds one key (its lane) and the rows of its chunks, so
+        // the sum over the rows needs no transpose; the two warps of a lane quarter add their halves.
+        for (int v = nv0; ok && v < nv; ++v) {
+            int b, hc, tile;
+            work_unit(a, wof(v), b, hc, tile);
+            const int head = wof(v) / a.ntiles;
+            const int k0 = tile * kMmaM, nkeys = min(kMmaM, a.nk - k0);
+            const size_t row_base = ((size_t)b * a.head_count + hc) * a.R;
+            if (head != prev) {
+                group_sync(kBarEpi, kEpiThreads);  // the previous head's statistics are no longer read
+                // padding rows (zero queries): M = FLT_MAX and inv = 0 make their terms exactly 0
+                if (one_launch) {
+                    for (int r = et; r < P.NP; r += kEpiThreads) {
+                        const float2 x = r < a.R ? __ldcg(a.rstats + row_base + r) : make_float2(FLT_MAX, 0.0f);
+                        rsm[r] = x.x;
+                        rsi[r] = x.y;
+                    }
+                } else {
+                    for (int r = ep; r < P.NP; r += 8) {
+                        float M = FLT_MAX, inv = 0.0f;
+                        if (r < a.R) fold_row(row_base + r, M, inv);
+                        if (lane == 0) {
+                            rsm[r] = M;
+                            rsi[r] = r < a.R ? inv : 0.0f;
+                        }
+                    }
+                }
+                group_sync(kBarEpi, kEpiThreads);
+                prev = head;
+            }
+            const int ab = v & 1;
+            const bool w = mbar_wait_or_abort(&B.acc_full[ab], (uint32_t)((v >> 1) & 1), a.err, abort_flag);
+            if (!group_all(kBarEpi, kEpiThreads, w)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t trow = tbase + (uint32_t)(ab * kAccCols) + ((uint32_t)(q * 32) << 16);
+            float hsum = 0.0f;
+            for (int c = c0; c < c1; ++c) {
+                float x[16];
+                tmem_ld16(trow + (uint32_t)(c * 16), x);
+#pragma unroll
+                for (int j = 0; j < 16; j += 2) {
+                    const int r = c * 16 + j;  // rows r, r + 1 (the padding rows have inv 0)
+                    const float2 e = mufu_expf2(__fadd2_rn(__fmul2_rn(make_float2(x[j], x[j + 1]),
+                                                                      make_float2(a.inv_sqrt_d, a.inv_sqrt_d)),
+                                                           make_float2(-rsm[r], -rsm[r + 1])));
+                    hsum = fmaf(e.x, rsi[r], hsum);
+                    hsum = fmaf(e.y, rsi[r + 1], hsum);
+                }
+            }
+            tc_fence_before();
+            mbar_arrive1(&B.acc_empty[ab]);
+            red[hf * 128 + kk] = hsum;
+            group_sync(kBarEpi, kEpiThreads);
+            if (et < 128 && et < nkeys) a.hs[((size_t)b * a.head_count + hc) * a.nk + k0 + et] = red[et] + red[128 + et];
+            group_sync(kBarEpi, kEpiThreads);
+        }
         // ---- pass 1: head scores sum_r exp(l - M_r) * inv_r (rocket.cpp:114-116) from the kept
         // exp(l - m_q): each term is e * (exp(m_q - M_r) * inv_r), one exp per (row, tile, quarter)
-        int prev = -1;
         const int kg = et & 31, rg = et >> 5;  // 4 keys (quarter kg / 8) x rows rg, rg + 8, ...
-        for (int i = 0; ok && P.p1 == 1 && i < nt; ++i) {
+        for (int i = 0; ok && P.p1 == 1 && !P.rc && i < nt; ++i) {
             int b, hc, tile;
             work_unit(a, w0 + i, b, hc, tile);
             const int head = (w0 + i) / a.ntiles;
@@ -761,6 +833,10 @@ int launch_kind(const EvictArgs& a, int batch, cudaStream_t st) {
     TcPlan P = tc_plan(KIND, a.R, a.D);
     P.nwork = batch * a.head_count * a.ntiles;
     P.nheads = batch * a.head_count;
+    // keep pass 0's exp values for pass 1 while they fit in L2 with room to spare, else recompute
+    // the logits in pass 1 (a second read of K, from HBM, costs less than writing and reading them)
+    const double kept_bytes = (double)P.nheads * a.R * a.nkp * 4.0;
+    P.rc = KIND != KIND_Q8 && kept_bytes > 48.0 * 1024 * 1024 ? 1 : 0;
     const int sms = sm_count();
     if (sms <= 0) return RKV_ERR_CUDA;
     const int grid = P.nwork < sms ? P.nwork : sms;

@@ -101,6 +101,34 @@ def test_stage1_long_prefix_select(kind, cuda):
         assert np.array_equal(got, want), (eng, boundary_report(total, got, want))
 
 
+@pytest.mark.parametrize("kind", ["f32", "bf16"])
+def test_stage1_recompute_form(kind, cuda):
+    """Kept exp values of 8 heads x 96 rows x 20000 keys (61 MB) exceed what
+    the persistent scorer keeps for pass 1, so pass 1 recomputes the logits
+    through the copy / MMA pipeline (in reverse tile order): kept indices equal
+    the oracle's and the other engines'."""
+    import torch
+    cfg = O.Config(num_heads=24, num_heads_kv=8, dim_head=128, prompt_budget=2500)
+    len_k = 20000
+    Q, K = rkvgen.stage1_inputs(97, 24, 8, 128, 32, len_k)
+    if kind == "bf16":
+        Q, K = rkvgen.bf16_round(Q), rkvgen.bf16_round(K)
+        Qd, Kd = rkvgen.bf16_bits(Q), rkvgen.bf16_bits(K)
+    else:
+        Qd, Kd = Q, K
+    want, total = O.prefill_eviction(Q, K, 32, len_k, cfg, want_total=True)
+    Qt = dev(Qd, kind, cuda).unsqueeze(0).contiguous()
+    Kt = dev(Kd, kind, cuda).unsqueeze(0).contiguous()
+    ev = rkv.Evictor(to_rkv(cfg), 32, len_k, 1, KIND[kind], cuda)
+    for eng in (rkv.ENGINE_TENSOR, rkv.ENGINE_SIMT):
+        k, n = ev(Qt, Kt, engine=eng)
+        torch.cuda.synchronize()
+        got = k[0, : int(n[0])].cpu().numpy()
+        assert len(got) == 2500
+        assert np.array_equal(got, want), (eng, boundary_report(total, got, want))
+    assert rkv.lib().rkv_workspace_status(rkv._ptr(ev.ws), 0) == 0
+
+
 def test_stage1_config0_full_size(cuda):
     """K [8, 8192, 128] fp32, Q [24, 32, 128] window, budget 1024, ks 63."""
     cfg = O.Config(num_heads=24, num_heads_kv=8, dim_head=128, prompt_budget=1024)
