@@ -4,16 +4,17 @@
 // plan fits.  evict_mma.cu keeps the non-persistent kernel for the rest.
 //
 // One CTA per SM walks a contiguous range of (item, KV head, 128-key tile)
-// work units.  Per tile the contraction D[128 keys][N rows] = K_tile . Q^T
-// (N = G * obs_w rounded up to 16) accumulates in tensor memory, alternating
-// between two accumulators so the epilogue of a tile overlaps the MMAs of the
-// next.  The reduction dimension is walked in "k-blocks" of 128 bytes of
-// operand row (32 fp32 or 64 bf16 values; a q8_0 block of 32 values is one
-// fp32 k-block after dequantisation).  Shared-memory operands use the
-// K-major 128-byte-swizzle layout of tcgen05.
+// work units.  Per tile the contraction D[128 query rows][128 keys] =
+// Q . K_tile^T accumulates in tensor memory (the window rows, G * obs_w of
+// them, on the lanes; lanes past them are not used), alternating between two
+// accumulators so the epilogue of a tile overlaps the MMAs of the next.  The
+// reduction dimension is walked in "k-blocks" of 128 bytes of operand row (32
+// fp32 or 64 bf16 values; a q8_0 block of 32 values is one fp32 k-block after
+// dequantisation).  Shared-memory operands use the K-major 128-byte-swizzle
+// layout of tcgen05.
 //
 // fp32 (and dequantised q8_0) runs as three TF32 products per K step,
-// hi.hi + hi.lo + lo.hi: the tensor core reads the top 19 bits of an fp32
+// hi.hi + lo.hi + hi.lo: the tensor core reads the top 19 bits of an fp32
 // operand (hi), and lo = x - hi is exact, so the logits carry close to fp32
 // accuracy.  bf16 runs one bf16 product (exact products, fp32 accumulation).
 //
@@ -32,24 +33,22 @@
 //               query block; q8_0 tiles loaded with coalesced 8-byte loads and
 //               dequantised exactly to fp32 in shared memory (x and lo), the
 //               q8_0 window queries likewise;
-//   warps 6-13  epilogue, two warps per tensor-memory lane quarter (warp w
-//               reads lanes 32 (w % 4) ..), each taking half of the window
-//               rows.
+//   warps 6-13  epilogue, two groups of four that take the tiles in turn (one
+//               accumulator each); warp w reads lanes 32 (w % 4) .. 32 (w % 4)
+//               + 31, so a thread holds one window row's 128 logits of a tile.
 //
-// Two passes over the CTA's tiles (rocket.cpp:91-116): pass 0 writes the
-// per-(row, tile) max and sum of exp(l - max) of l = (q . k) / sqrt(D); the
-// epilogue then folds a head's tile statistics into the row max M_r and
-// inv_r = 1 / (sum_r + 1e-9) (rocket.cpp:108-113), and pass 1 writes the head
-// score of every key, sum_r exp(l - M_r) * inv_r, for the pooling kernel.
-// Pass 1 has two forms.  While they fit in L2, pass 0 keeps every
-// exp(l - quarter max) and pass 1 streams them once (one exp per (row, tile,
-// quarter) rescales them).  For long prefixes, whose kept values would be
-// written to and read back from HBM, pass 1 instead runs the copies and MMAs
-// again over the tiles in reverse order (the first ones are still in L2) and
-// forms each key's score from the logits in tensor memory.  Both passes run
-// in one cooperative launch when every CTA can be resident: a bounded grid
-// barrier between them holds only the epilogue (in the recompute form the
-// copies and MMAs of pass 1 already run); otherwise one launch per pass.
+// Two passes over the CTA's tiles (rocket.cpp:91-116).  Pass 0: a thread
+// forms its row's max and sum of exp(l - max) over the tile, l = (q . k) /
+// sqrt(D), with no exchange between threads.  The epilogue then folds a
+// head's tile statistics into the row max M_r and inv_r = 1 / (sum_r + 1e-9)
+// (rocket.cpp:108-113).  Pass 1 runs the copies and MMAs again, over the tiles
+// in reverse order (its first tiles are the ones pass 0 read last, still in
+// L2), and writes the head score of every key, sum_r exp(l - M_r) * inv_r, for
+// the pooling kernel: a thread scales its row's logits and each warp sums its
+// 32 rows by shuffles.  Both passes run in one cooperative launch when every
+// CTA can be resident: a bounded grid barrier between them holds only the
+// epilogue while the copies and MMAs of pass 1 already run; otherwise one
+// launch per pass.
 // Every wait is bounded; a role that times out sets a CTA-wide abort flag so
 // the others leave their loops; copies and MMAs in flight are waited for and
 // the tensor memory is freed on every path.
@@ -62,6 +61,7 @@
 #include <string.h>
 
 #include <mutex>
+#include <type_traits>
 
 namespace rkv {
 namespace {
@@ -73,8 +73,7 @@ constexpr int kMaxStages = 8;
 constexpr int kLoStages = 2;
 constexpr int kAccCols = 128;       // tensor-memory columns per accumulator
 constexpr int kTmemCols = 2 * kAccCols;
-constexpr int kTbStride = 36;       // floats per row of an epilogue warp's transpose buffer (16-byte rows, conflict-free)
-constexpr int kBarConv = 1, kBarEpi = 2;
+constexpr int kBarConv = 1, kBarGrp = 2, kBarEpiAll = 4;  // named barriers: converters, epilogue groups 0 / 1, all epilogue warps
 constexpr int kSmemMax = 227 * 1024;  // dynamic shared memory per CTA on sm_100
 constexpr int kQ8Row = 136;           // bytes of one q8_0 row of 128 values
 constexpr int kQ8Words = 128 * kQ8Row / 8 / 128;  // 8-byte words per converter thread of a q8_0 tile (17)
@@ -83,11 +82,9 @@ enum { KIND_F32 = 0, KIND_BF16 = 1, KIND_Q8 = 2 };
 
 struct TcPlan {  // shared-memory offsets from the 1024-byte aligned base, and the work split
     int NP, nkb, rowb, S, q_atom, qbytes;
-    int off_qhi, off_qlo, off_stg, off_epi, off_epi1, off_lo, off_raw, total;
+    int off_qhi, off_qlo, off_stg, off_epi, off_lo, off_raw, total;
     int nwork, nheads;  // work units (128-key tiles) and (item, KV head) pairs
     int p0, p1;         // the passes this launch runs: 0 = scores and statistics, 1 = head scores
-    int rc;             // pass 1 recomputes the logits through the copy / MMA pipeline instead of reading
-                        // the kept exp values (chosen when those would not fit in L2)
 };
 
 __host__ __device__ inline int align1k(int x) { return (x + 1023) & ~1023; }
@@ -107,10 +104,10 @@ inline TcPlan tc_plan(int kind, int R, int D) {
     if (tf32) off += P.nkb * P.q_atom;
     P.off_stg = off;
     if (kind == KIND_Q8) off += align1k(128 * kQ8Row);
-    P.off_epi = off;  // pass 0: transpose buffers and quarter statistics
-    off += align1k(8 * 16 * kTbStride * 4 + 4 * 128 * 8);
-    P.off_epi1 = off;  // pass 1: row statistics, quarter weights, partial sums
-    off += 8192;
+    // the MMA reads 128 query rows; rows NP .. 127 fall on what follows the query block (these bytes, the
+    // low-part stages or the ring; their accumulator lanes are not used)
+    P.off_epi = off;  // pass 1: per epilogue group, [quarter][key] partial head scores
+    off += 2 * 4 * 128 * 4;
     P.off_lo = off;
     if (tf32) off += kLoStages * kStageB;
     P.off_raw = off;
@@ -224,7 +221,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     cta_range(P, a.ntiles, w0, nt);
     // visits of the copy / convert / MMA pipeline: pass 0's tiles in order, then (recompute form) pass 1's
     // in reverse, so that pass 1 starts on the tiles pass 0 read last (still in L2)
-    const int nv0 = P.p0 == 0 ? nt : 0, nv1 = (P.rc && P.p1 == 1) ? nt : 0, nv = nv0 + nv1;
+    const int nv0 = P.p0 == 0 ? nt : 0, nv1 = P.p1 == 1 ? nt : 0, nv = nv0 + nv1;
     auto wof = [&](int v) { return w0 + (v < nv0 ? v : nt - 1 - (v - nv0)); };
     const int S = P.S;
 
@@ -239,7 +236,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&B.acc_full[i], 1);
-            mbar_init(&B.acc_empty[i], kEpiThreads);
+            mbar_init(&B.acc_empty[i], 128);  // the epilogue group of this accumulator
         }
         mbar_init(B.q_full, 128);
         mbar_init(B.q_empty, 1);
@@ -297,7 +294,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer (the whole warp; one elected lane issues) ----------------
         {
-            const uint32_t idesc = mma_idesc(TF32 ? 2u : 1u, (uint32_t)P.NP);
+            const uint32_t idesc = mma_idesc(TF32 ? 2u : 1u, (uint32_t)kMmaM);  // M = 128 query rows, N = 128 keys
             int qn = 0, prev = -1;
             bool ok = true;
             for (int i = 0; i < nv && ok; ++i) {
@@ -333,10 +330,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     const uint64_t dQh = mma_desc_sw128(qh), dQl = mma_desc_sw128(ql);
                     for (int st = 0; st < steps; ++st) {
                         const uint64_t o = (uint64_t)(2 * st);
-                        mma_issue_w<TF32>(dacc, dKh + o, dQh + o, idesc, (kb | st) ? 1u : 0u);
+                        mma_issue_w<TF32>(dacc, dQh + o, dKh + o, idesc, (kb | st) ? 1u : 0u);
                         if (TF32) {
-                            mma_issue_w<TF32>(dacc, dKh + o, dQl + o, idesc, 1u);
-                            mma_issue_w<TF32>(dacc, dKl + o, dQh + o, idesc, 1u);
+                            mma_issue_w<TF32>(dacc, dQl + o, dKh + o, idesc, 1u);
+                            mma_issue_w<TF32>(dacc, dQh + o, dKl + o, idesc, 1u);
                         }
                     }
                     mma_commit_w(&B.raw_empty[s]);
@@ -491,104 +488,67 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
     } else {
         // ---------------- epilogue ----------------
-        const int ep = warp - 6, et = tid - 192, q = warp & 3, kk = q * 32 + lane;
-        const int hf = ep >> 2;  // which half of the window rows this warp takes
-        const int nch = P.NP / 16, cmid = (nch + 1) / 2;
-        const int c0 = hf ? cmid : 0, c1 = hf ? nch : cmid;
-        float* tb = reinterpret_cast<float*>(sm + P.off_epi) + ep * 16 * kTbStride;
-        float2* part = reinterpret_cast<float2*>(sm + P.off_epi + 8 * 16 * kTbStride * 4);  // [4][128]
-        float* rsm = reinterpret_cast<float*>(sm + P.off_epi1);          // pass 1: row max M_r [128]
-        float* rsi = reinterpret_cast<float*>(sm + P.off_epi1 + 512);    // pass 1: 1 / (row sum + 1e-9) [128]
-        float* csm = reinterpret_cast<float*>(sm + P.off_epi1 + 1024);   // pass 1: [128][4] quarter weights
-        float* red = reinterpret_cast<float*>(sm + P.off_epi1 + 3072);   // pass 1: [8][128] partial sums
+        // Window rows on the tensor-memory lanes, keys on the columns: a thread holds one row's logits of
+        // a tile.  Two groups of four warps take the visits in turn (group g the ones on accumulator g);
+        // warp w of a group reads lanes 32 (w % 4) .. 32 (w % 4) + 31, its rows.
+        const int ep = warp - 6, grp = ep >> 2, q = warp & 3, gt = (ep & 3) * 32 + lane;
+        const int r = q * 32 + lane;  // this thread's window row
+        const bool row_ok = r < a.R;
+        // rows of this warp: all valid, none (padding), or some (a per-lane select)
+        const int wmode = q * 32 + 32 <= a.R ? 0 : q * 32 >= a.R ? 1 : 2;
+        const int gbar = kBarGrp + grp;
+        float* red = reinterpret_cast<float*>(sm + P.off_epi) + grp * 4 * 128;  // pass 1: [quarter][key]
+        const uint32_t tacc = tbase + (uint32_t)(grp * kAccCols) + ((uint32_t)(q * 32) << 16);
         bool ok = true;
-        // ---- pass 0: per-(row, tile) max and sum of exp(l - max) (rocket.cpp:91-107); unless pass 1
-        // recomputes, every exp(l - quarter max) is kept (fp32, rows of nkp) with the quarter maxima
-        for (int i = 0; i < nv0 && ok; ++i) {
+        // ---- pass 0: per-(row, tile) max and sum of exp(l - max) (rocket.cpp:91-107)
+        for (int v = grp; v < nv0 && ok; v += 2) {
             int b, hc, tile;
-            work_unit(a, wof(i), b, hc, tile);
+            work_unit(a, wof(v), b, hc, tile);
             const int k0 = tile * kMmaM, nkeys = min(kMmaM, a.nk - k0);
             const size_t row_base = ((size_t)b * a.head_count + hc) * a.R;
-            const int ab = i & 1;
-            const bool w = mbar_wait_or_abort(&B.acc_full[ab], (uint32_t)((i >> 1) & 1), a.err, abort_flag);
-            if (!group_all(kBarEpi, kEpiThreads, w)) {
+            const bool w = mbar_wait_or_abort(&B.acc_full[grp], (uint32_t)((v >> 1) & 1), a.err, abort_flag);
+            if (!group_all(gbar, 128, w)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const uint32_t trow = tbase + (uint32_t)(ab * kAccCols) + ((uint32_t)(q * 32) << 16);
-            const int row = lane & 15, kh = lane >> 4;
-            for (int c = c0; c < c1; ++c) {
-                float v[16];
-                tmem_ld16(trow + (uint32_t)(c * 16), v);
+            // two sweeps over the row's 128 logits: the max, then the sum of exp(l - max).  The max is
+            // taken over the accumulator and scaled once: rounding is monotonic and the scale positive, so
+            // RN(max(x) / sqrt(D)) = max(RN(x / sqrt(D))).
+            float M = -FLT_MAX, S = 0.0f;  // rocket.cpp:93
+            if (wmode != 1) {
+                auto sweeps = [&](auto full) {
+                    float mx = -INFINITY;  // all -inf (or NaN): M = -FLT_MAX, as the running max from -FLT_MAX gives
+#pragma unroll 1
+                    for (int c = 0; c < 4; ++c) {
+                        float x[32];
+                        tmem_ld32(tacc + (uint32_t)(c * 32), x);
 #pragma unroll
-                for (int j = 0; j < 16; ++j) tb[j * kTbStride + lane] = kk < nkeys ? v[j] * a.inv_sqrt_d : -INFINITY;
-                __syncwarp();
-                // row c*16 + row, 16 of this warp's keys
-                const float4* rv4 = reinterpret_cast<const float4*>(tb + row * kTbStride + kh * 16);
-                float rv[16];
+                        for (int j = 0; j < 32; ++j)
+                            if (decltype(full)::value || c * 32 + j < nkeys) mx = fmaxf(mx, x[j]);
+                    }
+                    M = fmaxf(mx * a.inv_sqrt_d, -FLT_MAX);
+#pragma unroll 1
+                    for (int c = 0; c < 4; ++c) {
+                        float x[32];
+                        tmem_ld32(tacc + (uint32_t)(c * 32), x);
 #pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const float4 f = rv4[t];
-                    rv[4 * t] = f.x;
-                    rv[4 * t + 1] = f.y;
-                    rv[4 * t + 2] = f.z;
-                    rv[4 * t + 3] = f.w;
-                }
-                float m = -FLT_MAX;  // rocket.cpp:93
-#pragma unroll
-                for (int t = 0; t < 16; ++t) m = fmaxf(m, rv[t]);
-                m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
-                float e[16];
-                float s = 0.0f;
-#pragma unroll
-                for (int t = 0; t < 8; ++t) {
-                    const float2 x = mufu_expf2(__fadd2_rn(make_float2(rv[2 * t], rv[2 * t + 1]), make_float2(-m, -m)));
-                    e[2 * t] = x.x;
-                    e[2 * t + 1] = x.y;
-                    s += x.x;
-                    s += x.y;
-                }
-                s += __shfl_xor_sync(0xffffffffu, s, 16);
-                const int r = c * 16 + row;
-                if (kh == 0) {
-                    part[q * 128 + r] = make_float2(m, s);
-                    if (r < a.R && !P.rc) __stcg(a.qmax + ((row_base + r) * a.ntiles + tile) * 4 + q, m);
-                }
-                if (P.rc) {  // nothing kept: pass 1 recomputes
-                    __syncwarp();  // the transpose buffer is rewritten next
-                    continue;
-                }
-                // the exp values back through the transpose buffer, then one row per store
-                // instruction: 32 consecutive keys, 128 contiguous bytes
-                float4* eo = reinterpret_cast<float4*>(tb + row * kTbStride + kh * 16);
-#pragma unroll
-                for (int t = 0; t < 4; ++t) eo[t] = make_float4(e[4 * t], e[4 * t + 1], e[4 * t + 2], e[4 * t + 3]);
-                __syncwarp();
-                if (kk < nkeys) {
-                    float* ecol = a.logits + (row_base + c * 16) * (size_t)a.nkp + k0 + kk;
-#pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        if (c * 16 + j < a.R) __stcg(ecol + (size_t)j * a.nkp, tb[j * kTbStride + lane]);
-                }
-                __syncwarp();
+                        for (int j = 0; j < 32; j += 2) {
+                            const float2 l = __fmul2_rn(make_float2(x[j], x[j + 1]), make_float2(a.inv_sqrt_d, a.inv_sqrt_d));
+                            const float2 e = mufu_expf2(__fadd2_rn(l, make_float2(-M, -M)));
+                            if (decltype(full)::value || c * 32 + j < nkeys) S += e.x;
+                            if (decltype(full)::value || c * 32 + j + 1 < nkeys) S += e.y;
+                        }
+                    }
+                };
+                if (nkeys == kMmaM)
+                    sweeps(std::true_type{});
+                else
+                    sweeps(std::false_type{});
             }
             tc_fence_before();
-            mbar_arrive1(&B.acc_empty[ab]);
-            group_sync(kBarEpi, kEpiThreads);
-            if (et < a.R) {  // combine the four 32-key quarters of the tile
-                float M = -FLT_MAX;
-#pragma unroll
-                for (int t = 0; t < 4; ++t) M = fmaxf(M, part[t * 128 + et].x);
-                float Ssum = 0.0f;
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const float2 p = part[t * 128 + et];
-                    Ssum += p.y * det_expf(p.x - M);
-                }
-                __stcg(a.tstats + (row_base + et) * a.ntiles + tile, make_float2(M, Ssum));
-            }
-            group_sync(kBarEpi, kEpiThreads);
+            mbar_arrive1(&B.acc_empty[grp]);
+            if (row_ok) __stcg(a.tstats + (row_base + r) * a.ntiles + tile, make_float2(M, S));
         }
         // ---- the row fold (rocket.cpp:108-113): row max M_r over the tiles and
         // inv_r = 1 / (sum_t s_t exp(m_t - M_r) + 1e-9), one warp per row with every load in flight
@@ -620,12 +580,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             inv = 1.0f / (Ssum + 1e-9f);
         };
         const bool one_launch = P.p0 == 0 && P.p1 == 1;
-        if (ok && one_launch) {
+        if (one_launch) {
             // every CTA's statistics are written before any row folds them
-            group_sync(kBarEpi, kEpiThreads);
-            bool gb = true;
-            if (et == 0) gb = grid_barrier(a.gbar, gridDim.x, a.err, abort_flag);
-            ok = group_all(kBarEpi, kEpiThreads, gb);
+            ok = group_all(kBarEpiAll, kEpiThreads, ok);
+            bool gb = ok;
+            if (ep == 0 && lane == 0 && ok) gb = grid_barrier(a.gbar, gridDim.x, a.err, abort_flag);
+            ok = group_all(kBarEpiAll, kEpiThreads, gb);
             if (ok) {
                 const size_t nrows = (size_t)P.nheads * a.R;
                 for (size_t x = blockIdx.x + (size_t)gridDim.x * ep; x < nrows; x += (size_t)gridDim.x * 8) {
@@ -633,141 +593,87 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     fold_row(x, M, inv);
                     if (lane == 0) __stcg(a.rstats + x, make_float2(M, inv));
                 }
-                group_sync(kBarEpi, kEpiThreads);
-                if (et == 0) gb = grid_barrier(a.gbar, 2u * gridDim.x, a.err, abort_flag);
-                ok = group_all(kBarEpi, kEpiThreads, gb);
+                group_sync(kBarEpiAll, kEpiThreads);
+                if (ep == 0 && lane == 0) gb = grid_barrier(a.gbar, 2u * gridDim.x, a.err, abort_flag);
+                ok = group_all(kBarEpiAll, kEpiThreads, gb);
             }
         }
+        // ---- pass 1: head scores sum_r exp(l - M_r) * inv_r (rocket.cpp:114-116), the logits computed
+        // again.  A thread scales its row's 32 logits of a chunk, and the warp sums its 32 rows by
+        // recursive halving (lane l ends with key l of the chunk); the four warps' sums are added in
+        // quarter order.  Padding rows: M = FLT_MAX and inv = 0 (terms exactly 0).
         int prev = -1;
-        // ---- pass 1, recompute form: head scores sum_r exp(l - M_r) * inv_r (rocket.cpp:114-116) from
-        // the logits in tensor memory.  A thread holds one key (its lane) and the rows of its chunks, so
-        // the sum over the rows needs no transpose; the two warps of a lane quarter add their halves.
-        for (int v = nv0; ok && v < nv; ++v) {
+        float Mr = FLT_MAX, ir = 0.0f;
+        for (int v = nv0 + ((grp ^ nv0) & 1); ok && v < nv; v += 2) {
             int b, hc, tile;
             work_unit(a, wof(v), b, hc, tile);
             const int head = wof(v) / a.ntiles;
             const int k0 = tile * kMmaM, nkeys = min(kMmaM, a.nk - k0);
             const size_t row_base = ((size_t)b * a.head_count + hc) * a.R;
             if (head != prev) {
-                group_sync(kBarEpi, kEpiThreads);  // the previous head's statistics are no longer read
-                // padding rows (zero queries): M = FLT_MAX and inv = 0 make their terms exactly 0
                 if (one_launch) {
-                    for (int r = et; r < P.NP; r += kEpiThreads) {
-                        const float2 x = r < a.R ? __ldcg(a.rstats + row_base + r) : make_float2(FLT_MAX, 0.0f);
-                        rsm[r] = x.x;
-                        rsi[r] = x.y;
-                    }
+                    const float2 x = row_ok ? __ldcg(a.rstats + row_base + r) : make_float2(FLT_MAX, 0.0f);
+                    Mr = x.x;
+                    ir = x.y;
                 } else {
-                    for (int r = ep; r < P.NP; r += 8) {
-                        float M = FLT_MAX, inv = 0.0f;
-                        if (r < a.R) fold_row(row_base + r, M, inv);
-                        if (lane == 0) {
-                            rsm[r] = M;
-                            rsi[r] = r < a.R ? inv : 0.0f;
+                    Mr = FLT_MAX;
+                    ir = 0.0f;
+                    for (int rr = 0; rr < 32 && q * 32 + rr < a.R; ++rr) {  // warp-uniform bound
+                        float M, inv;
+                        fold_row(row_base + q * 32 + rr, M, inv);
+                        if (lane == rr) {
+                            Mr = M;
+                            ir = inv;
                         }
                     }
                 }
-                group_sync(kBarEpi, kEpiThreads);
                 prev = head;
             }
-            const int ab = v & 1;
-            const bool w = mbar_wait_or_abort(&B.acc_full[ab], (uint32_t)((v >> 1) & 1), a.err, abort_flag);
-            if (!group_all(kBarEpi, kEpiThreads, w)) {
+            const bool w = mbar_wait_or_abort(&B.acc_full[grp], (uint32_t)((v >> 1) & 1), a.err, abort_flag);
+            if (!group_all(gbar, 128, w)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const uint32_t trow = tbase + (uint32_t)(ab * kAccCols) + ((uint32_t)(q * 32) << 16);
-            float hsum = 0.0f;
-            for (int c = c0; c < c1; ++c) {
-                float x[16];
-                tmem_ld16(trow + (uint32_t)(c * 16), x);
+            float* rq = red + q * 128;
+            if (wmode == 1) {
 #pragma unroll
-                for (int j = 0; j < 16; j += 2) {
-                    const int r = c * 16 + j;  // rows r, r + 1 (the padding rows have inv 0)
-                    const float2 e = mufu_expf2(__fadd2_rn(__fmul2_rn(make_float2(x[j], x[j + 1]),
-                                                                      make_float2(a.inv_sqrt_d, a.inv_sqrt_d)),
-                                                           make_float2(-rsm[r], -rsm[r + 1])));
-                    hsum = fmaf(e.x, rsi[r], hsum);
-                    hsum = fmaf(e.y, rsi[r + 1], hsum);
+                for (int c = 0; c < 4; ++c) rq[c * 32 + lane] = 0.0f;
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < 4; ++c) {
+                    float x[32];
+                    tmem_ld32(tacc + (uint32_t)(c * 32), x);
+#pragma unroll
+                    for (int j = 0; j < 32; j += 2) {
+                        const float2 l = __fmul2_rn(make_float2(x[j], x[j + 1]), make_float2(a.inv_sqrt_d, a.inv_sqrt_d));
+                        const float2 e = mufu_expf2(__fadd2_rn(l, make_float2(-Mr, -Mr)));
+                        x[j] = e.x * ir;
+                        x[j + 1] = e.y * ir;
+                        if (wmode == 2 && !row_ok) x[j] = x[j + 1] = 0.0f;  // the logits of padding rows are not finite-safe
+                    }
+                    // recursive halving over the lanes: after the step of offset o a lane keeps the half of
+                    // its columns selected by bit o of its lane index and adds its partner's copy of it
+#pragma unroll
+                    for (int o = 16, n = 16; o >= 1; o >>= 1, n >>= 1) {
+                        const bool up = (lane & o) != 0;
+#pragma unroll
+                        for (int j = 0; j < n; ++j) {
+                            const float send = up ? x[j] : x[j + n];
+                            const float keep = up ? x[j + n] : x[j];
+                            x[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                        }
+                    }
+                    rq[c * 32 + lane] = x[0];
                 }
             }
             tc_fence_before();
-            mbar_arrive1(&B.acc_empty[ab]);
-            red[hf * 128 + kk] = hsum;
-            group_sync(kBarEpi, kEpiThreads);
-            if (et < 128 && et < nkeys) a.hs[((size_t)b * a.head_count + hc) * a.nk + k0 + et] = red[et] + red[128 + et];
-            group_sync(kBarEpi, kEpiThreads);
-        }
-        // ---- pass 1: head scores sum_r exp(l - M_r) * inv_r (rocket.cpp:114-116) from the kept
-        // exp(l - m_q): each term is e * (exp(m_q - M_r) * inv_r), one exp per (row, tile, quarter)
-        const int kg = et & 31, rg = et >> 5;  // 4 keys (quarter kg / 8) x rows rg, rg + 8, ...
-        for (int i = 0; ok && P.p1 == 1 && !P.rc && i < nt; ++i) {
-            int b, hc, tile;
-            work_unit(a, w0 + i, b, hc, tile);
-            const int head = (w0 + i) / a.ntiles;
-            const int k0 = tile * kMmaM, nkeys = min(kMmaM, a.nk - k0);
-            const size_t row_base = ((size_t)b * a.head_count + hc) * a.R;
-            if (head != prev) {
-                if (one_launch) {
-                    for (int r = et; r < P.NP; r += kEpiThreads) {
-                        const float2 v = r < a.R ? __ldcg(a.rstats + row_base + r) : make_float2(-FLT_MAX, 0.0f);
-                        rsm[r] = v.x;
-                        rsi[r] = v.y;
-                    }
-                } else {
-                    for (int r = ep; r < P.NP; r += 8) {
-                        float M = -FLT_MAX, inv = 0.0f;
-                        if (r < a.R) fold_row(row_base + r, M, inv);
-                        if (lane == 0) {
-                            rsm[r] = M;
-                            rsi[r] = r < a.R ? inv : 0.0f;
-                        }
-                    }
-                }
-                group_sync(kBarEpi, kEpiThreads);
-                prev = head;
-            }
-            // every load of the tile first: the quarter maxima and this thread's exp values
-            const int kq = 4 * kg, qq = kg >> 3;
-            float qm[2];
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const int x = et + kEpiThreads * j, r = x >> 2;
-                qm[j] = (x < P.NP * 4 && r < a.R) ? __ldcg(a.qmax + ((row_base + r) * a.ntiles + tile) * 4 + (x & 3)) : -FLT_MAX;
-            }
-            float4 ev[16];
-            const float* ebase = a.logits + row_base * (size_t)a.nkp + k0 + kq;
-#pragma unroll
-            for (int u = 0; u < 16; ++u) {
-                const int r = rg + 8 * u;
-                ev[u] = (r < a.R && kq < nkeys) ? __ldcg(reinterpret_cast<const float4*>(ebase + (size_t)r * a.nkp))
-                                                : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-            // weights of this tile: c[r][quarter] = exp(m_q - M_r) * inv_r (padding rows 0)
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const int x = et + kEpiThreads * j, r = x >> 2;
-                if (x < P.NP * 4) csm[x] = r < a.R ? det_expf(qm[j] - rsm[r]) * rsi[r] : 0.0f;
-            }
-            group_sync(kBarEpi, kEpiThreads);
-            float2 acc0 = make_float2(0.0f, 0.0f), acc1 = make_float2(0.0f, 0.0f);
-#pragma unroll
-            for (int u = 0; u < 16; ++u) {
-                const int r = rg + 8 * u;
-                const float cw = r < P.NP ? csm[r * 4 + qq] : 0.0f;
-                acc0 = __ffma2_rn(make_float2(ev[u].x, ev[u].y), make_float2(cw, cw), acc0);
-                acc1 = __ffma2_rn(make_float2(ev[u].z, ev[u].w), make_float2(cw, cw), acc1);
-            }
-            *reinterpret_cast<float4*>(red + rg * 128 + kq) = make_float4(acc0.x, acc0.y, acc1.x, acc1.y);
-            group_sync(kBarEpi, kEpiThreads);
-            if (et < 128 && et < nkeys) {
-                float h = 0.0f;
-#pragma unroll
-                for (int g = 0; g < 8; ++g) h += red[g * 128 + et];
-                a.hs[((size_t)b * a.head_count + hc) * a.nk + k0 + et] = h;
-            }
-            group_sync(kBarEpi, kEpiThreads);
+            mbar_arrive1(&B.acc_empty[grp]);
+            group_sync(gbar, 128);
+            if (gt < nkeys)
+                a.hs[((size_t)b * a.head_count + hc) * a.nk + k0 + gt] =
+                    ((red[gt] + red[128 + gt]) + red[256 + gt]) + red[384 + gt];
+            group_sync(gbar, 128);
         }
     }
 
@@ -833,10 +739,6 @@ int launch_kind(const EvictArgs& a, int batch, cudaStream_t st) {
     TcPlan P = tc_plan(KIND, a.R, a.D);
     P.nwork = batch * a.head_count * a.ntiles;
     P.nheads = batch * a.head_count;
-    // keep pass 0's exp values for pass 1 while they fit in L2 with room to spare, else recompute
-    // the logits in pass 1 (a second read of K, from HBM, costs less than writing and reading them)
-    const double kept_bytes = (double)P.nheads * a.R * a.nkp * 4.0;
-    P.rc = KIND != KIND_Q8 && kept_bytes > 48.0 * 1024 * 1024 ? 1 : 0;
     const int sms = sm_count();
     if (sms <= 0) return RKV_ERR_CUDA;
     const int grid = P.nwork < sms ? P.nwork : sms;
