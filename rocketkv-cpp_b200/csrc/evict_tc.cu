@@ -6,8 +6,8 @@
 // One CTA per SM walks a contiguous range of (item, KV head, 128-key tile)
 // work units.  Per tile the contraction D[128 query rows][128 keys] =
 // Q . K_tile^T accumulates in tensor memory (the window rows, G * obs_w of
-// them, on the lanes; lanes past them are not used), alternating between two
-// accumulators so the epilogue of a tile overlaps the MMAs of the next.  The
+// them, on the lanes; lanes past them are not used), cycling through four
+// accumulators so the epilogue of a tile overlaps the MMAs of the next ones.  The
 // reduction dimension is walked in "k-blocks" of 128 bytes of operand row (32
 // fp32 or 64 bf16 values; a q8_0 block of 32 values is one fp32 k-block after
 // dequantisation).  Shared-memory operands use the K-major 128-byte-swizzle
@@ -18,7 +18,7 @@
 // operand (hi), and lo = x - hi is exact, so the logits carry close to fp32
 // accuracy.  bf16 runs one bf16 product (exact products, fp32 accumulation).
 //
-// Warp roles (448 threads):
+// Warp roles (704 threads):
 //   warp 0      TMA producer (fp32, bf16): the window queries of each KV
 //               head (one tensor copy per query head and k-block, into the
 //               resident query block) and one copy per k-block of 128 key
@@ -33,7 +33,7 @@
 //               query block; q8_0 tiles loaded with coalesced 8-byte loads and
 //               dequantised exactly to fp32 in shared memory (x and lo), the
 //               q8_0 window queries likewise;
-//   warps 6-13  epilogue, two groups of four that take the tiles in turn (one
+//   warps 6-21  epilogue, four groups of four that take the tiles in turn (one
 //               accumulator each); warp w reads lanes 32 (w % 4) .. 32 (w % 4)
 //               + 31, so a thread holds one window row's 128 logits of a tile.
 //
@@ -66,14 +66,15 @@
 namespace rkv {
 namespace {
 
-constexpr int kTcThreads = 448;
-constexpr int kEpiThreads = 256;    // warps 6-13
+constexpr int kTcThreads = 704;
+constexpr int kAccs = 4;            // tensor-memory accumulators, one per epilogue group
+constexpr int kEpiThreads = 128 * kAccs;  // warps 6-21
 constexpr int kStageB = 128 * 128;  // one operand stage: 128 rows x 128 bytes
 constexpr int kMaxStages = 8;
 constexpr int kLoStages = 2;
 constexpr int kAccCols = 128;       // tensor-memory columns per accumulator
-constexpr int kTmemCols = 2 * kAccCols;
-constexpr int kBarConv = 1, kBarGrp = 2, kBarEpiAll = 4;  // named barriers: converters, epilogue groups 0 / 1, all epilogue warps
+constexpr int kTmemCols = kAccs * kAccCols;
+constexpr int kBarConv = 1, kBarGrp = 2, kBarEpiAll = 2 + kAccs;  // named barriers: converters, epilogue groups, all epilogue warps
 constexpr int kSmemMax = 227 * 1024;  // dynamic shared memory per CTA on sm_100
 constexpr int kQ8Row = 136;           // bytes of one q8_0 row of 128 values
 constexpr int kQ8Words = 128 * kQ8Row / 8 / 128;  // 8-byte words per converter thread of a q8_0 tile (17)
@@ -107,7 +108,7 @@ inline TcPlan tc_plan(int kind, int R, int D) {
     // the MMA reads 128 query rows; rows NP .. 127 fall on what follows the query block (these bytes, the
     // low-part stages or the ring; their accumulator lanes are not used)
     P.off_epi = off;  // pass 1: per epilogue group, [quarter][key] partial head scores
-    off += 2 * 4 * 128 * 4;
+    off += kAccs * 4 * 128 * 4;
     P.off_lo = off;
     if (tf32) off += kLoStages * kStageB;
     P.off_raw = off;
@@ -123,7 +124,8 @@ struct Bars {
 };
 __device__ __forceinline__ Bars bars_of(uint8_t* sm) {
     uint64_t* b = reinterpret_cast<uint64_t*>(sm);
-    return Bars{b, b + 8, b + 16, b + 20, b + 24, b + 26, b + 28, b + 29, b + 30, b + 31};
+    return Bars{b, b + 8, b + 16, b + 20, b + 24, b + 24 + kAccs, b + 24 + 2 * kAccs, b + 25 + 2 * kAccs,
+                b + 26 + 2 * kAccs, b + 27 + 2 * kAccs};
 }
 
 __device__ __forceinline__ void work_unit(const EvictArgs& a, int w, int& b, int& hc, int& tile) {
@@ -213,8 +215,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const Bars B = bars_of(sm);
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + 256);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + 260);
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + 512);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + 516);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     int w0, nt;
@@ -234,7 +236,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_init(&B.lo_full[i], 128);
             mbar_init(&B.lo_empty[i], 1);
         }
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < kAccs; ++i) {
             mbar_init(&B.acc_full[i], 1);
             mbar_init(&B.acc_empty[i], 128);  // the epilogue group of this accumulator
         }
@@ -304,8 +306,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     ++qn;
                     prev = head;
                 }
-                const int ab = i & 1;
-                if (i >= 2 && !__all_sync(0xffffffffu, mbar_wait_or_abort(&B.acc_empty[ab], (uint32_t)(((i >> 1) + 1) & 1),
+                const int ab = i % kAccs;
+                if (i >= kAccs && !__all_sync(0xffffffffu, mbar_wait_or_abort(&B.acc_empty[ab], (uint32_t)(((i / kAccs) + 1) & 1),
                                                                              a.err, abort_flag)))
                     break;
                 tc_fence_after();
@@ -489,7 +491,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     } else {
         // ---------------- epilogue ----------------
         // Window rows on the tensor-memory lanes, keys on the columns: a thread holds one row's logits of
-        // a tile.  Two groups of four warps take the visits in turn (group g the ones on accumulator g);
+        // a tile.  Four groups of four warps take the visits in turn (group g the ones on accumulator g);
         // warp w of a group reads lanes 32 (w % 4) .. 32 (w % 4) + 31, its rows.
         const int ep = warp - 6, grp = ep >> 2, q = warp & 3, gt = (ep & 3) * 32 + lane;
         const int r = q * 32 + lane;  // this thread's window row
@@ -501,12 +503,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t tacc = tbase + (uint32_t)(grp * kAccCols) + ((uint32_t)(q * 32) << 16);
         bool ok = true;
         // ---- pass 0: per-(row, tile) max and sum of exp(l - max) (rocket.cpp:91-107)
-        for (int v = grp; v < nv0 && ok; v += 2) {
+        for (int v = grp; v < nv0 && ok; v += kAccs) {
             int b, hc, tile;
             work_unit(a, wof(v), b, hc, tile);
             const int k0 = tile * kMmaM, nkeys = min(kMmaM, a.nk - k0);
             const size_t row_base = ((size_t)b * a.head_count + hc) * a.R;
-            const bool w = mbar_wait_or_abort(&B.acc_full[grp], (uint32_t)((v >> 1) & 1), a.err, abort_flag);
+            const bool w = mbar_wait_or_abort(&B.acc_full[grp], (uint32_t)((v / kAccs) & 1), a.err, abort_flag);
             if (!group_all(gbar, 128, w)) {
                 ok = false;
                 break;
@@ -588,7 +590,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             ok = group_all(kBarEpiAll, kEpiThreads, gb);
             if (ok) {
                 const size_t nrows = (size_t)P.nheads * a.R;
-                for (size_t x = blockIdx.x + (size_t)gridDim.x * ep; x < nrows; x += (size_t)gridDim.x * 8) {
+                for (size_t x = blockIdx.x + (size_t)gridDim.x * ep; x < nrows; x += (size_t)gridDim.x * (kEpiThreads / 32)) {
                     float M, inv;
                     fold_row(x, M, inv);
                     if (lane == 0) __stcg(a.rstats + x, make_float2(M, inv));
@@ -604,7 +606,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // quarter order.  Padding rows: M = FLT_MAX and inv = 0 (terms exactly 0).
         int prev = -1;
         float Mr = FLT_MAX, ir = 0.0f;
-        for (int v = nv0 + ((grp ^ nv0) & 1); ok && v < nv; v += 2) {
+        for (int v = nv0 + (grp - nv0 % kAccs + kAccs) % kAccs; ok && v < nv; v += kAccs) {
             int b, hc, tile;
             work_unit(a, wof(v), b, hc, tile);
             const int head = wof(v) / a.ntiles;
@@ -629,7 +631,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
                 prev = head;
             }
-            const bool w = mbar_wait_or_abort(&B.acc_full[grp], (uint32_t)((v >> 1) & 1), a.err, abort_flag);
+            const bool w = mbar_wait_or_abort(&B.acc_full[grp], (uint32_t)((v / kAccs) & 1), a.err, abort_flag);
             if (!group_all(gbar, 128, w)) {
                 ok = false;
                 break;
