@@ -101,6 +101,29 @@ def test_stage1_long_prefix_select(kind, cuda):
         assert np.array_equal(got, want), (eng, boundary_report(total, got, want))
 
 
+@pytest.mark.parametrize("H,HK,window,kind", [
+    (32, 8, 32, "bf16"),  # 128 window rows: every lane quarter full
+    (16, 8, 24, "bf16"),  # 48 rows: the second quarter partly padding
+    (24, 8, 40, "f32"),   # 120 rows: the fourth quarter partly padding
+    (8, 8, 8, "f32"),     # 8 rows: most of the first quarter padding
+])
+def test_stage1_window_row_counts(H, HK, window, kind, cuda):
+    """The persistent scorer holds the window rows on the tensor-memory lanes,
+    32 per warp: row counts that fill every lane quarter, or leave one partly
+    or mostly padding, keep the oracle's indices."""
+    cfg = O.Config(num_heads=H, num_heads_kv=HK, dim_head=128, window_size=window, prompt_budget=700)
+    len_k = 3000
+    Q, K = rkvgen.stage1_inputs(400 + H + window, H, HK, 128, window, len_k)
+    if kind == "bf16":
+        Q, K = rkvgen.bf16_round(Q), rkvgen.bf16_round(K)
+        Qd, Kd = rkvgen.bf16_bits(Q), rkvgen.bf16_bits(K)
+    else:
+        Qd, Kd = Q, K
+    want, total = O.prefill_eviction(Q, K, window, len_k, cfg, want_total=True)
+    got = run_gpu(Qd, Kd, kind, window, len_k, cfg, cuda)
+    assert np.array_equal(got, want), boundary_report(total, got, want)
+
+
 @pytest.mark.parametrize("kind", ["f32", "bf16"])
 def test_stage1_recompute_form(kind, cuda):
     """Kept exp values of 8 heads x 96 rows x 20000 keys (61 MB) exceed what
