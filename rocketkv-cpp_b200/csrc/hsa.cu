@@ -611,22 +611,26 @@ __global__ void __launch_bounds__(kSelThreads, 8) hsa_select_kernel(const HsaArg
         float P0[MAXG], P1[MAXG];
 #pragma unroll
         for (int h = 0; h < MAXG; ++h) P0[h] = P1[h] = 0.0f;
+        // the two pages c and c + 128 of a thread through the paired exp (each lane's result is det_expf's)
         for (int base = 0; base < nch; base += 256) {
+            const int c0 = base + tid, c1 = c0 + kSelThreads;
+            const bool v0 = c0 < nch, v1 = c1 < nch;
 #pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
-                const int c = base + tid + hf * kSelThreads;
-                if (c < nch)
-#pragma unroll
-                    for (int h = 0; h < MAXG; ++h)
-                        if (h < G) {
-                            const float e = det_expf(__fsub_rn(wl[(size_t)h * NP + c], hmax[h]));
-                            wl[(size_t)h * NP + c] = e;
-                            if (hf == 0)
-                                P0[h] = __fadd_rn(P0[h], e);
-                            else
-                                P1[h] = __fadd_rn(P1[h], e);
-                        }
-            }
+            for (int h = 0; h < MAXG; ++h)
+                if (h < G) {
+                    float* row = wl + (size_t)h * NP;
+                    const float x0 = v0 ? __fsub_rn(row[c0], hmax[h]) : 0.0f;
+                    const float x1 = v1 ? __fsub_rn(row[c1], hmax[h]) : 0.0f;
+                    const float2 e = det_expf2(make_float2(x0, x1));
+                    if (v0) {
+                        row[c0] = e.x;
+                        P0[h] = __fadd_rn(P0[h], e.x);
+                    }
+                    if (v1) {
+                        row[c1] = e.y;
+                        P1[h] = __fadd_rn(P1[h], e.y);
+                    }
+                }
         }
         // halving tree: s = 128 in the thread, 64 and 32 in shared memory, 16 ... 1 in warp 0
 #pragma unroll
