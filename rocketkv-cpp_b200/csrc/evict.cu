@@ -722,7 +722,6 @@ EvictShape evict_shape(const rkv_config& c, int len_q, int len_k, int batch, int
     s.off_keys = off;     off = align_up(off + B * nk * sizeof(uint32_t), kWorkspaceAlign);
     s.off_pooled = off;   off = align_up(off + B * (size_t)c.num_heads_kv * nk * sizeof(float), kWorkspaceAlign);
     s.off_hs = off;       off = align_up(off + B * HC * nk * sizeof(float), kWorkspaceAlign);
-    s.off_qmax = off;     off = align_up(off + B * HC * R * s.ntiles * 4 * sizeof(float), kWorkspaceAlign);
     s.ws_bytes = off;
     return s;
 }

@@ -16,11 +16,10 @@ struct EvictArgs {
     int k_head_rows;  // rows per KV head in K (len_k, or nk when compacted)
     int head_begin, head_count;
     float inv_sqrt_d;
-    float* logits;      // [batch][head_count][R][nk]; the per-tile tensor-core engine keeps head scores [batch][head_count][nk]
-                        // here; the persistent one keeps exp(l - quarter max) [batch][head_count][R][nkp] here
-    int nkp;            // nk rounded up to 4 (16-byte rows of the persistent engine's exp values)
-    float* hs;          // [batch][head_count][nk] head scores of the persistent tensor-core engine
-    float* qmax;        // [batch][head_count][R][ntiles][4] per-(row, tile, 32-key quarter) logit max
+    float* logits;      // [batch][head_count][R][nkp] logits of the CUDA-core engine; the per-tile tensor-core engine
+                        // keeps head scores [batch][head_count][nk] here
+    int nkp;            // nk rounded up to 4 (16-byte rows)
+    float* hs;          // [batch][head_count][nk] head scores of the persistent tensor-core engines
     float2* tstats;     // [batch][head_count][R][ntiles]  (tile max, tile sum)
     float2* rstats;     // [batch][head_count][R]          (row max, 1/(sum+1e-9))
     unsigned* counters; // [batch][head_count]
@@ -51,7 +50,7 @@ struct EvictShape {
     int G, obs_w, nk, R, ntiles, target_keep;
     bool keep_all;
     int nkp;
-    size_t off_counters, off_rstats, off_tstats, off_logits, off_keys, off_pooled, off_hs, off_qmax, ws_bytes;
+    size_t off_counters, off_rstats, off_tstats, off_logits, off_keys, off_pooled, off_hs, ws_bytes;
 };
 
 EvictShape evict_shape(const rkv_config& c, int len_q, int len_k, int batch, int head_count);

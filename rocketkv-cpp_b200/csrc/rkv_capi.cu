@@ -121,7 +121,6 @@ EvictArgs make_evict_args(const void* Q, const void* K, int dtype, int len_q, in
     a.logits = reinterpret_cast<float*>(ws + s.off_logits);
     a.nkp = s.nkp;
     a.hs = reinterpret_cast<float*>(ws + s.off_hs);
-    a.qmax = reinterpret_cast<float*>(ws + s.off_qmax);
     a.tstats = reinterpret_cast<float2*>(ws + s.off_tstats);
     a.rstats = reinterpret_cast<float2*>(ws + s.off_rstats);
     a.counters = reinterpret_cast<unsigned*>(ws + s.off_counters);
