@@ -1095,6 +1095,104 @@ __global__ void __launch_bounds__(kSumBuildNT, sizeof(T) == 2 ? 4 : 3) hsa_summa
 // consecutive words of a row (coalesced along the row), and the extrema pass
 // through a [2][D][TP] tile in shared memory to leave as 16-byte runs of a
 // dimension's pages.  Same values as hsa_summary_build_kernel.
+// bf16 rows of 128 values, pages of one or two rows (the headline layout).  A warp takes 16 pages: it reads
+// one page per load instruction (lanes 0-15 the 16 chunks of the first row, lanes 16-31 those of the
+// second), so K is read once in whole lines; one shuffle gives each lane both rows' chunk, and lanes 0-15
+// form the max of x, lanes 16-31 the max of -x of the same eight dimensions (max(first row, second row), as
+// page_extrema).  The warp's extrema pass through its own shared-memory tile, [page pair][summary row],
+// written as 32-byte vectors, and leave as one 32-byte run of pages per summary row and pair of lanes, so
+// every output sector is written whole by one instruction.  Pages from nchunks to npp are written as zeros.
+constexpr int kTilePages = 16;
+__global__ void __launch_bounds__(kSumBuildNT, 3) hsa_summary_build_tile_kernel(const uint8_t* K, long long kv_stride,
+                                                                              int len_k, int C, int Lc, int nchunks,
+                                                                              int npp, uint8_t* summary,
+                                                                              long long sum_stride, long long mask_off) {
+    constexpr int D = 128, RB = D * 2, NR = 2 * D;  // summary rows of an (item, KV head): max x, then max -x
+    extern __shared__ __align__(16) uint32_t tsm[];  // [warp][page pair][NR] words
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int hk = blockIdx.y, b = blockIdx.z;
+    const int p0 = (blockIdx.x * (kSumBuildNT / 32) + warp) * kTilePages;
+    if (p0 >= npp) return;  // warp-uniform
+    const int np = min(kTilePages, npp - p0);  // 16, or 8 at the end (npp is a multiple of 8)
+    const int sg = lane >> 4, c = lane & 15;   // sign (0: max x, 1: max -x) and chunk: dimensions 8c .. 8c + 7
+    uint32_t* wt = tsm + warp * (kTilePages / 2) * NR;
+    const uint8_t* Kh = K + (size_t)b * kv_stride + (size_t)hk * len_k * RB + c * 16;
+    const uint32_t fl = sg ? 0x80008000u : 0u;
+    uint32_t nf = 0u;  // non-finite flags of the lane's eight dimensions
+#pragma unroll 1
+    for (int hb = 0; hb < np / 8; ++hb) {  // eight pages at a time
+        uint4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int p = p0 + 8 * hb + j;
+            v[j] = make_uint4(0u, 0u, 0u, 0u);
+            if (p < nchunks) {
+                const int r0 = p * C, r = r0 + sg < min(r0 + C, Lc) ? r0 + sg : r0;  // a one-row page repeats it
+                v[j] = __ldg(reinterpret_cast<const uint4*>(Kh + (size_t)r * RB));
+            }
+        }
+        uint32_t acc[8][4];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t o[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+                const uint32_t q = __shfl_xor_sync(0xffffffffu, o[w], 16);
+                const uint32_t r0w = sg ? q : o[w], r1w = sg ? o[w] : q;  // the first row first
+                acc[j][w] = Chunk<uint16_t>::wmax(r0w ^ fl, r1w ^ fl);
+            }
+            if (p0 + 8 * hb + j < nchunks) {
+#pragma unroll
+                for (int w = 0; w < 4; ++w)
+#pragma unroll
+                    for (int hf = 0; hf < 2; ++hf) {
+                        const uint32_t x = (acc[j][w] >> (16 * hf)) & 0xffffu;
+                        if ((x & 0x7fffu) > 0x7f80u || x == 0xff80u) nf |= 1u << (2 * w + hf);
+                    }
+            } else {
+#pragma unroll
+                for (int w = 0; w < 4; ++w) acc[j][w] = 0u;  // padding pages
+            }
+        }
+        // page pair m (pages 2m, 2m + 1 of the tile): the words of dimensions 8c .. 8c + 7, two vectors
+#pragma unroll
+        for (int mm = 0; mm < 4; ++mm) {
+            uint32_t wd[8];
+#pragma unroll
+            for (int d = 0; d < 8; ++d)
+                wd[d] = __byte_perm(acc[2 * mm][d >> 1], acc[2 * mm + 1][d >> 1], (d & 1) ? 0x7632u : 0x5410u);
+            uint32_t* dst = wt + (4 * hb + mm) * NR + sg * D + 8 * c;
+            *reinterpret_cast<uint4*>(dst) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+            *reinterpret_cast<uint4*>(dst + 4) = make_uint4(wd[4], wd[5], wd[6], wd[7]);
+        }
+    }
+    __syncwarp();
+    uint16_t* Sb = reinterpret_cast<uint16_t*>(summary + (size_t)b * sum_stride + (size_t)hk * NR * npp * 2);  // [NR][npp]
+    if (np == kTilePages) {  // two lanes per summary row, 16 bytes each: 32 bytes of pages
+#pragma unroll 4
+        for (int r0 = 0; r0 < NR; r0 += 16) {
+            const int row = r0 + (lane >> 1), h = lane & 1;
+            const uint4 o = make_uint4(wt[(4 * h) * NR + row], wt[(4 * h + 1) * NR + row], wt[(4 * h + 2) * NR + row],
+                                       wt[(4 * h + 3) * NR + row]);
+            *reinterpret_cast<uint4*>(Sb + (size_t)row * npp + p0 + 8 * h) = o;
+        }
+    } else {  // the last eight pages: one lane per row
+#pragma unroll 4
+        for (int r0 = 0; r0 < NR; r0 += 32) {
+            const int row = r0 + lane;
+            const uint4 o = make_uint4(wt[row], wt[NR + row], wt[2 * NR + row], wt[3 * NR + row]);
+            *reinterpret_cast<uint4*>(Sb + (size_t)row * npp + p0) = o;
+        }
+    }
+    // flags: lanes c and c + 16 cover the same dimensions; mask word c / 4, bits 8 (c % 4) ..
+    uint32_t* mask = reinterpret_cast<uint32_t*>(summary + (size_t)b * sum_stride + mask_off) + hk * (D / 32);
+#pragma unroll
+    for (int mw = 0; mw < D / 32; ++mw) {
+        const uint32_t m = __reduce_or_sync(0xffffffffu, (c >> 2) == mw ? nf << (8 * (c & 3)) : 0u);
+        if (lane == 0 && m) atomicOr(mask + mw, m);
+    }
+}
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kSumBuildNT) hsa_summary_build_rows_kernel(const uint8_t* K, long long kv_stride,
                                                                          int len_k, int C, int Lc, int nchunks,
@@ -1762,7 +1860,15 @@ static int build_t(const uint8_t* K, int HK, int len_k, long long kv_stride, con
     hsa_summary_mask_clear<<<batch, 128, 0, st>>>(summary, s.item_bytes, s.mask_off, HK * (D / 32));
     constexpr int pages_per_cta = (kSumBuildNT / 32) * kBuildPagesPerWarp;
     dim3 grid((s.npp + pages_per_cta - 1) / pages_per_cta, HK, batch);
-    if (s.C >= 4) {  // long pages: coalesced row reads, extrema transposed through shared memory
+    if (sizeof(T) == 2 && D == 128 && s.C <= 2) {  // bf16 pages of one or two rows: a page per load instruction
+        constexpr int pages_per_cta = (kSumBuildNT / 32) * kTilePages;
+        const size_t smem = (size_t)(kSumBuildNT / 32) * (kTilePages / 2) * 2 * D * sizeof(uint32_t);
+        auto f = hsa_summary_build_tile_kernel;
+        if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return RKV_ERR_CUDA;
+        f<<<dim3((s.npp + pages_per_cta - 1) / pages_per_cta, HK, batch), kSumBuildNT, smem, st>>>(
+            K, kv_stride, len_k, s.C, s.Lc, s.nchunks, s.npp, summary, s.item_bytes, s.mask_off);
+    } else if (s.C >= 4) {  // long pages: coalesced row reads, extrema transposed through shared memory
         const int rowb = D * (int)sizeof(T);
         int TP = 16384 / rowb;
         if (TP > 64) TP = 64;
