@@ -35,7 +35,8 @@
 //               q8_0 window queries likewise;
 //   warps 6-21  epilogue, four groups of four that take the tiles in turn (one
 //               accumulator each); warp w reads lanes 32 (w % 4) .. 32 (w % 4)
-//               + 31, so a thread holds one window row's 128 logits of a tile.
+//               + 31, so a thread holds one window row's 128 logits of a tile
+//               (pass 0) or one key's logits of every window row (pass 1).
 //
 // Two passes over the CTA's tiles (rocket.cpp:91-116).  Pass 0: a thread
 // forms its row's max and sum of exp(l - max) over the tile, l = (q . k) /
@@ -43,9 +44,10 @@
 // head's tile statistics into the row max M_r and inv_r = 1 / (sum_r + 1e-9)
 // (rocket.cpp:108-113).  Pass 1 runs the copies and MMAs again, over the tiles
 // in reverse order (its first tiles are the ones pass 0 read last, still in
-// L2), and writes the head score of every key, sum_r exp(l - M_r) * inv_r, for
-// the pooling kernel: a thread scales its row's logits and each warp sums its
-// 32 rows by shuffles.  Both passes run in one cooperative launch when every
+// L2), with the operands swapped so that the keys sit on the lanes (D[128
+// keys][NP rows] = K_tile . Q^T), and writes the head score of every key,
+// sum_r exp(l - M_r) * inv_r, for the pooling kernel: a thread adds its key's
+// terms in row order, as the reference does.  Both passes run in one cooperative launch when every
 // CTA can be resident: a bounded grid barrier between them holds only the
 // epilogue while the copies and MMAs of pass 1 already run; otherwise one
 // launch per pass.
@@ -85,6 +87,7 @@ struct TcPlan {  // shared-memory offsets from the 1024-byte aligned base, and t
     int NP, nkb, rowb, S, q_atom, qbytes;
     int off_qhi, off_qlo, off_stg, off_epi, off_lo, off_raw, total;
     int nwork, nheads;  // work units (128-key tiles) and (item, KV head) pairs
+    int aligned;        // split the tiles head by head (cta_range)
     int p0, p1;         // the passes this launch runs: 0 = scores and statistics, 1 = head scores
 };
 
@@ -107,8 +110,8 @@ inline TcPlan tc_plan(int kind, int R, int D) {
     if (kind == KIND_Q8) off += align1k(128 * kQ8Row);
     // the MMA reads 128 query rows; rows NP .. 127 fall on what follows the query block (these bytes, the
     // low-part stages or the ring; their accumulator lanes are not used)
-    P.off_epi = off;  // pass 1: per epilogue group, [quarter][key] partial head scores
-    off += kAccs * 4 * 128 * 4;
+    P.off_epi = off;  // pass 1: per epilogue group, the (-M_r, inv_r) of the window rows
+    off += kAccs * 128 * 8;
     P.off_lo = off;
     if (tf32) off += kLoStages * kStageB;
     P.off_raw = off;
@@ -134,6 +137,31 @@ __device__ __forceinline__ void work_unit(const EvictArgs& a, int w, int& b, int
     hc = t % a.head_count;
     b = t / a.head_count;
 }
+
+// The (sequence, KV head) of the work units a role walks through, with the division redone only when a
+// unit leaves the current head's range of tiles: the per-visit loops of the copy and MMA roles are short
+// serial chains, and an integer division by a runtime value is a long dependent sequence in them.
+struct HeadCursor {
+    int head = -1, lo = 0, hi = 0;
+    __device__ __forceinline__ bool has(int w) const { return w >= lo && w < hi; }
+    __device__ __forceinline__ void move(int w, int ntiles) {
+        head = w / ntiles;
+        lo = head * ntiles;
+        hi = lo + ntiles;
+    }
+};
+
+// Slot and phase parity of a ring of n stages, advanced one use at a time (slot = g % n, parity = (g / n) & 1)
+struct StageRing {
+    int s = 0;
+    uint32_t ph = 0;
+    __device__ __forceinline__ void next(int n) {
+        if (++s == n) {
+            s = 0;
+            ph ^= 1u;
+        }
+    }
+};
 
 // 16-byte chunk c of row r of a 128-byte-swizzled operand block
 __device__ __forceinline__ int sw128(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
@@ -180,13 +208,13 @@ __device__ __forceinline__ bool grid_barrier(unsigned* cnt, unsigned n, int* err
     return true;
 }
 
-// This CTA's work units [w0, w0 + nt).  With at least as many CTAs as
-// (item, KV head) pairs every CTA takes tiles of one head only (the CTAs of a
-// head split its tiles evenly), so the resident window queries are loaded once;
-// else contiguous ranges.
+// This CTA's work units [w0, w0 + nt).  Head-aligned split (P.aligned, at least as many CTAs as
+// (item, KV head) pairs): every CTA takes tiles of one head only (the CTAs of a head split its tiles
+// evenly), so the resident window queries are loaded once; else the even split of all tiles into
+// contiguous ranges, a CTA crossing at most a few head boundaries.
 __device__ __forceinline__ void cta_range(const TcPlan& P, int ntiles, int& w0, int& nt) {
     const int G = gridDim.x, c = blockIdx.x;
-    if (P.nheads <= G) {
+    if (P.aligned) {
         const int base = G / P.nheads, extra = G % P.nheads;  // the first `extra` heads get base + 1 CTAs
         int h, j, m;
         if (c < extra * (base + 1)) {
@@ -256,14 +284,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (warp == 0) {
         // ---------------- TMA producer (the whole warp; one elected lane issues) ----------------
         if (TMA) {
-            int issued = 0, qn = 0, prev = -1;
+            int issued = 0, qn = 0, b = 0, hk = 0;
+            HeadCursor cur;
+            StageRing rs;
             bool ok = true;
             for (int i = 0; i < nv && ok; ++i) {
-                int b, hc, tile;
-                work_unit(a, wof(i), b, hc, tile);
-                const int hk = a.head_begin + hc;
-                const int head = wof(i) / a.ntiles;
-                if (head != prev) {  // the window rows of this KV head's query group (rocket.cpp:85-90)
+                const int w = wof(i);
+                if (!cur.has(w)) {  // the window rows of this KV head's query group (rocket.cpp:85-90)
+                    cur.move(w, a.ntiles);
+                    hk = a.head_begin + cur.head % a.head_count;
+                    b = cur.head / a.head_count;
                     if (qn > 0 && !__all_sync(0xffffffffu, mbar_wait_or_abort(B.q_empty, (uint32_t)((qn - 1) & 1), a.err, abort_flag)))
                         break;
                     mbar_arrive_expect_tx_w(B.q_raw, (uint32_t)P.qbytes);
@@ -272,19 +302,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                             tma_load_4d_w(sm + P.off_qhi + kb * P.q_atom + g * a.obs_w * 128, &tmq, kb * (128 / EB),
                                           a.q_row0, hk * a.G + g, b, B.q_raw);
                     ++qn;
-                    prev = head;
                 }
-                const int y = hk * a.k_head_rows + tile * kMmaM;
+                const int y = hk * a.k_head_rows + (w - cur.lo) * kMmaM;
                 for (int kb = 0; kb < P.nkb; ++kb) {
-                    const int g = i * P.nkb + kb, s = g % S;
-                    if (g >= S && !__all_sync(0xffffffffu, mbar_wait_or_abort(&B.raw_empty[s], (uint32_t)(((g / S) + 1) & 1),
-                                                                                a.err, abort_flag))) {
+                    const int s = rs.s;
+                    if (issued >= S &&
+                        !__all_sync(0xffffffffu, mbar_wait_or_abort(&B.raw_empty[s], rs.ph ^ 1u, a.err, abort_flag))) {
                         ok = false;
                         break;
                     }
                     mbar_arrive_expect_tx_w(&B.raw_full[s], kStageB);
                     tma_load_3d_w(sm + P.off_raw + s * kStageB, &tmk, kb * (128 / EB), y, b, &B.raw_full[s]);
                     ++issued;
+                    rs.next(S);
                 }
             }
             // every copy issued lands before the CTA can exit
@@ -296,15 +326,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer (the whole warp; one elected lane issues) ----------------
         {
-            const uint32_t idesc = mma_idesc(TF32 ? 2u : 1u, (uint32_t)kMmaM);  // M = 128 query rows, N = 128 keys
-            int qn = 0, prev = -1;
+            // pass 0: D[128 query-row lanes][128 keys] = Q . K_tile^T; pass 1: D[128 key lanes][NP query rows] =
+            // K_tile . Q^T (the same products with the operands swapped)
+            const uint32_t idesc0 = mma_idesc(TF32 ? 2u : 1u, (uint32_t)kMmaM);
+            const uint32_t idesc1 = mma_idesc(TF32 ? 2u : 1u, (uint32_t)P.NP);
+            int qn = 0;
+            HeadCursor cur;
+            StageRing rs;
             bool ok = true;
             for (int i = 0; i < nv && ok; ++i) {
-                const int head = wof(i) / a.ntiles;
-                if (head != prev) {
+                const int w = wof(i);
+                if (!cur.has(w)) {
                     if (!__all_sync(0xffffffffu, mbar_wait_or_abort(B.q_full, (uint32_t)(qn & 1), a.err, abort_flag))) break;
                     ++qn;
-                    prev = head;
+                    cur.move(w, a.ntiles);
                 }
                 const int ab = i % kAccs;
                 if (i >= kAccs && !__all_sync(0xffffffffu, mbar_wait_or_abort(&B.acc_empty[ab], (uint32_t)(((i / kAccs) + 1) & 1),
@@ -313,10 +348,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 tc_fence_after();
                 const uint32_t dacc = tbase + (uint32_t)(ab * kAccCols);
                 for (int kb = 0; kb < P.nkb; ++kb) {
-                    const int g = i * P.nkb + kb, s = g % S, l = g % kLoStages;
-                    const bool w = TF32 ? mbar_wait_or_abort(&B.lo_full[l], (uint32_t)((g / kLoStages) & 1), a.err, abort_flag)
-                                        : mbar_wait_or_abort(&B.raw_full[s], (uint32_t)((g / S) & 1), a.err, abort_flag);
-                    if (!__all_sync(0xffffffffu, w)) {
+                    const int g = i * P.nkb + kb, s = rs.s, l = g % kLoStages;
+                    const bool landed = TF32 ? mbar_wait_or_abort(&B.lo_full[l], (uint32_t)((g / kLoStages) & 1), a.err, abort_flag)
+                                             : mbar_wait_or_abort(&B.raw_full[s], rs.ph, a.err, abort_flag);
+                    if (!__all_sync(0xffffffffu, landed)) {
                         ok = false;
                         break;
                     }
@@ -330,20 +365,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     // a K step of 32 bytes adds 2 to the descriptors' start-address field
                     const uint64_t dKh = mma_desc_sw128(kh), dKl = mma_desc_sw128(kl);
                     const uint64_t dQh = mma_desc_sw128(qh), dQl = mma_desc_sw128(ql);
+                    const bool keys_on_lanes = i >= nv0;
+                    const uint32_t idesc = keys_on_lanes ? idesc1 : idesc0;
+                    auto mma = [&](uint64_t dq, uint64_t dk, uint32_t acc) {
+                        mma_issue_w<TF32>(dacc, keys_on_lanes ? dk : dq, keys_on_lanes ? dq : dk, idesc, acc);
+                    };
                     for (int st = 0; st < steps; ++st) {
                         const uint64_t o = (uint64_t)(2 * st);
-                        mma_issue_w<TF32>(dacc, dQh + o, dKh + o, idesc, (kb | st) ? 1u : 0u);
+                        mma(dQh + o, dKh + o, (kb | st) ? 1u : 0u);
                         if (TF32) {
-                            mma_issue_w<TF32>(dacc, dQl + o, dKh + o, idesc, 1u);
-                            mma_issue_w<TF32>(dacc, dQh + o, dKl + o, idesc, 1u);
+                            mma(dQl + o, dKh + o, 1u);
+                            mma(dQh + o, dKl + o, 1u);
                         }
                     }
                     mma_commit_w(&B.raw_empty[s]);
                     if (TF32) mma_commit_w(&B.lo_empty[l]);
+                    rs.next(S);
                 }
                 if (!ok) break;
                 mma_commit_w(&B.acc_full[ab]);
-                if (i + 1 == nv || wof(i + 1) / a.ntiles != head) mma_commit_w(B.q_empty);
+                if (i + 1 == nv || !cur.has(wof(i + 1))) mma_commit_w(B.q_empty);
             }
             // every MMA issued completes before the tensor memory is freed
             mma_commit_w(B.mma_done);
@@ -354,6 +395,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // ---------------- operand converters ----------------
         const int ct = tid - 64;
         int qn = 0, prev = -1;
+        StageRing rs;
         uint8_t* qhi = sm + P.off_qhi;
         uint8_t* qlo = sm + P.off_qlo;
         // the padding rows R .. NP-1 of the query blocks stay zero
@@ -452,15 +494,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (i + 1 < nv) q8_fetch(i + 1);
             }
             bool ok = true;
-            for (int kb = 0; kb < P.nkb; ++kb) {
-                const int g = i * P.nkb + kb, s = g % S, l = g % kLoStages;
+            for (int kb = 0; kb < P.nkb; ++kb, rs.next(S)) {
+                const int g = i * P.nkb + kb, s = rs.s, l = g % kLoStages;
                 uint8_t* raw = sm + P.off_raw + s * kStageB;
                 uint8_t* lo = sm + P.off_lo + l * kStageB;
                 bool w = true;
                 if (KIND == KIND_F32)
-                    w = mbar_wait_or_abort(&B.raw_full[s], (uint32_t)((g / S) & 1), a.err, abort_flag);
+                    w = mbar_wait_or_abort(&B.raw_full[s], rs.ph, a.err, abort_flag);
                 else if (g >= S)
-                    w = mbar_wait_or_abort(&B.raw_empty[s], (uint32_t)(((g / S) + 1) & 1), a.err, abort_flag);
+                    w = mbar_wait_or_abort(&B.raw_empty[s], rs.ph ^ 1u, a.err, abort_flag);
                 if (w && g >= kLoStages)
                     w = mbar_wait_or_abort(&B.lo_empty[l], (uint32_t)(((g / kLoStages) + 1) & 1), a.err, abort_flag);
                 if (!group_all(kBarConv, 128, w)) {
@@ -490,16 +532,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
     } else {
         // ---------------- epilogue ----------------
-        // Window rows on the tensor-memory lanes, keys on the columns: a thread holds one row's logits of
-        // a tile.  Four groups of four warps take the visits in turn (group g the ones on accumulator g);
-        // warp w of a group reads lanes 32 (w % 4) .. 32 (w % 4) + 31, its rows.
-        const int ep = warp - 6, grp = ep >> 2, q = warp & 3, gt = (ep & 3) * 32 + lane;
-        const int r = q * 32 + lane;  // this thread's window row
+        // Four groups of four warps take the visits in turn (group g the ones on accumulator g); warp w of
+        // a group reads tensor-memory lanes 32 (w % 4) .. 32 (w % 4) + 31.  Pass 0 has the window rows on
+        // the lanes (a thread holds one row's logits of a tile), pass 1 the keys (one key's logits of
+        // every row).
+        const int ep = warp - 6, grp = ep >> 2, q = warp & 3;
+        const int r = q * 32 + lane;  // this thread's lane: its window row in pass 0, its key in pass 1
         const bool row_ok = r < a.R;
-        // rows of this warp: all valid, none (padding), or some (a per-lane select)
+        // rows of this warp in pass 0: all valid, none (padding), or some (a per-lane select)
         const int wmode = q * 32 + 32 <= a.R ? 0 : q * 32 >= a.R ? 1 : 2;
         const int gbar = kBarGrp + grp;
-        float* red = reinterpret_cast<float*>(sm + P.off_epi) + grp * 4 * 128;  // pass 1: [quarter][key]
         const uint32_t tacc = tbase + (uint32_t)(grp * kAccCols) + ((uint32_t)(q * 32) << 16);
         bool ok = true;
         // ---- pass 0: per-(row, tile) max and sum of exp(l - max) (rocket.cpp:91-107)
@@ -601,11 +643,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
         }
         // ---- pass 1: head scores sum_r exp(l - M_r) * inv_r (rocket.cpp:114-116), the logits computed
-        // again.  A thread scales its row's 32 logits of a chunk, and the warp sums its 32 rows by
-        // recursive halving (lane l ends with key l of the chunk); the four warps' sums are added in
-        // quarter order.  Padding rows: M = FLT_MAX and inv = 0 (terms exactly 0).
+        // again with the keys on the tensor-memory lanes (D[128 keys][NP rows] = K_tile . Q^T): a thread
+        // holds one key's logits of every window row and adds the terms in row order, as the reference
+        // does, with no exchange between threads.  The rows' (-M_r, inv_r) sit in shared memory, one copy
+        // per epilogue group, rewritten when the group's tiles move to another KV head.
+        float2* rst = reinterpret_cast<float2*>(sm + P.off_epi) + grp * 128;
+        const int nch = (a.R + 31) >> 5;  // 32-row chunks of the accumulator
         int prev = -1;
-        float Mr = FLT_MAX, ir = 0.0f;
         for (int v = nv0 + (grp - nv0 % kAccs + kAccs) % kAccs; ok && v < nv; v += kAccs) {
             int b, hc, tile;
             work_unit(a, wof(v), b, hc, tile);
@@ -613,22 +657,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int k0 = tile * kMmaM, nkeys = min(kMmaM, a.nk - k0);
             const size_t row_base = ((size_t)b * a.head_count + hc) * a.R;
             if (head != prev) {
+                group_sync(gbar, 128);  // the group is done with the previous head's rows
                 if (one_launch) {
-                    const float2 x = row_ok ? __ldcg(a.rstats + row_base + r) : make_float2(FLT_MAX, 0.0f);
-                    Mr = x.x;
-                    ir = x.y;
+                    if (r < a.R) {
+                        const float2 x = __ldcg(a.rstats + row_base + r);
+                        rst[r] = make_float2(-x.x, x.y);
+                    }
                 } else {
-                    Mr = FLT_MAX;
-                    ir = 0.0f;
                     for (int rr = 0; rr < 32 && q * 32 + rr < a.R; ++rr) {  // warp-uniform bound
                         float M, inv;
                         fold_row(row_base + q * 32 + rr, M, inv);
-                        if (lane == rr) {
-                            Mr = M;
-                            ir = inv;
-                        }
+                        if (lane == 0) rst[q * 32 + rr] = make_float2(-M, inv);
                     }
                 }
+                group_sync(gbar, 128);
                 prev = head;
             }
             const bool w = mbar_wait_or_abort(&B.acc_full[grp], (uint32_t)((v / kAccs) & 1), a.err, abort_flag);
@@ -637,45 +679,34 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 break;
             }
             tc_fence_after();
-            float* rq = red + q * 128;
-            if (wmode == 1) {
-#pragma unroll
-                for (int c = 0; c < 4; ++c) rq[c * 32 + lane] = 0.0f;
-            } else {
+            float hsum = 0.0f;
 #pragma unroll 1
-                for (int c = 0; c < 4; ++c) {
-                    float x[32];
-                    tmem_ld32(tacc + (uint32_t)(c * 32), x);
+            for (int c = 0; c < nch; ++c) {
+                float x[32];
+                tmem_ld32(tacc + (uint32_t)(c * 32), x);
+                if (c + 1 == nch) {  // every logit of the tile is in registers: the accumulator is free
+                    tc_fence_before();
+                    mbar_arrive1(&B.acc_empty[grp]);
+                }
+                const float4* rs4 = reinterpret_cast<const float4*>(rst + c * 32);
+                auto terms = [&](auto full) {
 #pragma unroll
                     for (int j = 0; j < 32; j += 2) {
+                        if (!decltype(full)::value && c * 32 + j >= a.R) break;
+                        const float4 st = rs4[j >> 1];  // (-M_r, inv_r, -M_r+1, inv_r+1)
                         const float2 l = __fmul2_rn(make_float2(x[j], x[j + 1]), make_float2(a.inv_sqrt_d, a.inv_sqrt_d));
-                        const float2 e = mufu_expf2(__fadd2_rn(l, make_float2(-Mr, -Mr)));
-                        x[j] = e.x * ir;
-                        x[j + 1] = e.y * ir;
-                        if (wmode == 2 && !row_ok) x[j] = x[j + 1] = 0.0f;  // the logits of padding rows are not finite-safe
+                        const float2 e = mufu_expf2(__fadd2_rn(l, make_float2(st.x, st.z)));
+                        hsum = __fadd_rn(hsum, __fmul_rn(e.x, st.y));
+                        if (!decltype(full)::value && c * 32 + j + 1 >= a.R) break;
+                        hsum = __fadd_rn(hsum, __fmul_rn(e.y, st.w));
                     }
-                    // recursive halving over the lanes: after the step of offset o a lane keeps the half of
-                    // its columns selected by bit o of its lane index and adds its partner's copy of it
-#pragma unroll
-                    for (int o = 16, n = 16; o >= 1; o >>= 1, n >>= 1) {
-                        const bool up = (lane & o) != 0;
-#pragma unroll
-                        for (int j = 0; j < n; ++j) {
-                            const float send = up ? x[j] : x[j + n];
-                            const float keep = up ? x[j + n] : x[j];
-                            x[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-                        }
-                    }
-                    rq[c * 32 + lane] = x[0];
-                }
+                };
+                if (c * 32 + 32 <= a.R)
+                    terms(std::true_type{});
+                else
+                    terms(std::false_type{});
             }
-            tc_fence_before();
-            mbar_arrive1(&B.acc_empty[grp]);
-            group_sync(gbar, 128);
-            if (gt < nkeys)
-                a.hs[((size_t)b * a.head_count + hc) * a.nk + k0 + gt] =
-                    ((red[gt] + red[128 + gt]) + red[256 + gt]) + red[384 + gt];
-            group_sync(gbar, 128);
+            if (r < nkeys) a.hs[((size_t)b * a.head_count + hc) * a.nk + k0 + r] = hsum;
         }
     }
 
@@ -744,6 +775,13 @@ int launch_kind(const EvictArgs& a, int batch, cudaStream_t st) {
     const int sms = sm_count();
     if (sms <= 0) return RKV_ERR_CUDA;
     const int grid = P.nwork < sms ? P.nwork : sms;
+    // the head-aligned split unless it leaves some CTA more tiles than the even split would (64 heads of
+    // 1024 tiles over 148 CTAs: 512 against 443)
+    P.aligned = 0;
+    if (P.nheads <= grid) {
+        const int base = grid / P.nheads;
+        P.aligned = (a.ntiles + base - 1) / base <= (P.nwork + grid - 1) / grid;
+    }
     CUtensorMap tk, tq;
     memset(&tk, 0, sizeof(tk));
     memset(&tq, 0, sizeof(tq));

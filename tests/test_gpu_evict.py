@@ -152,6 +152,38 @@ def test_stage1_recompute_form(kind, cuda):
     assert rkv.lib().rkv_workspace_status(rkv._ptr(ev.ws), 0) == 0
 
 
+@pytest.mark.parametrize("kind", ["f32", "bf16"])
+def test_stage1_even_split_crosses_heads(kind, cuda):
+    """8 sequences x 8 KV heads of 20 key tiles: the head-aligned split would
+    give some CTAs 10 tiles, so the persistent scorer splits all 1280 tiles
+    evenly (at most 9 per CTA) and CTAs cross from one KV head (and sequence)
+    to the next, reloading the window queries and the row statistics: kept
+    indices equal the oracle's for every sequence, on both engines."""
+    import torch
+    cfg = O.Config(num_heads=24, num_heads_kv=8, dim_head=128, prompt_budget=300)
+    nb, len_k = 8, 2560
+    Qs, Ks, wants = [], [], []
+    for b in range(nb):
+        Q, K = rkvgen.stage1_inputs(300 + b, 24, 8, 128, 32, len_k)
+        if kind == "bf16":
+            Q, K = rkvgen.bf16_round(Q), rkvgen.bf16_round(K)
+        wants.append(O.prefill_eviction(Q, K, 32, len_k, cfg, want_total=True))
+        Qs.append(rkvgen.bf16_bits(Q) if kind == "bf16" else Q)
+        Ks.append(rkvgen.bf16_bits(K) if kind == "bf16" else K)
+    Qt = torch.stack([dev(q, kind, cuda) for q in Qs]).contiguous()
+    Kt = torch.stack([dev(k, kind, cuda) for k in Ks]).contiguous()
+    ev = rkv.Evictor(to_rkv(cfg), 32, len_k, nb, KIND[kind], cuda)
+    for eng in (rkv.ENGINE_TENSOR, rkv.ENGINE_SIMT):
+        k, n = ev(Qt, Kt, engine=eng)
+        torch.cuda.synchronize()
+        for b in range(nb):
+            want, total = wants[b]
+            got = k[b, : int(n[b])].cpu().numpy()
+            assert len(got) == 300
+            assert np.array_equal(got, want), (eng, b, boundary_report(total, got, want))
+    assert rkv.lib().rkv_workspace_status(rkv._ptr(ev.ws), 0) == 0
+
+
 def test_stage1_config0_full_size(cuda):
     """K [8, 8192, 128] fp32, Q [24, 32, 128] window, budget 1024, ks 63."""
     cfg = O.Config(num_heads=24, num_heads_kv=8, dim_head=128, prompt_budget=1024)
