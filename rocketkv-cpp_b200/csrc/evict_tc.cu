@@ -24,12 +24,14 @@
 //               resident query block) and one copy per k-block of 128 key
 //               rows into a ring of 16 KB stages;
 //   warp 1      allocates tensor memory; issues the MMAs and the
-//               tcgen05.commit arrivals that release stages and accumulators.
+//               tcgen05.commit arrivals that release stages and accumulators
+//               (bf16: warps 1 and 2, taking the tiles in turn).
 //               Warps 0 and 1 run their loops converged and one lane, picked
 //               by elect.sync inside each issuing statement, issues: the
 //               operands stay warp-uniform, which keeps the issue of a copy or
 //               an MMA at a few cycles instead of ~100 (measured);
-//   warps 2-5   operand converters: lo = x - hi of every fp32 k-block and
+//   warps 2-5   operand converters (3-5 for bf16, which only forwards the
+//               window queries' arrival): lo = x - hi of every fp32 k-block and
 //               query block; q8_0 tiles loaded with coalesced 8-byte loads and
 //               dequantised exactly to fp32 in shared memory (x and lo), the
 //               q8_0 window queries likewise;
@@ -240,6 +242,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     constexpr bool TF32 = KIND != KIND_BF16;
     constexpr bool TMA = KIND != KIND_Q8;
     constexpr int EB = KIND == KIND_BF16 ? 2 : 4;
+    // MMA issuers: bf16 needs no operand conversion, so warp 2 joins warp 1 and the two take the visits
+    // in turn (one issuer's waits, fences and commits overlap the other's MMAs); fp32 and q8_0 keep all
+    // four converter warps and one issuer
+    constexpr int kIssuers = TF32 ? 1 : 2;
+    constexpr int kConv = 128 - 32 * (kIssuers - 1);  // converter threads
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const Bars B = bars_of(sm);
@@ -268,9 +275,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_init(&B.acc_full[i], 1);
             mbar_init(&B.acc_empty[i], 128);  // the epilogue group of this accumulator
         }
-        mbar_init(B.q_full, 128);
-        mbar_init(B.q_empty, 1);
-        mbar_init(B.mma_done, 1);
+        mbar_init(B.q_full, kConv);
+        mbar_init(B.q_empty, kIssuers);
+        mbar_init(B.mma_done, kIssuers);
         mbar_init(B.q_raw, 1);
         *abort_flag = 0;
         fence_mbar_init();
@@ -323,9 +330,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (qn > 0) mbar_wait_bounded(B.q_raw, (uint32_t)((qn - 1) & 1), a.err);
         }
         __syncwarp();
-    } else if (warp == 1) {
-        // ---------------- MMA issuer (the whole warp; one elected lane issues) ----------------
+    } else if (warp < 1 + kIssuers) {
+        // ---------------- MMA issuers (whole warps; one elected lane issues) ----------------
+        // Issuer j takes the visits i with i % kIssuers == j; every issuer walks all visits to follow the
+        // stage ring and the KV heads (it waits for each head's window queries and releases them once
+        // its own MMAs on the head are issued, so q_empty completes when every issuer has done so).
         {
+            const int iss = warp - 1;
             // pass 0: D[128 query-row lanes][128 keys] = Q . K_tile^T; pass 1: D[128 key lanes][NP query rows] =
             // K_tile . Q^T (the same products with the operands swapped)
             const uint32_t idesc0 = mma_idesc(TF32 ? 2u : 1u, (uint32_t)kMmaM);
@@ -341,49 +352,53 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     ++qn;
                     cur.move(w, a.ntiles);
                 }
-                const int ab = i % kAccs;
-                if (i >= kAccs && !__all_sync(0xffffffffu, mbar_wait_or_abort(&B.acc_empty[ab], (uint32_t)(((i / kAccs) + 1) & 1),
-                                                                             a.err, abort_flag)))
-                    break;
-                tc_fence_after();
-                const uint32_t dacc = tbase + (uint32_t)(ab * kAccCols);
-                for (int kb = 0; kb < P.nkb; ++kb) {
-                    const int g = i * P.nkb + kb, s = rs.s, l = g % kLoStages;
-                    const bool landed = TF32 ? mbar_wait_or_abort(&B.lo_full[l], (uint32_t)((g / kLoStages) & 1), a.err, abort_flag)
-                                             : mbar_wait_or_abort(&B.raw_full[s], rs.ph, a.err, abort_flag);
-                    if (!__all_sync(0xffffffffu, landed)) {
-                        ok = false;
+                if (i % kIssuers == iss) {
+                    const int ab = i % kAccs;
+                    if (i >= kAccs && !__all_sync(0xffffffffu, mbar_wait_or_abort(&B.acc_empty[ab], (uint32_t)(((i / kAccs) + 1) & 1),
+                                                                                 a.err, abort_flag)))
                         break;
-                    }
                     tc_fence_after();
-                    const uint32_t kh = smem_u32(sm + P.off_raw + s * kStageB);
-                    const uint32_t kl = smem_u32(sm + P.off_lo + l * kStageB);
-                    const uint32_t qh = smem_u32(sm + P.off_qhi + kb * P.q_atom);
-                    const uint32_t ql = smem_u32(sm + P.off_qlo + kb * P.q_atom);
-                    const int rem = (P.rowb - kb * 128) / 32;
-                    const int steps = rem < 4 ? rem : 4;
-                    // a K step of 32 bytes adds 2 to the descriptors' start-address field
-                    const uint64_t dKh = mma_desc_sw128(kh), dKl = mma_desc_sw128(kl);
-                    const uint64_t dQh = mma_desc_sw128(qh), dQl = mma_desc_sw128(ql);
-                    const bool keys_on_lanes = i >= nv0;
-                    const uint32_t idesc = keys_on_lanes ? idesc1 : idesc0;
-                    auto mma = [&](uint64_t dq, uint64_t dk, uint32_t acc) {
-                        mma_issue_w<TF32>(dacc, keys_on_lanes ? dk : dq, keys_on_lanes ? dq : dk, idesc, acc);
-                    };
-                    for (int st = 0; st < steps; ++st) {
-                        const uint64_t o = (uint64_t)(2 * st);
-                        mma(dQh + o, dKh + o, (kb | st) ? 1u : 0u);
-                        if (TF32) {
-                            mma(dQl + o, dKh + o, 1u);
-                            mma(dQh + o, dKl + o, 1u);
+                    const uint32_t dacc = tbase + (uint32_t)(ab * kAccCols);
+                    for (int kb = 0; kb < P.nkb; ++kb) {
+                        const int g = i * P.nkb + kb, s = rs.s, l = g % kLoStages;
+                        const bool landed = TF32 ? mbar_wait_or_abort(&B.lo_full[l], (uint32_t)((g / kLoStages) & 1), a.err, abort_flag)
+                                                 : mbar_wait_or_abort(&B.raw_full[s], rs.ph, a.err, abort_flag);
+                        if (!__all_sync(0xffffffffu, landed)) {
+                            ok = false;
+                            break;
                         }
+                        tc_fence_after();
+                        const uint32_t kh = smem_u32(sm + P.off_raw + s * kStageB);
+                        const uint32_t kl = smem_u32(sm + P.off_lo + l * kStageB);
+                        const uint32_t qh = smem_u32(sm + P.off_qhi + kb * P.q_atom);
+                        const uint32_t ql = smem_u32(sm + P.off_qlo + kb * P.q_atom);
+                        const int rem = (P.rowb - kb * 128) / 32;
+                        const int steps = rem < 4 ? rem : 4;
+                        // a K step of 32 bytes adds 2 to the descriptors' start-address field
+                        const uint64_t dKh = mma_desc_sw128(kh), dKl = mma_desc_sw128(kl);
+                        const uint64_t dQh = mma_desc_sw128(qh), dQl = mma_desc_sw128(ql);
+                        const bool keys_on_lanes = i >= nv0;
+                        const uint32_t idesc = keys_on_lanes ? idesc1 : idesc0;
+                        auto mma = [&](uint64_t dq, uint64_t dk, uint32_t acc) {
+                            mma_issue_w<TF32>(dacc, keys_on_lanes ? dk : dq, keys_on_lanes ? dq : dk, idesc, acc);
+                        };
+                        for (int st = 0; st < steps; ++st) {
+                            const uint64_t o = (uint64_t)(2 * st);
+                            mma(dQh + o, dKh + o, (kb | st) ? 1u : 0u);
+                            if (TF32) {
+                                mma(dQl + o, dKh + o, 1u);
+                                mma(dQh + o, dKl + o, 1u);
+                            }
+                        }
+                        mma_commit_w(&B.raw_empty[s]);
+                        if (TF32) mma_commit_w(&B.lo_empty[l]);
+                        rs.next(S);
                     }
-                    mma_commit_w(&B.raw_empty[s]);
-                    if (TF32) mma_commit_w(&B.lo_empty[l]);
-                    rs.next(S);
+                    if (!ok) break;
+                    mma_commit_w(&B.acc_full[ab]);
+                } else {
+                    for (int kb = 0; kb < P.nkb; ++kb) rs.next(S);  // the other issuer's stages
                 }
-                if (!ok) break;
-                mma_commit_w(&B.acc_full[ab]);
                 if (i + 1 == nv || !cur.has(wof(i + 1))) mma_commit_w(B.q_empty);
             }
             // every MMA issued completes before the tensor memory is freed
@@ -393,13 +408,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         __syncwarp();
     } else if (warp < 6) {
         // ---------------- operand converters ----------------
-        const int ct = tid - 64;
+        const int ct = tid - 32 * (1 + kIssuers);
         int qn = 0, prev = -1;
         StageRing rs;
         uint8_t* qhi = sm + P.off_qhi;
         uint8_t* qlo = sm + P.off_qlo;
         // the padding rows R .. NP-1 of the query blocks stay zero
-        for (int p = ct; p < P.nkb * (P.NP - a.R) * 8; p += 128) {
+        for (int p = ct; p < P.nkb * (P.NP - a.R) * 8; p += kConv) {
             const int kb = p / ((P.NP - a.R) * 8), u = p % ((P.NP - a.R) * 8);
             const int off = kb * P.q_atom + a.R * 128 + u * 16;
             *reinterpret_cast<uint4*>(qhi + off) = make_uint4(0u, 0u, 0u, 0u);
@@ -430,7 +445,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (TMA) {
                     // the producer's query copies have landed: the low parts of fp32 rows
                     const bool ok = mbar_wait_or_abort(B.q_raw, (uint32_t)(qn & 1), a.err, abort_flag);
-                    if (!group_all(kBarConv, 128, ok)) break;
+                    if (!group_all(kBarConv, kConv, ok)) break;
                     if (TF32) {
                         const int per = a.R * 8;  // 16-byte units of the window rows in one query block
                         for (int p0 = 0; p0 < P.nkb * per; p0 += 8 * 128) {
@@ -451,7 +466,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                 } else {
                     const bool ok = qn == 0 || mbar_wait_or_abort(B.q_empty, (uint32_t)((qn - 1) & 1), a.err, abort_flag);
-                    if (!group_all(kBarConv, 128, ok)) break;
+                    if (!group_all(kBarConv, kConv, ok)) break;
                     // q8_0 window rows: every load of a round in flight first (rocket.cpp:85-90)
                     const int hk = a.head_begin + hc;
                     const uint8_t* Qb = a.Q + (size_t)b * a.q_stride;
@@ -490,7 +505,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 uint2* stg = reinterpret_cast<uint2*>(sm + P.off_stg);
 #pragma unroll
                 for (int j = 0; j < kQ8Words; ++j) stg[ct + 128 * j] = pre[j];
-                group_sync(kBarConv, 128);
+                group_sync(kBarConv, kConv);
                 if (i + 1 < nv) q8_fetch(i + 1);
             }
             bool ok = true;
@@ -505,7 +520,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     w = mbar_wait_or_abort(&B.raw_empty[s], rs.ph ^ 1u, a.err, abort_flag);
                 if (w && g >= kLoStages)
                     w = mbar_wait_or_abort(&B.lo_empty[l], (uint32_t)(((g / kLoStages) + 1) & 1), a.err, abort_flag);
-                if (!group_all(kBarConv, 128, w)) {
+                if (!group_all(kBarConv, kConv, w)) {
                     ok = false;
                     break;
                 }
@@ -528,7 +543,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 mbar_arrive1(&B.lo_full[l]);
             }
             if (!ok) break;
-            if (KIND == KIND_Q8) group_sync(kBarConv, 128);  // the staging area is refilled next
+            if (KIND == KIND_Q8) group_sync(kBarConv, kConv);  // the staging area is refilled next
         }
     } else {
         // ---------------- epilogue ----------------
