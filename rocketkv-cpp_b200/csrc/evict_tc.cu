@@ -661,8 +661,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // again with the keys on the tensor-memory lanes (D[128 keys][NP rows] = K_tile . Q^T): a thread
         // holds one key's logits of every window row and adds the terms in row order, as the reference
         // does, with no exchange between threads.  The rows' (-M_r, inv_r) sit in shared memory, one copy
-        // per epilogue group, rewritten when the group's tiles move to another KV head.
-        float2* rst = reinterpret_cast<float2*>(sm + P.off_epi) + grp * 128;
+        // per epilogue group, rewritten when the group's tiles move to another KV head, as one float4 per
+        // row pair (-M_2i, -M_2i+1, inv_2i, inv_2i+1): each half is the paired operand of one instruction.
+        float* rst = reinterpret_cast<float*>(sm + P.off_epi) + grp * 256;
+        auto put_row = [&](int row, float M, float inv) {
+            rst[4 * (row >> 1) + (row & 1)] = -M;
+            rst[4 * (row >> 1) + 2 + (row & 1)] = inv;
+        };
         const int nch = (a.R + 31) >> 5;  // 32-row chunks of the accumulator
         int prev = -1;
         for (int v = nv0 + (grp - nv0 % kAccs + kAccs) % kAccs; ok && v < nv; v += kAccs) {
@@ -676,13 +681,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (one_launch) {
                     if (r < a.R) {
                         const float2 x = __ldcg(a.rstats + row_base + r);
-                        rst[r] = make_float2(-x.x, x.y);
+                        put_row(r, x.x, x.y);
                     }
                 } else {
                     for (int rr = 0; rr < 32 && q * 32 + rr < a.R; ++rr) {  // warp-uniform bound
                         float M, inv;
                         fold_row(row_base + q * 32 + rr, M, inv);
-                        if (lane == 0) rst[q * 32 + rr] = make_float2(-M, inv);
+                        if (lane == 0) put_row(q * 32 + rr, M, inv);
                     }
                 }
                 group_sync(gbar, 128);
@@ -703,17 +708,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     tc_fence_before();
                     mbar_arrive1(&B.acc_empty[grp]);
                 }
-                const float4* rs4 = reinterpret_cast<const float4*>(rst + c * 32);
+                const float4* rs4 = reinterpret_cast<const float4*>(rst + c * 64);
                 auto terms = [&](auto full) {
 #pragma unroll
                     for (int j = 0; j < 32; j += 2) {
                         if (!decltype(full)::value && c * 32 + j >= a.R) break;
-                        const float4 st = rs4[j >> 1];  // (-M_r, inv_r, -M_r+1, inv_r+1)
+                        const float4 st = rs4[j >> 1];  // (-M_r, -M_r+1, inv_r, inv_r+1)
                         const float2 l = __fmul2_rn(make_float2(x[j], x[j + 1]), make_float2(a.inv_sqrt_d, a.inv_sqrt_d));
-                        const float2 e = mufu_expf2(__fadd2_rn(l, make_float2(st.x, st.z)));
-                        hsum = __fadd_rn(hsum, __fmul_rn(e.x, st.y));
+                        const float2 e = mufu_expf2(__fadd2_rn(l, make_float2(st.x, st.y)));
+                        const float2 t = __fmul2_rn(e, make_float2(st.z, st.w));
+                        hsum = __fadd_rn(hsum, t.x);
                         if (!decltype(full)::value && c * 32 + j + 1 >= a.R) break;
-                        hsum = __fadd_rn(hsum, __fmul_rn(e.y, st.w));
+                        hsum = __fadd_rn(hsum, t.y);
                     }
                 };
                 if (c * 32 + 32 <= a.R)
