@@ -140,6 +140,18 @@ __device__ __forceinline__ void work_unit(const EvictArgs& a, int w, int& b, int
     b = t / a.head_count;
 }
 
+// exp(l - M) for two logits as 2^(x s2 - M log2 e), x the raw accumulator and s2 = log2(e) / sqrt(D): one
+// fused multiply-add and the MUFU ex2 per value.  Its error is a few ulp of the exponent (t <= 0, relative
+// error about |t| 2^-23) plus the rounding of M log2 e, a factor shared by every term of one (row, tile)
+// sum or of one row's head-score terms; both lie far below the logits' own error (the fp32 accumulation of
+// the dot product, and for fp32 operands the three TF32 products).  nm2 = -(M log2 e), kept finite so
+// that an all -inf row gives 0, as exp(-inf - M) does.
+__device__ __forceinline__ float neg_m2(float M) { return -fmaxf(M * 1.44269504088896341f, -FLT_MAX); }
+__device__ __forceinline__ float2 exp2_pair(float x0, float x1, float s2, float2 nm2) {
+    const float2 t = __ffma2_rn(make_float2(x0, x1), make_float2(s2, s2), nm2);
+    return make_float2(ex2_approx(t.x), ex2_approx(t.y));
+}
+
 // The (sequence, KV head) of the work units a role walks through, with the division redone only when a
 // unit leaves the current head's range of tiles: the per-visit loops of the copy and MMA roles are short
 // serial chains, and an integer division by a runtime value is a long dependent sequence in them.
@@ -557,6 +569,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // rows of this warp in pass 0: all valid, none (padding), or some (a per-lane select)
         const int wmode = q * 32 + 32 <= a.R ? 0 : q * 32 >= a.R ? 1 : 2;
         const int gbar = kBarGrp + grp;
+        const float s2 = a.inv_sqrt_d * 1.44269504088896341f;  // log2(e) / sqrt(D)
         const uint32_t tacc = tbase + (uint32_t)(grp * kAccCols) + ((uint32_t)(q * 32) << 16);
         bool ok = true;
         // ---- pass 0: per-(row, tile) max and sum of exp(l - max) (rocket.cpp:91-107)
@@ -587,14 +600,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                             if (decltype(full)::value || c * 32 + j < nkeys) mx = fmaxf(mx, x[j]);
                     }
                     M = fmaxf(mx * a.inv_sqrt_d, -FLT_MAX);
+                    const float nm = neg_m2(M);
 #pragma unroll 1
                     for (int c = 0; c < 4; ++c) {
                         float x[32];
                         tmem_ld32(tacc + (uint32_t)(c * 32), x);
 #pragma unroll
                         for (int j = 0; j < 32; j += 2) {
-                            const float2 l = __fmul2_rn(make_float2(x[j], x[j + 1]), make_float2(a.inv_sqrt_d, a.inv_sqrt_d));
-                            const float2 e = mufu_expf2(__fadd2_rn(l, make_float2(-M, -M)));
+                            const float2 e = exp2_pair(x[j], x[j + 1], s2, make_float2(nm, nm));
                             if (decltype(full)::value || c * 32 + j < nkeys) S += e.x;
                             if (decltype(full)::value || c * 32 + j + 1 < nkeys) S += e.y;
                         }
@@ -660,12 +673,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // ---- pass 1: head scores sum_r exp(l - M_r) * inv_r (rocket.cpp:114-116), the logits computed
         // again with the keys on the tensor-memory lanes (D[128 keys][NP rows] = K_tile . Q^T): a thread
         // holds one key's logits of every window row and adds the terms in row order, as the reference
-        // does, with no exchange between threads.  The rows' (-M_r, inv_r) sit in shared memory, one copy
-        // per epilogue group, rewritten when the group's tiles move to another KV head, as one float4 per
-        // row pair (-M_2i, -M_2i+1, inv_2i, inv_2i+1): each half is the paired operand of one instruction.
+        // does, with no exchange between threads.  The rows' (-M_r log2 e, inv_r) sit in shared memory, one
+        // copy per epilogue group, rewritten when the group's tiles move to another KV head, as one float4
+        // per row pair (-M_2i log2 e, -M_2i+1 log2 e, inv_2i, inv_2i+1): each half is the paired operand
+        // of one instruction.
         float* rst = reinterpret_cast<float*>(sm + P.off_epi) + grp * 256;
         auto put_row = [&](int row, float M, float inv) {
-            rst[4 * (row >> 1) + (row & 1)] = -M;
+            rst[4 * (row >> 1) + (row & 1)] = neg_m2(M);
             rst[4 * (row >> 1) + 2 + (row & 1)] = inv;
         };
         const int nch = (a.R + 31) >> 5;  // 32-row chunks of the accumulator
@@ -713,9 +727,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                     for (int j = 0; j < 32; j += 2) {
                         if (!decltype(full)::value && c * 32 + j >= a.R) break;
-                        const float4 st = rs4[j >> 1];  // (-M_r, -M_r+1, inv_r, inv_r+1)
-                        const float2 l = __fmul2_rn(make_float2(x[j], x[j + 1]), make_float2(a.inv_sqrt_d, a.inv_sqrt_d));
-                        const float2 e = mufu_expf2(__fadd2_rn(l, make_float2(st.x, st.y)));
+                        const float4 st = rs4[j >> 1];  // (-M_r log2 e, -M_r+1 log2 e, inv_r, inv_r+1)
+                        const float2 e = exp2_pair(x[j], x[j + 1], s2, make_float2(st.x, st.y));
                         const float2 t = __fmul2_rn(e, make_float2(st.z, st.w));
                         hsum = __fadd_rn(hsum, t.x);
                         if (!decltype(full)::value && c * 32 + j + 1 >= a.R) break;

@@ -110,24 +110,11 @@ __device__ __forceinline__ uint4 tf32_lo(const uint4& x) {
                       __float_as_uint(__fsub_rn(__uint_as_float(x.w), __uint_as_float(x.w & 0xFFFFE000u))));
 }
 
-// exp(x) of two values x <= 0 on the MUFU: 2^t with t = x log2 e rounded,
-// times 1 + e ln 2, where e is the part of x log2 e the rounding dropped
-// (the exact residual of the product by a fused multiply-add, plus x times
-// the part of log2 e below fp32).  About 2 ulp; x below -104 (and -inf)
-// give 0, results below the normal range flush to 0, NaN gives 0.
+// 2^t on the MUFU (ex2.approx, results below the normal range flush to 0, -inf gives 0).
 __device__ __forceinline__ float ex2_approx(float t) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(t));
     return y;
-}
-__device__ __forceinline__ float2 mufu_expf2(float2 x) {
-    const float l2e = __int_as_float(0x3fb8aa3b), l2e_lo = __int_as_float(0x32a57060), ln2 = __int_as_float(0x3f317218);
-    const float2 xc = make_float2(fmaxf(x.x, -104.0f), fmaxf(x.y, -104.0f));
-    const float2 t = __fmul2_rn(xc, make_float2(l2e, l2e));
-    float2 e = __ffma2_rn(xc, make_float2(l2e, l2e), make_float2(-t.x, -t.y));
-    e = __ffma2_rn(xc, make_float2(l2e_lo, l2e_lo), e);
-    const float2 p = make_float2(ex2_approx(t.x), ex2_approx(t.y));
-    return __ffma2_rn(p, __fmul2_rn(e, make_float2(ln2, ln2)), p);
 }
 
 // Two int8 (the low and high byte of w) -> exact fp32, by placing each
