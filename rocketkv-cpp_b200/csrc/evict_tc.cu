@@ -112,7 +112,7 @@ inline TcPlan tc_plan(int kind, int R, int D) {
     if (kind == KIND_Q8) off += align1k(128 * kQ8Row);
     // the MMA reads 128 query rows; rows NP .. 127 fall on what follows the query block (these bytes, the
     // low-part stages or the ring; their accumulator lanes are not used)
-    P.off_epi = off;  // pass 1: per epilogue group, the (-M_r, inv_r) of the window rows
+    P.off_epi = off;  // pass 1: per epilogue group, the window rows' (-M_r log2 e, inv_r) by row pairs
     off += kAccs * 128 * 8;
     P.off_lo = off;
     if (tf32) off += kLoStages * kStageB;
