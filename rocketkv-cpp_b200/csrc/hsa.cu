@@ -966,7 +966,7 @@ __global__ void __launch_bounds__(kNT, 3) hsa_attn_kernel(const HsaArgs a) {
 }
 
 // ===========================================================================
-// Page summaries (persistent cache state; SURVEY-style "page min/max" option)
+// Page summaries (persistent cache state: per-page max and min of K)
 // ===========================================================================
 // For every (item, KV head), dimension d and page p (rows p C .. min(p C + C,
 // Lc) - 1 of the compressed cache), the summary holds the NaN-ignoring max of
